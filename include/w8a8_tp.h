@@ -1,0 +1,141 @@
+/*
+ * w8a8_tp.h — C ABI of the B200 (sm_100a) W8A8 tensor-parallel linear path.
+ *
+ * One shared library (mini-sglang-fork_b200/_w8a8_tp.so) exports these
+ * entry points.  Plain pointers and sizes only: device pointers are raw CUDA
+ * device addresses, `stream` is a cudaStream_t passed as void*.  The caller
+ * owns every tensor; the library owns only a communicator's IPC-shared
+ * buffers.  No call allocates device memory, synchronises the device or
+ * throws; all of them return an int status (0 = W8A8_OK) and leave a message
+ * for w8a8_last_error() on failure.  Shapes and alignment are validated on the
+ * host before any launch.
+ *
+ * Reference interfaces replaced (paths inside mini-sglang, M/ = python/minisgl/):
+ *   - _LinearTPImpl.forward = F.linear(x, W, b)          M/layers/linear.py:31-32
+ *   - LinearOProj / LinearRowParallel forward + all_reduce M/layers/linear.py:102-106,123-127
+ *   - silu_and_mul(x, out)                                 M/layers/activation.py:9-12
+ *   - NCCLWrapper(rank, world, max_bytes, uid)             M/kernel/csrc/src/pynccl.cu:74-91
+ *   - NCCLWrapper::all_reduce(t, "sum")                    M/kernel/csrc/src/pynccl.cu:93-134
+ *   - init_pynccl (UID broadcast over the CPU group)       M/kernel/pynccl.py:45-78
+ *   - host::RuntimeCheck / PanicError message channel      M/kernel/csrc/include/minisgl/utils.h:40-88
+ */
+#ifndef W8A8_TP_H_
+#define W8A8_TP_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum w8a8_status {
+  W8A8_OK = 0,
+  W8A8_ERR_INVALID_ARG = 1, /* bad shape, null pointer, bad rank/world     */
+  W8A8_ERR_ALIGNMENT = 2,   /* pointer / stride not 16-byte aligned        */
+  W8A8_ERR_CUDA = 3,        /* a CUDA runtime/driver call failed           */
+  W8A8_ERR_UNSUPPORTED = 4, /* device is not sm_100 or size beyond limits  */
+  W8A8_ERR_TIMEOUT = 5,     /* a bounded device-side wait gave up          */
+  W8A8_ERR_WORKSPACE = 6,   /* workspace missing or too small              */
+  W8A8_ERR_STATE = 7        /* communicator used before its peers were opened */
+};
+
+/* Last error message of the calling thread ("" if none).  Replaces the
+ * PanicError text channel of M/kernel/csrc/include/minisgl/utils.h:40-88. */
+const char* w8a8_last_error(void);
+
+/* ABI version (bumped on any signature change). */
+int w8a8_abi_version(void);
+
+/* Reads (and optionally clears) the device-side error word the kernels set
+ * when a bounded wait gives up (W8A8_ERR_TIMEOUT) — synchronises the current
+ * device.  *code receives the bitwise OR of the kernel error bits. */
+int w8a8_device_error(int* code, int clear);
+
+/* ---------------------------------------------------------------- kernel 1
+ * Per-token symmetric absmax quantiser: x[M, K] bf16 (row stride ldx
+ * elements) -> q[M, K] int8 (contiguous) + scale[M] fp32,
+ * scale = amax/127, q = clamp(rint(x/scale), -127, 127), q = 0 if scale = 0.
+ * No reference counterpart (the reference feeds bf16 to F.linear,
+ * M/layers/linear.py:31-32); it is the input side of every W8A8 linear.
+ * Needs K % 8 == 0, ldx % 8 == 0, 16-byte aligned x and q. */
+int w8a8_quant_per_token(const void* x, int64_t ldx, int8_t* q, float* scale,
+                         int64_t M, int64_t K, void* stream);
+
+/* Fused SiLU*mul + per-token quantiser.  gate_up[M, 2I] bf16 (row stride ld
+ * elements); y = bf16(silu(gate) * up) as silu_and_mul computes it
+ * (M/layers/activation.py:9-12), then q/scale of y as above.  y_out[M, I]
+ * (nullable) receives the bf16 y.  Needs I % 8 == 0, ld % 8 == 0. */
+int w8a8_silu_mul_quant(const void* gate_up, int64_t ld, int8_t* q, float* scale,
+                        void* y_out, int64_t M, int64_t I, void* stream);
+
+/* ---------------------------------------------------------------- kernel 2
+ * W8A8 GEMM on tcgen05 tensor cores: C[M, N] bf16 =
+ *   bf16((f32(A[M,K] . B[N,K]^T) * sa[m]) * sb[n] + bias[n])
+ * A = int8 activations [M, K] row-major, B = int8 weight [N, K] row-major
+ * (nn.Linear layout), sa[M] / sb[N] fp32 scales, bias[N] bf16 (nullable).
+ * c_i32 (nullable) receives the exact int32 accumulator [M, N].
+ * Replaces F.linear in _LinearTPImpl.forward (M/layers/linear.py:31-32).
+ * Needs K % 16 == 0, N % 16 == 0, 16-byte aligned A, B, C.
+ * `workspace` (zero-initialised once by the caller, left zeroed by every
+ * successful call) serves split-K; w8a8_gemm_workspace_size() gives the bytes
+ * a shape needs with the default heuristics (0 = none needed). */
+size_t w8a8_gemm_workspace_size(int64_t M, int64_t N, int64_t K);
+int w8a8_gemm(const int8_t* A, const int8_t* B, const float* sa, const float* sb,
+              const void* bias, void* C, int32_t* c_i32, int64_t M, int64_t N, int64_t K,
+              void* workspace, size_t workspace_bytes, void* stream);
+
+/* Same as w8a8_gemm with an explicit tile configuration (for tests and
+ * tuning): variant 0 = auto, 1 = 128x256 tiles, 2 = 128x128 tiles,
+ * 3..6 = weight-stationary (swap-AB) 128 x {16,32,64,128}; splits = 0 auto,
+ * else the split-K factor. */
+int w8a8_gemm_config(const int8_t* A, const int8_t* B, const float* sa, const float* sb,
+                     const void* bias, void* C, int32_t* c_i32, int64_t M, int64_t N,
+                     int64_t K, int variant, int splits, void* workspace,
+                     size_t workspace_bytes, void* stream);
+
+/* Host-only planner query (no GPU needed): the tile configuration w8a8_gemm
+ * would use for a shape on a device with num_sms SMs.  out[8] receives
+ * {variant, BN, swap, tiles, splits, k-blocks per split, CTAs, workspace bytes}. */
+int w8a8_gemm_plan(int64_t M, int64_t N, int64_t K, int variant, int splits, size_t workspace_bytes,
+                   int num_sms, int64_t* out);
+
+/* ---------------------------------------------------------------- kernel 3
+ * Tensor-parallel communicator over NVLink / NVSwitch peer memory.
+ * Replaces NCCLWrapper (M/kernel/csrc/src/pynccl.cu:74-91) + init_pynccl
+ * (M/kernel/pynccl.py:45-78): each rank creates its buffers, exports an
+ * opaque handle blob of w8a8_comm_handle_bytes() bytes, the blobs are
+ * all-gathered over the CPU group (rank order), then every rank opens its
+ * peers. */
+typedef struct w8a8_comm w8a8_comm;
+size_t w8a8_comm_handle_bytes(void);
+int w8a8_comm_create(int rank, int world, int device, size_t max_bytes, w8a8_comm** comm,
+                     void* handle_out);
+int w8a8_comm_open_peers(w8a8_comm* comm, const void* all_handles);
+/* Bounded-wait budget of every device-side flag wait (default 10 s). */
+int w8a8_comm_set_timeout_ms(w8a8_comm* comm, int64_t timeout_ms);
+
+/* In-place sum all-reduce of a bf16 tensor across the ranks; every rank gets
+ * the fp32 sum of the ranks' values in rank order, rounded once to bf16.
+ * Replaces NCCLWrapper::all_reduce(t, "sum") (M/kernel/csrc/src/pynccl.cu:93-134)
+ * and PyNCCLDistributedImpl.all_reduce (M/distributed/impl.py:44-50). */
+int w8a8_all_reduce(w8a8_comm* comm, void* x, int64_t numel, void* stream);
+
+/* Row-parallel W8A8 linear with the all-reduce fused into the GEMM: every
+ * rank passes its K-shard (A[M, K_local], B[N, K_local]) and receives the
+ * all-reduced C[M, N] on every rank.  Replaces LinearOProj.forward /
+ * LinearRowParallel.forward (M/layers/linear.py:102-106,123-127). */
+int w8a8_gemm_allreduce(w8a8_comm* comm, const int8_t* A, const int8_t* B, const float* sa,
+                        const float* sb, const void* bias, void* C, int64_t M, int64_t N,
+                        int64_t K, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Device-side status of the communicator: *device_error != 0 once a bounded
+ * flag wait gave up (a peer that never arrived); synchronises the device. */
+int w8a8_comm_status(w8a8_comm* comm, int* device_error);
+void w8a8_comm_destroy(w8a8_comm* comm);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* W8A8_TP_H_ */

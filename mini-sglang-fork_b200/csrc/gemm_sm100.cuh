@@ -1,0 +1,397 @@
+// Kernel 2: W8A8 GEMM on 5th-generation tensor cores (tcgen05, kind::i8).
+//
+//   C[M, N] = bf16( (f32(sum_k A[m,k] * B[n,k]) * sa[m]) * sb[n] + bias[n] )
+//
+// A: int8 activations [M, K] (K contiguous); B: int8 weight [N, K]
+// (nn.Linear layout, K contiguous).  Both operands are K-major, which is the
+// layout tcgen05 reads natively.
+//
+// Structure (one persistent CTA per SM, 6 warps, warp-specialised):
+//   warp 0      TMA producer: 2-D tiled bulk-tensor loads of a 128-row tile of
+//               the "wide" operand and a BN-row tile of the "narrow" operand,
+//               128 K-bytes per stage, 128-byte swizzle, STAGES-deep mbarrier
+//               ring.
+//   warp 1      owns the TMEM allocation; lane 0 issues tcgen05.mma
+//               (M=128, N=BN, K=32 per instruction, 4 per stage) into one of
+//               two TMEM accumulators and commits stage releases and
+//               accumulator-ready signals through tcgen05.commit.
+//   warps 2-5   epilogue: tcgen05.ld of the int32 accumulator (warp w reads
+//               TMEM lanes 32*(w%4)..+31), dequant in fp32 with separately
+//               rounded multiplies, bf16 store; releases the accumulator so the
+//               MMA of the next tile overlaps this epilogue.
+//
+// Orientation.  Normal: the 128-row side is A (tokens), the BN side is B
+// (output channels).  Weight-stationary ("swap", small M): the 128-row side is
+// B (output channels, filling the 128-lane MMA M slot), the BN side is the
+// handful of tokens; the math is unchanged (C^T = B . A^T) and the epilogue
+// writes C[m, n] with n along the 32 lanes of a warp.
+//
+// Split-K (few output tiles, e.g. decode): the K blocks of a tile are cut into
+// `splits` ranges handled by different CTAs.  Each adds its int32 partial tile
+// into a workspace with red.global.add (exact and order-independent), then the
+// last CTA to arrive on the tile's counter dequantises the sum, writes C and
+// zeroes the workspace tile and counter again, so the workspace stays zeroed
+// between calls.
+//
+// Every mbarrier wait is bounded (%globaltimer); on expiry the CTA raises a
+// shared abort flag and the device error word, drains its in-flight TMA loads
+// and MMAs (bounded too), frees TMEM and exits.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+
+#include <cstdint>
+
+#include "sm100.cuh"
+
+namespace w8a8 {
+
+struct GemmArgs {
+  const float* sa;            // [M] activation scales
+  const float* sb;            // [N] weight scales
+  const __nv_bfloat16* bias;  // [N] or null
+  __nv_bfloat16* C;           // [M, N] bf16 output (row stride ldc)
+  int32_t* c_i32;             // [M, N] int32 accumulator output or null
+  int32_t* ws;                // split-K workspace (zeroed)
+  uint32_t* counters;         // split-K tile arrival counters (zeroed)
+  unsigned int* err;          // device error word
+  long long timeout_ns;
+  int M, N, K;
+  int ldc;
+  int tiles_w, tiles_n;       // tiles along the 128-row side / the BN side
+  int num_tiles, splits, kb_per_split, kblocks;
+  int units;                  // num_tiles * splits
+  int wide_fast;              // raster: 1 = consecutive tiles walk the 128-row side
+};
+
+template <int BN, int STAGES, bool SWAP>
+struct GemmTraits {
+  static constexpr int kBM = 128;
+  static constexpr int kBK = 128;  // bytes of K per stage (= int8 elements)
+  static constexpr int kMmaK = 32;
+  static constexpr int kTileWBytes = kBM * kBK;
+  static constexpr int kTileNBytes = BN * kBK;
+  static constexpr int kStageBytes = kTileWBytes + kTileNBytes;
+  static constexpr int kAccCols = BN;
+  static constexpr int kChunk = BN < 32 ? BN : 32;  // TMEM columns per epilogue load
+  static constexpr int kChunks = BN / kChunk;
+  static constexpr int kTmemCols = (2 * BN) <= 32 ? 32 : (2 * BN) <= 64 ? 64 : (2 * BN) <= 128 ? 128
+                                   : (2 * BN) <= 256 ? 256 : 512;
+  static constexpr int kBarrierBytes = 256;
+  static constexpr int kSmemBytes = 1024 + STAGES * kStageBytes + kBarrierBytes;
+  static constexpr int kThreads = 192;
+  static constexpr uint32_t kIdesc = dev::idesc_i8(kBM, BN);
+  static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "MMA N");
+  static_assert(kSmemBytes <= 227 * 1024, "shared memory");
+};
+
+__device__ __forceinline__ void unit_coords(const GemmArgs& a, int unit, int& tw, int& tn, int& kb0,
+                                            int& kb1, int& tile) {
+  tile = unit / a.splits;
+  const int split = unit - tile * a.splits;
+  if (a.wide_fast) {
+    tw = tile % a.tiles_w;
+    tn = tile / a.tiles_w;
+  } else {
+    tn = tile % a.tiles_n;
+    tw = tile / a.tiles_n;
+  }
+  kb0 = split * a.kb_per_split;
+  kb1 = min(a.kblocks, kb0 + a.kb_per_split);
+}
+
+__device__ __forceinline__ float dequant1(int32_t acc, float sa, float sb) {
+  return __fmul_rn(__fmul_rn(__int2float_rn(acc), sa), sb);
+}
+
+// Dequantise 32 accumulators of one TMEM row and store them.
+//   normal: row = token m, the 32 values are channels n0..n0+31.
+//   swap:   row = channel n, the 32 values are tokens m0..m0+31.
+template <bool SWAP, int CH>
+__device__ __forceinline__ void store_chunk(const GemmArgs& a, int row, int col0, const uint32_t (&v)[32]) {
+  if (!SWAP) {
+    const int m = row;
+    if (m >= a.M) return;
+    const float sam = __ldg(a.sa + m);
+    __nv_bfloat16* crow = a.C + static_cast<int64_t>(m) * a.ldc;
+#pragma unroll
+    for (int g = 0; g < 4; ++g) {
+      const int n = col0 + g * 8;
+      if (n >= a.N) break;  // N % 16 == 0: granules are either fully in or out
+      uint4 pk;
+      __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&pk);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int c0 = g * 8 + 2 * j;
+        float y0 = dequant1(static_cast<int32_t>(v[c0]), sam, __ldg(a.sb + n + 2 * j));
+        float y1 = dequant1(static_cast<int32_t>(v[c0 + 1]), sam, __ldg(a.sb + n + 2 * j + 1));
+        if (a.bias) {
+          y0 = __fadd_rn(y0, __bfloat162float(a.bias[n + 2 * j]));
+          y1 = __fadd_rn(y1, __bfloat162float(a.bias[n + 2 * j + 1]));
+        }
+        h[j] = __floats2bfloat162_rn(y0, y1);
+      }
+      *reinterpret_cast<uint4*>(crow + n) = pk;
+      if (a.c_i32) {
+        int4* dst = reinterpret_cast<int4*>(a.c_i32 + static_cast<int64_t>(m) * a.N + n);
+        dst[0] = make_int4(v[g * 8 + 0], v[g * 8 + 1], v[g * 8 + 2], v[g * 8 + 3]);
+        dst[1] = make_int4(v[g * 8 + 4], v[g * 8 + 5], v[g * 8 + 6], v[g * 8 + 7]);
+      }
+    }
+  } else {
+    const int n = row;
+    if (n >= a.N) return;
+    const float sbn = __ldg(a.sb + n);
+    const float bn = a.bias ? __bfloat162float(a.bias[n]) : 0.0f;
+#pragma unroll
+    for (int j = 0; j < CH; ++j) {
+      const int m = col0 + j;
+      if (m >= a.M) break;
+      float y = dequant1(static_cast<int32_t>(v[j]), __ldg(a.sa + m), sbn);
+      if (a.bias) y = __fadd_rn(y, bn);
+      a.C[static_cast<int64_t>(m) * a.ldc + n] = __float2bfloat16_rn(y);
+      if (a.c_i32) a.c_i32[static_cast<int64_t>(m) * a.N + n] = static_cast<int32_t>(v[j]);
+    }
+  }
+}
+
+template <int BN, int STAGES, bool SWAP>
+__global__ void __launch_bounds__(192, 1)
+    w8a8_gemm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_n,
+                     const GemmArgs args) {
+  using T = GemmTraits<BN, STAGES, SWAP>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* s_w = smem;
+  uint8_t* s_n = smem + STAGES * T::kTileWBytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(s_n + STAGES * T::kTileNBytes);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + STAGES;
+  uint64_t* acc_full = bars + 2 * STAGES;
+  uint64_t* acc_empty = acc_full + 2;
+  uint64_t* drain = acc_empty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  volatile int* last_flag = abort_flag + 1;
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      dev::mbar_init(dev::smem_u32(full + s), 1);
+      dev::mbar_init(dev::smem_u32(empty + s), 1);
+    }
+    for (int s = 0; s < 2; ++s) {
+      dev::mbar_init(dev::smem_u32(acc_full + s), 1);
+      dev::mbar_init(dev::smem_u32(acc_empty + s), 128);
+    }
+    dev::mbar_init(dev::smem_u32(drain), 1);
+    *abort_flag = 0;
+    *last_flag = 0;
+    dev::fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    dev::prefetch_tmap(&tm_w);
+    dev::prefetch_tmap(&tm_n);
+  }
+  if (warp == 1) {
+    dev::tmem_alloc(dev::smem_u32(tmem_slot), T::kTmemCols);
+    dev::tmem_relinquish();
+  }
+  dev::tc_fence_before();
+  __syncthreads();
+  dev::tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const long long tmo = args.timeout_ns;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------------------------------------------------- producer
+      // Weight-stationary tiles stream each weight byte once (evict first) and
+      // re-read the few token rows (evict last); the normal orientation reuses
+      // both operands across tiles and keeps the default policy.
+      const uint64_t pol_w = dev::policy_evict_first();
+      const uint64_t pol_n = dev::policy_evict_last();
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t issued_mask = 0, issued_phase = 0;
+      bool ok = true;
+      for (int unit = blockIdx.x; unit < args.units && ok; unit += gridDim.x) {
+        int tw, tn, kb0, kb1, tile;
+        unit_coords(args, unit, tw, tn, kb0, kb1, tile);
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!dev::mbar_wait(dev::smem_u32(empty + stage), phase ^ 1u, abort_flag, args.err,
+                              kErrGemmWait, tmo)) {
+            ok = false;
+            break;
+          }
+          const uint32_t fb = dev::smem_u32(full + stage);
+          dev::mbar_expect_tx(fb, T::kStageBytes);
+          if constexpr (SWAP) {
+            dev::tma_load_2d_hint(dev::smem_u32(s_w + stage * T::kTileWBytes), &tm_w, fb, kb * T::kBK,
+                                  tw * T::kBM, pol_w);
+            dev::tma_load_2d_hint(dev::smem_u32(s_n + stage * T::kTileNBytes), &tm_n, fb, kb * T::kBK,
+                                  tn * BN, pol_n);
+          } else {
+            dev::tma_load_2d(dev::smem_u32(s_w + stage * T::kTileWBytes), &tm_w, fb, kb * T::kBK, tw * T::kBM);
+            dev::tma_load_2d(dev::smem_u32(s_n + stage * T::kTileNBytes), &tm_n, fb, kb * T::kBK, tn * BN);
+          }
+          issued_mask |= 1u << stage;
+          issued_phase = (issued_phase & ~(1u << stage)) | (phase << stage);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      // Every issued load must land before the CTA may exit.
+      for (int s = 0; s < STAGES; ++s) {
+        if (issued_mask & (1u << s)) {
+          if (!dev::mbar_wait_drain(dev::smem_u32(full + s), (issued_phase >> s) & 1u, tmo)) {
+            if (args.err) atomicOr(args.err, kErrGemmDrain);
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ------------------------------------------------------- MMA issuer
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      for (int unit = blockIdx.x; unit < args.units && ok; unit += gridDim.x) {
+        int tw, tn, kb0, kb1, tile;
+        unit_coords(args, unit, tw, tn, kb0, kb1, tile);
+        if (!dev::mbar_wait(dev::smem_u32(acc_empty + acc), acc_phase ^ 1u, abort_flag, args.err,
+                            kErrGemmWait, tmo)) {
+          break;
+        }
+        dev::tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * T::kAccCols);
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!dev::mbar_wait(dev::smem_u32(full + stage), phase, abort_flag, args.err, kErrGemmWait,
+                              tmo)) {
+            ok = false;
+            break;
+          }
+          dev::tc_fence_after();
+          const uint64_t dw = dev::sdesc_k_sw128(dev::smem_u32(s_w + stage * T::kTileWBytes));
+          const uint64_t dn = dev::sdesc_k_sw128(dev::smem_u32(s_n + stage * T::kTileNBytes));
+#pragma unroll
+          for (int k = 0; k < T::kBK / T::kMmaK; ++k) {
+            const uint64_t off = static_cast<uint64_t>((k * T::kMmaK) >> 4);
+            dev::mma_i8(d_tmem, dw + off, dn + off, T::kIdesc, (kb > kb0 || k > 0) ? 1u : 0u);
+          }
+          dev::tc_commit(dev::smem_u32(empty + stage));
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        dev::tc_commit(dev::smem_u32(acc_full + acc));
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1u;
+        }
+      }
+      // All MMAs this thread issued must finish before TMEM is freed.
+      dev::tc_commit(dev::smem_u32(drain));
+      if (!dev::mbar_wait_drain(dev::smem_u32(drain), 0, tmo)) {
+        if (args.err) atomicOr(args.err, kErrGemmDrain);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int quarter = warp & 3;
+    const int row_in_tile = quarter * 32 + lane;
+    const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
+    const int et = threadIdx.x - 64;  // 0..127 among the epilogue threads
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int unit = blockIdx.x; unit < args.units; unit += gridDim.x) {
+      int tw, tn, kb0, kb1, tile;
+      unit_coords(args, unit, tw, tn, kb0, kb1, tile);
+      const bool ok = dev::mbar_wait(dev::smem_u32(acc_full + acc), acc_phase, abort_flag, args.err,
+                                     kErrGemmWait, tmo);
+      if (dev::named_bar_or(1, 128, !ok)) break;  // uniform exit of all epilogue threads
+      dev::tc_fence_after();
+      const uint32_t t_acc = tmem_base + lane_base + static_cast<uint32_t>(acc * T::kAccCols);
+      const int row = tw * T::kBM + row_in_tile;
+      if (args.splits == 1) {
+#pragma unroll 1
+        for (int c = 0; c < T::kChunks; ++c) {
+          uint32_t v[32];
+          dev::tmem_ld<T::kChunk>(t_acc + c * T::kChunk, v);
+          dev::tmem_wait_ld(v);
+          if (c == T::kChunks - 1) {
+            dev::tc_fence_before();
+            dev::mbar_arrive(dev::smem_u32(acc_empty + acc));
+          }
+          store_chunk<SWAP, T::kChunk>(args, row, tn * BN + c * T::kChunk, v);
+        }
+      } else {
+        int32_t* wtile = args.ws + static_cast<int64_t>(tile) * (T::kBM * BN);
+#pragma unroll 1
+        for (int c = 0; c < T::kChunks; ++c) {
+          uint32_t v[32];
+          dev::tmem_ld<T::kChunk>(t_acc + c * T::kChunk, v);
+          dev::tmem_wait_ld(v);
+          if (c == T::kChunks - 1) {
+            dev::tc_fence_before();
+            dev::mbar_arrive(dev::smem_u32(acc_empty + acc));
+          }
+#pragma unroll
+          for (int j = 0; j < T::kChunk; ++j)
+            atomicAdd(wtile + (c * T::kChunk + j) * T::kBM + row_in_tile, static_cast<int32_t>(v[j]));
+        }
+        __threadfence();
+        dev::named_bar_sync(1, 128);
+        if (et == 0) {
+          const uint32_t prev = atomicAdd(args.counters + tile, 1u);
+          *last_flag = (prev == static_cast<uint32_t>(args.splits - 1)) ? 1 : 0;
+        }
+        dev::named_bar_sync(1, 128);
+        const bool last = *last_flag != 0;
+        if (last) {
+          __threadfence();
+#pragma unroll 1
+          for (int c = 0; c < T::kChunks; ++c) {
+            uint32_t v[32];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              if (j < T::kChunk) {
+                int32_t* p = wtile + (c * T::kChunk + j) * T::kBM + row_in_tile;
+                v[j] = static_cast<uint32_t>(__ldcg(p));
+                __stcg(p, 0);
+              } else {
+                v[j] = 0u;
+              }
+            }
+            store_chunk<SWAP, T::kChunk>(args, row, tn * BN + c * T::kChunk, v);
+          }
+          if (et == 0) args.counters[tile] = 0u;
+        }
+        // last_flag is rewritten by the next tile: keep every reader ahead of it
+        dev::named_bar_sync(1, 128);
+      }
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1u;
+      }
+    }
+    dev::tc_fence_before();
+  }
+
+  __syncthreads();
+  if (warp == 1) {
+    dev::tc_fence_after();
+    dev::tmem_dealloc(tmem_base, T::kTmemCols);
+  }
+}
+
+}  // namespace w8a8

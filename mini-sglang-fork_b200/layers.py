@@ -1,0 +1,193 @@
+"""W8A8 tensor-parallel linear layers with mini-sglang's operator surface.
+
+Same class names, constructor signatures, size bookkeeping and state-dict
+rules as mini-sglang's bf16 layers (M/layers/linear.py:13-127,
+M/layers/base.py:15-99); the weight is held as int8 ``weight [N_local,
+K_local]`` plus ``weight_scale [N_local]`` fp32, and ``forward`` runs the
+per-token quantiser and the tcgen05 int8 GEMM.  Row-parallel layers return
+the all-reduced output like the reference; when a peer-memory communicator is
+enabled the reduction is fused into the GEMM, otherwise the plugin stack's
+``all_reduce`` runs after it.
+
+Weight sharding (for loaders): quantise the UNSHARDED bf16 weight per output
+channel, then shard ``weight`` exactly like the bf16 tensor
+(M/models/weight.py:34-52); ``weight_scale`` follows dim-0 shards
+(column-parallel) and is replicated for dim-1 shards (row-parallel).
+"""
+from __future__ import annotations
+
+from typing import Any, Dict, List, Optional, Union
+
+import torch
+
+from . import ops
+from .distributed import DistributedCommunicator, div_even, get_peer_mem_comm, get_tp_info
+from .ops import QuantizedActivation
+
+_STATE_DICT = Dict[str, torch.Tensor]
+
+__all__ = [
+    "BaseOP",
+    "LinearReplicated",
+    "LinearColParallelMerged",
+    "LinearQKVMerged",
+    "LinearOProj",
+    "LinearRowParallel",
+    "GatedMLP",
+    "silu_and_mul",
+    "silu_and_mul_quant",
+]
+
+silu_and_mul = ops.silu_and_mul
+silu_and_mul_quant = ops.silu_and_mul_quant
+
+
+def _concat_prefix(prefix: str, name: str) -> str:
+    return f"{prefix}.{name}" if prefix else name
+
+
+class BaseOP:
+    """State-dict discovery of every public tensor / sub-op attribute, as
+    ``BaseOP`` does (M/layers/base.py:15-53): names starting with ``_`` are
+    private; ``load_state_dict`` replaces each tensor after checking that shape
+    and dtype match."""
+
+    def forward(self, *args: Any, **kwargs: Any) -> Any:  # pragma: no cover - abstract
+        raise NotImplementedError
+
+    def state_dict(self, *, prefix: str = "", result: Optional[_STATE_DICT] = None) -> _STATE_DICT:
+        result = result if result is not None else {}
+        for name, value in self.__dict__.items():
+            if name.startswith("_"):
+                continue
+            if isinstance(value, torch.Tensor):
+                result[_concat_prefix(prefix, name)] = value
+            elif isinstance(value, BaseOP):
+                value.state_dict(prefix=_concat_prefix(prefix, name), result=result)
+        return result
+
+    def load_state_dict(self, state_dict: _STATE_DICT, *, prefix: str = "", _internal: bool = False) -> None:
+        for name, value in list(self.__dict__.items()):
+            if name.startswith("_"):
+                continue
+            if isinstance(value, torch.Tensor):
+                item = state_dict.pop(_concat_prefix(prefix, name))
+                if not isinstance(item, torch.Tensor):
+                    raise TypeError(f"{_concat_prefix(prefix, name)} is not a tensor")
+                if value.shape != item.shape or value.dtype != item.dtype:
+                    raise ValueError(f"{_concat_prefix(prefix, name)}: expected {tuple(value.shape)} {value.dtype}, "
+                                     f"got {tuple(item.shape)} {item.dtype}")
+                setattr(self, name, item)
+            elif isinstance(value, BaseOP):
+                value.load_state_dict(state_dict, prefix=_concat_prefix(prefix, name), _internal=True)
+        if not _internal and state_dict:
+            raise RuntimeError(f"Unexpected keys in state_dict: {list(state_dict.keys())}")
+
+
+class _LinearTPImpl(BaseOP):
+    """W8A8 counterpart of ``_LinearTPImpl`` (M/layers/linear.py:13-32)."""
+
+    def __init__(self, full_isize: int, full_osize: int, local_isize: int, local_osize: int, has_bias: bool):
+        self.full_input_size = full_isize
+        self.full_output_size = full_osize
+        self.local_input_size = local_isize
+        self.local_output_size = local_osize
+        self.weight = torch.empty(local_osize, local_isize, dtype=torch.int8)
+        self.weight_scale = torch.empty(local_osize, dtype=torch.float32)
+        self.bias = torch.empty(local_osize, dtype=torch.bfloat16) if has_bias else None
+
+    def _quantize_input(self, x: Union[torch.Tensor, QuantizedActivation]) -> QuantizedActivation:
+        if isinstance(x, QuantizedActivation):
+            return x
+        q, s = ops.quant_per_token(x)
+        return QuantizedActivation(q, s)
+
+    def forward(self, x: Union[torch.Tensor, QuantizedActivation]) -> torch.Tensor:
+        qa = self._quantize_input(x)
+        return ops.w8a8_gemm(qa.q, self.weight, qa.s, self.weight_scale, self.bias)
+
+
+class LinearReplicated(_LinearTPImpl):
+    """Unsharded W8A8 linear (M/layers/linear.py:35-53)."""
+
+    def __init__(self, input_size: int, output_size: int, has_bias: bool):
+        super().__init__(input_size, output_size, input_size, output_size, has_bias)
+
+
+class LinearColParallelMerged(_LinearTPImpl):
+    """Column-parallel merged linear, e.g. gate_up (M/layers/linear.py:56-68)."""
+
+    def __init__(self, input_size: int, output_sizes: List[int], has_bias: bool):
+        tp_info = get_tp_info()
+        tp_output_sizes = [div_even(size, tp_info.size) for size in output_sizes]
+        super().__init__(input_size, sum(output_sizes), input_size, sum(tp_output_sizes), has_bias)
+
+
+class LinearQKVMerged(_LinearTPImpl):
+    """Column-parallel q|k|v over heads, kv replicated when kv_heads < tp
+    (M/layers/linear.py:71-88)."""
+
+    def __init__(self, hidden_size: int, head_dim: int, num_qo_heads: int, num_kv_heads: int, has_bias: bool):
+        tp_info = get_tp_info()
+        local_num_qo = div_even(num_qo_heads, tp_info.size)
+        local_num_kv = div_even(num_kv_heads, tp_info.size, allow_replicate=True)
+        full_osize = (num_qo_heads + 2 * num_kv_heads) * head_dim
+        local_osize = (local_num_qo + 2 * local_num_kv) * head_dim
+        super().__init__(hidden_size, full_osize, hidden_size, local_osize, has_bias)
+
+
+class _RowParallel(_LinearTPImpl):
+    """Row-parallel forward: local W8A8 GEMM of the K-shard, then the sum over
+    ranks (M/layers/linear.py:102-106,123-127).  With a peer-memory
+    communicator the reduction runs inside the GEMM kernel."""
+
+    _tp_size: int
+    _comm: DistributedCommunicator
+
+    def forward(self, x: Union[torch.Tensor, QuantizedActivation]) -> torch.Tensor:
+        qa = self._quantize_input(x)
+        if self._tp_size > 1:
+            fused = get_peer_mem_comm()
+            if fused is not None:
+                return fused.gemm_allreduce(qa.q, self.weight, qa.s, self.weight_scale, self.bias)
+            y = ops.w8a8_gemm(qa.q, self.weight, qa.s, self.weight_scale, self.bias)
+            return self._comm.all_reduce(y)
+        return ops.w8a8_gemm(qa.q, self.weight, qa.s, self.weight_scale, self.bias)
+
+
+class LinearOProj(_RowParallel):
+    """o_proj (M/layers/linear.py:91-106)."""
+
+    def __init__(self, input_size: int, output_size: int, has_bias: bool):
+        tp_info = get_tp_info()
+        self._comm = DistributedCommunicator()
+        self._tp_size = tp_info.size
+        super().__init__(input_size, output_size, div_even(input_size, tp_info.size), output_size, has_bias)
+
+
+class LinearRowParallel(_RowParallel):
+    """down_proj (M/layers/linear.py:109-127)."""
+
+    def __init__(self, input_size: int, output_size: int, has_bias: bool):
+        tp_info = get_tp_info()
+        self._comm = DistributedCommunicator()
+        self._tp_size = tp_info.size
+        super().__init__(input_size, output_size, div_even(input_size, tp_info.size), output_size, has_bias)
+
+
+class GatedMLP(BaseOP):
+    """W8A8 ``GatedMLP`` (M/models/utils.py:25-50): gate_up (column-parallel)
+    -> fused SiLU*mul + per-token quant -> down (row-parallel + all-reduce).
+    The bf16 product of SiLU*mul never touches HBM."""
+
+    def __init__(self, hidden_size: int, intermediate_size: int):
+        self.gate_up_proj = LinearColParallelMerged(hidden_size, [intermediate_size, intermediate_size],
+                                                    has_bias=False)
+        self.down_proj = LinearRowParallel(intermediate_size, hidden_size, has_bias=False)
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        gate_up = self.gate_up_proj.forward(x)
+        del x
+        y = silu_and_mul_quant(gate_up)
+        del gate_up
+        return self.down_proj.forward(y)

@@ -1,0 +1,180 @@
+"""Torch-facing wrappers of the C ABI (``include/w8a8_tp.h``).
+
+Every op launches hand-written sm_100a CUDA through ``_w8a8_tp.so`` on the
+caller's current CUDA stream.  There is no CPU or library fallback: a
+non-CUDA tensor, a missing library or a non-B200 device raises.
+"""
+from __future__ import annotations
+
+import ctypes
+from typing import Dict, Optional, Tuple
+
+import torch
+
+from . import _lib
+
+__all__ = [
+    "quant_per_token",
+    "silu_and_mul_quant",
+    "silu_and_mul",
+    "w8a8_gemm",
+    "gemm_plan",
+    "gemm_workspace",
+    "device_error",
+    "QuantizedActivation",
+    "WORKSPACE_BYTES",
+]
+
+# Split-K workspace kept per device (zeroed once, left zeroed by every call).
+WORKSPACE_BYTES = 64 << 20
+_workspaces: Dict[int, torch.Tensor] = {}
+
+
+class QuantizedActivation:
+    """An int8 activation with its per-token fp32 scales (``q [M, K]``, ``s [M]``).
+
+    Produced by :func:`silu_and_mul_quant` and accepted by every W8A8 linear's
+    ``forward`` in place of a bf16 tensor, so ``GatedMLP`` can hand the fused
+    SiLU*mul+quant output straight to ``down_proj``.
+    """
+
+    __slots__ = ("q", "s")
+
+    def __init__(self, q: torch.Tensor, s: torch.Tensor):
+        self.q = q
+        self.s = s
+
+    @property
+    def shape(self):
+        return self.q.shape
+
+    @property
+    def device(self):
+        return self.q.device
+
+
+def _stream(t: torch.Tensor) -> int:
+    return torch.cuda.current_stream(t.device).cuda_stream
+
+
+def _require_cuda(name: str, *ts: Optional[torch.Tensor]) -> None:
+    for t in ts:
+        if t is not None and not t.is_cuda:
+            raise _lib.W8A8Error(_lib.ERR_UNSUPPORTED,
+                                 f"{name}: CUDA tensors required (got {t.device}); there is no CPU path")
+
+
+def _ptr(t: Optional[torch.Tensor]) -> Optional[int]:
+    return None if t is None else t.data_ptr()
+
+
+def gemm_workspace(device: torch.device) -> torch.Tensor:
+    """The zero-initialised split-K workspace of ``device`` (allocated once)."""
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    ws = _workspaces.get(idx)
+    if ws is None:
+        ws = torch.zeros(WORKSPACE_BYTES, dtype=torch.uint8, device=torch.device("cuda", idx))
+        _workspaces[idx] = ws
+    return ws
+
+
+def quant_per_token(x: torch.Tensor, out_q: Optional[torch.Tensor] = None,
+                    out_s: Optional[torch.Tensor] = None) -> Tuple[torch.Tensor, torch.Tensor]:
+    """Per-token symmetric absmax int8 quantisation of ``x [M, K]`` bf16."""
+    _require_cuda("quant_per_token", x)
+    if x.dtype != torch.bfloat16 or x.dim() != 2 or x.stride(1) != 1:
+        raise _lib.W8A8Error(_lib.ERR_INVALID_ARG, "quant_per_token: x must be a 2-D bf16 tensor with unit column stride")
+    m, k = x.shape
+    q = out_q if out_q is not None else torch.empty(m, k, dtype=torch.int8, device=x.device)
+    s = out_s if out_s is not None else torch.empty(m, dtype=torch.float32, device=x.device)
+    lib = _lib.load()
+    _lib.check(lib.w8a8_quant_per_token(_ptr(x), x.stride(0), _ptr(q), _ptr(s), m, k, _stream(x)),
+               "quant_per_token")
+    return q, s
+
+
+def silu_and_mul_quant(gate_up: torch.Tensor, with_bf16: bool = False):
+    """Fused ``silu(g) * u`` (rounded to bf16) + per-token int8 quantisation.
+
+    ``gate_up [M, 2I]`` bf16 -> :class:`QuantizedActivation` (``q [M, I]``,
+    ``s [M]``); with ``with_bf16`` also returns the bf16 ``[M, I]`` product.
+    """
+    _require_cuda("silu_and_mul_quant", gate_up)
+    if gate_up.dtype != torch.bfloat16 or gate_up.dim() != 2 or gate_up.stride(1) != 1:
+        raise _lib.W8A8Error(_lib.ERR_INVALID_ARG, "silu_and_mul_quant: gate_up must be 2-D bf16 with unit column stride")
+    m, two_i = gate_up.shape
+    if two_i % 2:
+        raise _lib.W8A8Error(_lib.ERR_INVALID_ARG, "silu_and_mul_quant: last dim must be even")
+    i = two_i // 2
+    q = torch.empty(m, i, dtype=torch.int8, device=gate_up.device)
+    s = torch.empty(m, dtype=torch.float32, device=gate_up.device)
+    y = torch.empty(m, i, dtype=torch.bfloat16, device=gate_up.device) if with_bf16 else None
+    lib = _lib.load()
+    _lib.check(lib.w8a8_silu_mul_quant(_ptr(gate_up), gate_up.stride(0), _ptr(q), _ptr(s), _ptr(y), m, i,
+                                       _stream(gate_up)), "silu_and_mul_quant")
+    qa = QuantizedActivation(q, s)
+    return (qa, y) if with_bf16 else qa
+
+
+def silu_and_mul(x: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """bf16 ``silu(x[:, :I]) * x[:, I:]`` — the signature of ``silu_and_mul``
+    (M/layers/activation.py:9-12), computed by the fused kernel."""
+    qa, y = silu_and_mul_quant(x, with_bf16=True)
+    if out is not None:
+        out.copy_(y)
+        return out
+    return y
+
+
+def gemm_plan(m: int, n: int, k: int, variant: int = 0, splits: int = 0,
+              workspace_bytes: int = WORKSPACE_BYTES, num_sms: int = 148) -> Dict[str, int]:
+    """Host-only query of the tile configuration the GEMM would use."""
+    out = (ctypes.c_int64 * 8)()
+    _lib.check(_lib.load().w8a8_gemm_plan(m, n, k, variant, splits, workspace_bytes, num_sms, out),
+               "gemm_plan")
+    keys = ("variant", "bn", "swap", "tiles", "splits", "kb_per_split", "grid", "workspace_bytes")
+    return dict(zip(keys, (int(v) for v in out)))
+
+
+def w8a8_gemm(aq: torch.Tensor, wq: torch.Tensor, sa: torch.Tensor, sw: torch.Tensor,
+              bias: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None,
+              out_i32: Optional[torch.Tensor] = None, variant: int = 0, splits: int = 0) -> torch.Tensor:
+    """``bf16((f32(aq @ wq.T) * sa[:, None]) * sw[None, :] + bias)`` on tcgen05.
+
+    ``aq [M, K]`` int8, ``wq [N, K]`` int8, ``sa [M]`` / ``sw [N]`` fp32,
+    ``bias [N]`` bf16 or None.  ``out_i32`` (optional ``[M, N]`` int32)
+    receives the exact accumulator.
+    """
+    _require_cuda("w8a8_gemm", aq, wq, sa, sw, bias, out, out_i32)
+    if aq.dtype != torch.int8 or wq.dtype != torch.int8:
+        raise _lib.W8A8Error(_lib.ERR_INVALID_ARG, "w8a8_gemm: int8 operands required")
+    if not (aq.is_contiguous() and wq.is_contiguous() and sa.is_contiguous() and sw.is_contiguous()):
+        raise _lib.W8A8Error(_lib.ERR_INVALID_ARG, "w8a8_gemm: contiguous operands required")
+    if sa.dtype != torch.float32 or sw.dtype != torch.float32:
+        raise _lib.W8A8Error(_lib.ERR_INVALID_ARG, "w8a8_gemm: fp32 scales required")
+    m, k = aq.shape
+    n, k2 = wq.shape
+    if k2 != k or sa.numel() != m or sw.numel() != n:
+        raise _lib.W8A8Error(_lib.ERR_INVALID_ARG, f"w8a8_gemm: shape mismatch A{tuple(aq.shape)} B{tuple(wq.shape)}")
+    if bias is not None and (bias.dtype != torch.bfloat16 or bias.numel() != n or not bias.is_contiguous()):
+        raise _lib.W8A8Error(_lib.ERR_INVALID_ARG, "w8a8_gemm: bias must be contiguous bf16 [N]")
+    if out is None:
+        out = torch.empty(m, n, dtype=torch.bfloat16, device=aq.device)
+    elif out.dtype != torch.bfloat16 or tuple(out.shape) != (m, n) or not out.is_contiguous():
+        raise _lib.W8A8Error(_lib.ERR_INVALID_ARG, "w8a8_gemm: out must be contiguous bf16 [M, N]")
+    if out_i32 is not None and (out_i32.dtype != torch.int32 or tuple(out_i32.shape) != (m, n)
+                                or not out_i32.is_contiguous()):
+        raise _lib.W8A8Error(_lib.ERR_INVALID_ARG, "w8a8_gemm: out_i32 must be contiguous int32 [M, N]")
+    ws = gemm_workspace(aq.device)
+    lib = _lib.load()
+    st = lib.w8a8_gemm_config(_ptr(aq), _ptr(wq), _ptr(sa), _ptr(sw), _ptr(bias), _ptr(out), _ptr(out_i32),
+                              m, n, k, variant, splits, _ptr(ws), ws.numel(), _stream(aq))
+    _lib.check(st, "w8a8_gemm")
+    return out
+
+
+def device_error(clear: bool = True) -> int:
+    """Device-side error bits (bounded waits that gave up); synchronises."""
+    code = ctypes.c_int(0)
+    _lib.check(_lib.load().w8a8_device_error(ctypes.byref(code), 1 if clear else 0), "device_error")
+    return code.value

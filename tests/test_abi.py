@@ -1,0 +1,102 @@
+"""CPU: the C-ABI library loads, exports every symbol include/w8a8_tp.h
+declares, validates arguments on the host, and plans tiles — no GPU calls."""
+from __future__ import annotations
+
+import ctypes
+import os
+import re
+
+import pytest
+
+from conftest import ROOT
+
+
+def _declared_symbols():
+    src = open(os.path.join(ROOT, "include", "w8a8_tp.h")).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    return sorted(set(re.findall(r"\b(w8a8_[a-z0-9_]+)\s*\(", src)))
+
+
+def test_library_exports_every_declared_symbol(pkg):
+    lib = pkg.load_library()
+    names = _declared_symbols()
+    assert len(names) >= 15
+    for n in names:
+        assert hasattr(lib, n), n
+    # the ctypes binding covers exactly the declared surface
+    assert sorted(pkg._lib.SIGNATURES) == names
+
+
+def test_abi_version_and_error_channel(pkg):
+    lib = pkg.load_library()
+    assert lib.w8a8_abi_version() == 1
+    assert isinstance(lib.w8a8_last_error(), bytes)
+
+
+def test_host_validation_rejects_bad_arguments(pkg):
+    """Argument checks run on the host before any CUDA call."""
+    lib = pkg.load_library()
+    L = pkg._lib
+    # null pointers / misaligned K are rejected with a status and a message
+    st = lib.w8a8_quant_per_token(None, 16, None, None, 4, 16, None)
+    assert st == L.ERR_INVALID_ARG and b"null" in lib.w8a8_last_error()
+    st = lib.w8a8_quant_per_token(16, 12, 16, 16, 4, 12, None)
+    assert st == L.ERR_INVALID_ARG and b"multiple of 8" in lib.w8a8_last_error()
+    st = lib.w8a8_quant_per_token(24, 16, 16, 16, 4, 16, None)
+    assert st == L.ERR_ALIGNMENT
+    st = lib.w8a8_gemm(16, 16, 16, 16, None, 16, None, 8, 24, 40, None, 0, None)
+    assert st == L.ERR_INVALID_ARG and b"multiple of 16" in lib.w8a8_last_error()
+    st = lib.w8a8_gemm(16, 16, 16, 16, None, 16, None, 8, 20, 32, None, 0, None)
+    assert st == L.ERR_INVALID_ARG
+    st = lib.w8a8_gemm(16, 18, 16, 16, None, 16, None, 8, 32, 32, None, 0, None)
+    assert st == L.ERR_ALIGNMENT
+    st = lib.w8a8_silu_mul_quant(16, 10, 16, 16, None, 2, 12, None)
+    assert st == L.ERR_INVALID_ARG
+    # empty batches are a no-op success, as F.linear on an empty input
+    assert lib.w8a8_quant_per_token(None, 16, None, None, 0, 16, None) == L.OK
+    assert lib.w8a8_silu_mul_quant(None, 32, None, None, None, 0, 16, None) == L.OK
+    assert lib.w8a8_gemm_config(16, 16, 16, 16, None, 16, None, 0, 32, 32, 0, 0, None, 0, None) == L.OK
+    assert lib.w8a8_gemm_config(16, 16, 16, 16, None, 16, None, 8, 32, 32, 9, 0, None, 0, None) == L.ERR_INVALID_ARG
+
+
+@pytest.mark.parametrize("m,n,k,variant,bn,swap", [
+    (1, 24576, 4096, 3, 16, 1), (16, 24576, 4096, 3, 16, 1), (17, 24576, 4096, 4, 32, 1),
+    (64, 6144, 1024, 5, 64, 1), (65, 6144, 1024, 2, 128, 0), (256, 5120, 8192, 2, 128, 0),
+    (8192, 24576, 4096, 1, 256, 0), (8192, 4096, 12288, 1, 256, 0), (4096, 6400, 5120, 1, 256, 0),
+])
+def test_planner_variant_choice(pkg, m, n, k, variant, bn, swap):
+    p = pkg.ops.gemm_plan(m, n, k)
+    assert (p["variant"], p["bn"], p["swap"]) == (variant, bn, swap)
+    assert 1 <= p["grid"] <= 148
+    assert p["splits"] >= 1 and p["kb_per_split"] * p["splits"] >= (k + 127) // 128
+    assert (p["splits"] - 1) * p["kb_per_split"] < (k + 127) // 128  # no empty split
+    if p["splits"] > 1:
+        assert p["workspace_bytes"] >= p["tiles"] * 128 * p["bn"] * 4
+
+
+def test_planner_splits_small_m_to_fill_the_gpu(pkg):
+    # decode: down_proj of the Qwen3-8B MLP has only 32 weight tiles
+    p = pkg.ops.gemm_plan(1, 4096, 12288)
+    assert p["tiles"] == 32 and p["splits"] > 4 and p["tiles"] * p["splits"] >= 148
+    # large prefill keeps one split
+    assert pkg.ops.gemm_plan(8192, 24576, 4096)["splits"] == 1
+
+
+def test_planner_respects_workspace_limit(pkg):
+    p = pkg.ops.gemm_plan(1, 4096, 12288, workspace_bytes=0)
+    assert p["splits"] == 1 and p["workspace_bytes"] == 0
+    with pytest.raises(pkg.W8A8Error):
+        pkg.ops.gemm_plan(1, 4096, 12288, splits=4, workspace_bytes=1024)
+    p = pkg.ops.gemm_plan(1, 4096, 12288, splits=4)
+    assert p["splits"] == 4
+
+
+def test_ops_refuse_cpu_tensors(pkg):
+    import torch
+
+    x = torch.zeros(4, 16, dtype=torch.bfloat16)
+    with pytest.raises(pkg.W8A8Error, match="no CPU path"):
+        pkg.ops.quant_per_token(x)
+    with pytest.raises(pkg.W8A8Error, match="no CPU path"):
+        pkg.ops.w8a8_gemm(torch.zeros(4, 16, dtype=torch.int8), torch.zeros(16, 16, dtype=torch.int8),
+                          torch.zeros(4), torch.zeros(16))

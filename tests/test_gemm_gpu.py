@@ -1,0 +1,138 @@
+"""GPU: kernel 2 (tcgen05 W8A8 GEMM) vs the CPU oracle.
+
+The int32 accumulator must be bit-exact.  The bf16 output follows the same
+separately-rounded fp32 dequant as the oracle and is asserted bit-exact too;
+the north-star tolerance (1e-2 rel / 1e-2 abs) is asserted on top as the
+contract bound.
+"""
+from __future__ import annotations
+
+import pytest
+import torch
+
+from conftest import golden
+
+pytestmark = pytest.mark.gpu
+
+RTOL = 1e-2
+ATOL = 1e-2
+
+
+def _operands(m, n, k, seed, bias=False):
+    g = torch.Generator().manual_seed(seed)
+    aq = torch.randint(-127, 128, (m, k), generator=g, dtype=torch.int8)
+    wq = torch.randint(-127, 128, (n, k), generator=g, dtype=torch.int8)
+    sa = torch.rand(m, generator=g) * 0.02 + 1e-4
+    sw = torch.rand(n, generator=g) * 0.002 + 1e-5
+    b = (torch.randn(n, generator=g) * 0.5).bfloat16() if bias else None
+    return aq, wq, sa, sw, b
+
+
+def _check(pkg, oracle, dev, m, n, k, variant=0, splits=0, bias=False, seed=0):
+    aq, wq, sa, sw, b = _operands(m, n, k, seed, bias)
+    acc_ref = oracle.int_gemm(aq, wq)
+    y_ref = oracle.dequant(acc_ref, sa, sw, b)
+    acc = torch.empty(m, n, dtype=torch.int32, device=dev)
+    y = pkg.ops.w8a8_gemm(aq.to(dev), wq.to(dev), sa.to(dev), sw.to(dev), None if b is None else b.to(dev),
+                          out_i32=acc, variant=variant, splits=splits)
+    torch.cuda.synchronize()
+    assert pkg.ops.device_error() == 0
+    assert torch.equal(acc.cpu(), acc_ref), f"int32 mismatch m={m} n={n} k={k} v={variant} s={splits}"
+    yc = y.cpu()
+    torch.testing.assert_close(yc.float(), y_ref.float(), rtol=RTOL, atol=ATOL)
+    assert torch.equal(yc, y_ref), f"bf16 mismatch m={m} n={n} k={k} v={variant} s={splits}"
+
+
+# (m, n, k) spanning every variant's edge cases: partial tiles, K not a
+# multiple of the 128-byte stage, tiny shapes.
+CASES = [
+    (1, 16, 16), (3, 48, 64), (17, 80, 144), (64, 272, 256), (128, 128, 128),
+    (130, 112, 160), (200, 512, 384), (257, 784, 1040), (64, 6144, 1024),
+]
+
+
+@pytest.mark.parametrize("variant", [1, 2, 3, 4, 5, 6])
+@pytest.mark.parametrize("m,n,k", CASES)
+def test_gemm_variants_bit_exact(pkg, oracle, cuda_dev, variant, m, n, k):
+    _check(pkg, oracle, cuda_dev, m, n, k, variant=variant, splits=1, seed=m + n + k + variant)
+
+
+@pytest.mark.parametrize("variant", [1, 2, 3, 5, 6])
+@pytest.mark.parametrize("splits", [2, 3, 7])
+def test_gemm_split_k_bit_exact(pkg, oracle, cuda_dev, variant, splits):
+    _check(pkg, oracle, cuda_dev, 40, 400, 1024, variant=variant, splits=splits, seed=splits * 10 + variant)
+
+
+@pytest.mark.parametrize("m,n,k", [(1, 24576, 4096), (16, 4096, 12288), (64, 6144, 1024), (256, 5120, 8192),
+                                   (2048, 2048, 4096), (33, 1280, 8192)])
+def test_gemm_auto_plan(pkg, oracle, cuda_dev, m, n, k):
+    _check(pkg, oracle, cuda_dev, m, n, k, bias=(m % 2 == 0), seed=m * 3 + n)
+
+
+def test_split_k_workspace_stays_zero(pkg, oracle, cuda_dev):
+    """Back-to-back split-K calls: every call leaves the workspace zeroed."""
+    for rep in range(3):
+        _check(pkg, oracle, cuda_dev, 5, 4096, 12288, seed=rep)
+    ws = pkg.ops.gemm_workspace(cuda_dev)
+    assert int(ws.count_nonzero()) == 0
+
+
+def test_gemm_golden_small(pkg, oracle, cuda_dev):
+    d = golden("w8a8_small.pt")
+    for key, c in d.items():
+        if key == "silu_mul_quant":
+            continue
+        dev = cuda_dev
+        xq, xs = pkg.ops.quant_per_token(c["x"].to(dev))
+        assert torch.equal(xq.cpu(), c["xq"]) and torch.equal(xs.cpu(), c["xs"]), key
+        n = c["wq"].shape[0]
+        if n % 16 or c["x"].shape[1] % 16:
+            continue
+        acc = torch.empty(c["acc"].shape, dtype=torch.int32, device=dev)
+        y = pkg.ops.w8a8_gemm(xq, c["wq"].to(dev), xs, c["ws"].to(dev),
+                              None if c["bias"] is None else c["bias"].to(dev), out_i32=acc)
+        assert torch.equal(acc.cpu(), c["acc"]), key
+        assert torch.equal(y.cpu(), c["y"]), key
+
+
+def test_gemm_matches_reference_bf16_forward_on_exact_inputs(pkg, oracle, cuda_dev):
+    """The full GPU path (quant kernel + GEMM) reproduces the reference layers'
+    bf16 F.linear outputs bit for bit on quantisation-exact inputs."""
+    d = golden("bf16_forward_exact.pt")
+    for key, c in d["cases"].items():
+        wq, ws = oracle.quant_weight_per_channel(c["weight"])
+        if wq.shape[0] % 16 or wq.shape[1] % 16:
+            continue
+        xq, xs = pkg.ops.quant_per_token(c["x"].to(cuda_dev))
+        y = pkg.ops.w8a8_gemm(xq, wq.to(cuda_dev), xs, ws.to(cuda_dev),
+                              None if c["bias"] is None else c["bias"].to(cuda_dev))
+        assert torch.equal(y.cpu(), c["y"]), key
+
+
+def test_gemm_empty_batch(pkg, cuda_dev):
+    aq = torch.empty(0, 64, dtype=torch.int8, device=cuda_dev)
+    wq = torch.zeros(32, 64, dtype=torch.int8, device=cuda_dev)
+    y = pkg.ops.w8a8_gemm(aq, wq, torch.empty(0, device=cuda_dev), torch.ones(32, device=cuda_dev))
+    assert y.shape == (0, 32)
+
+
+def test_gemm_extreme_values(pkg, oracle, cuda_dev):
+    """All-(-127) operands: the largest int32 magnitudes the K range produces."""
+    m, n, k = 24, 64, 16384
+    aq = torch.full((m, k), -127, dtype=torch.int8)
+    wq = torch.full((n, k), -127, dtype=torch.int8)
+    wq[1::2] = 127
+    sa = torch.full((m,), 1e-3)
+    sw = torch.full((n,), 1e-3)
+    acc = torch.empty(m, n, dtype=torch.int32, device=cuda_dev)
+    y = pkg.ops.w8a8_gemm(aq.to(cuda_dev), wq.to(cuda_dev), sa.to(cuda_dev), sw.to(cuda_dev), out_i32=acc)
+    ref = oracle.int_gemm(aq, wq)
+    assert torch.equal(acc.cpu(), ref)
+    assert torch.equal(y.cpu(), oracle.dequant(ref, sa, sw))
+
+
+def test_gemm_rejects_bad_shapes_without_launch(pkg, cuda_dev):
+    aq = torch.zeros(4, 24, dtype=torch.int8, device=cuda_dev)
+    wq = torch.zeros(32, 24, dtype=torch.int8, device=cuda_dev)
+    with pytest.raises(pkg.W8A8Error, match="multiple of 16"):
+        pkg.ops.w8a8_gemm(aq, wq, torch.ones(4, device=cuda_dev), torch.ones(32, device=cuda_dev))

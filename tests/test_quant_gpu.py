@@ -1,0 +1,92 @@
+"""GPU: kernel 1 (per-token quantiser, fused SiLU*mul+quant) vs the CPU oracle.
+
+int8 values and fp32 scales must be bit-exact.  The fused kernel's bf16 SiLU
+product may differ from the CPU's in the last bit where expf differs by an ulp;
+it is checked within 1 bf16 ulp (rel 2**-7) and its quantisation is checked
+bit-exact against the oracle applied to the kernel's own bf16 product.
+"""
+from __future__ import annotations
+
+import pytest
+import torch
+
+from conftest import golden
+
+pytestmark = pytest.mark.gpu
+
+SHAPES = [(1, 8), (1, 4096), (3, 24), (17, 1024), (64, 1024), (130, 5120), (257, 12288), (5, 28672), (33, 25600)]
+
+
+def _x(m, k, seed, scale=1.0):
+    g = torch.Generator().manual_seed(seed)
+    return (torch.randn(m, k, generator=g) * scale).bfloat16()
+
+
+@pytest.mark.parametrize("m,k", SHAPES)
+def test_quant_per_token_bit_exact(pkg, oracle, cuda_dev, m, k):
+    x = _x(m, k, seed=m * 7 + k)
+    q, s = pkg.ops.quant_per_token(x.to(cuda_dev))
+    qr, sr = oracle.quant_per_token(x)
+    assert torch.equal(s.cpu(), sr)
+    assert torch.equal(q.cpu(), qr)
+
+
+def test_quant_edge_rows(pkg, oracle, cuda_dev):
+    x = _x(6, 256, seed=3, scale=30.0)
+    x[0] = 0                                   # all-zero row: scale 0, q 0
+    x[1, :] = 1e-30                            # tiny values
+    x[2, 5] = 3.0e38                           # near bf16 max
+    x[3] = torch.linspace(-127, 127, 256).round().bfloat16()   # exact halves / integers
+    x[4, :128] = 0.5
+    x[4, 128] = 127                            # scale exactly 1 -> 0.5 rounds to even 0
+    q, s = pkg.ops.quant_per_token(x.to(cuda_dev))
+    qr, sr = oracle.quant_per_token(x)
+    assert torch.equal(s.cpu(), sr) and torch.equal(q.cpu(), qr)
+    assert float(s[0]) == 0.0 and int(q[0].abs().max()) == 0
+    assert int(q[4, 0]) == 0
+
+
+def test_quant_strided_rows(pkg, oracle, cuda_dev):
+    """A row-strided view (e.g. a slice of a wider buffer) quantises like its copy."""
+    big = _x(9, 512, seed=11).to(cuda_dev)
+    view = big[:, 128:384]
+    q, s = pkg.ops.quant_per_token(view)
+    qr, sr = oracle.quant_per_token(view.cpu())
+    assert torch.equal(q.cpu(), qr) and torch.equal(s.cpu(), sr)
+
+
+def test_quant_empty_batch(pkg, cuda_dev):
+    q, s = pkg.ops.quant_per_token(torch.empty(0, 64, dtype=torch.bfloat16, device=cuda_dev))
+    assert q.shape == (0, 64) and s.shape == (0,)
+
+
+@pytest.mark.parametrize("m,i", [(1, 8), (7, 96), (64, 3072), (5, 12288), (33, 6400), (2, 14336)])
+def test_silu_mul_quant(pkg, oracle, cuda_dev, m, i):
+    gu = _x(m, 2 * i, seed=m + i, scale=2.0)
+    qa, y = pkg.ops.silu_and_mul_quant(gu.to(cuda_dev), with_bf16=True)
+    y_ref = oracle.silu_and_mul(gu)
+    yc = y.cpu()
+    # bf16 product within one bf16 ulp of the CPU reference
+    diff = (yc.float() - y_ref.float()).abs()
+    assert torch.all(diff <= y_ref.float().abs() * 2.0 ** -7 + 1e-30), float(diff.max())
+    mismatch = (yc != y_ref).float().mean().item()
+    assert mismatch < 1e-3, mismatch
+    # quantisation of the kernel's own bf16 product is bit-exact
+    q_ref, s_ref = oracle.quant_per_token(yc)
+    assert torch.equal(qa.s.cpu(), s_ref) and torch.equal(qa.q.cpu(), q_ref)
+
+
+def test_silu_mul_quant_golden(pkg, oracle, cuda_dev):
+    c = golden("w8a8_small.pt")["silu_mul_quant"]
+    qa, y = pkg.ops.silu_and_mul_quant(c["gate_up"].to(cuda_dev), with_bf16=True)
+    q_ref, s_ref = oracle.quant_per_token(y.cpu())
+    assert torch.equal(qa.q.cpu(), q_ref) and torch.equal(qa.s.cpu(), s_ref)
+    assert (y.cpu().float() - c["y"].float()).abs().max() <= c["y"].float().abs().max() * 2.0 ** -7
+
+
+def test_silu_and_mul_compat_signature(pkg, oracle, cuda_dev):
+    gu = _x(4, 64, seed=9).to(cuda_dev)
+    out = torch.empty(4, 32, dtype=torch.bfloat16, device=cuda_dev)
+    y = pkg.silu_and_mul(gu, out=out)
+    assert y.data_ptr() == out.data_ptr()
+    torch.testing.assert_close(y.cpu(), oracle.silu_and_mul(gu.cpu()), rtol=2 ** -7, atol=0)
