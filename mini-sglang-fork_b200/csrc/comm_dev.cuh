@@ -1,0 +1,146 @@
+// Device side of the tensor-parallel communicator: layout of the IPC-shared
+// buffer, cross-rank flags with release/acquire at system scope, and the
+// bounded flag wait.
+//
+// Every rank owns one cudaMalloc'd buffer, mapped into its peers with CUDA
+// IPC (peer loads/stores travel over NVLink / NVSwitch):
+//
+//   [flags: 2 phases x kMaxSlots x kMaxWorld u32][ctrl: 1 KB][half 0][half 1]
+//
+// flags[phase][slot][src] on rank r is written by rank `src` (a peer store)
+// and polled by rank r (local loads).  A flag holds the epoch of the call
+// that last signalled it; waits compare for equality, epochs only grow.
+// ctrl[0] = epoch of the last completed call, ctrl[1] = CTAs finished in the
+// current call, ctrl[2..3] = where the last bounded wait gave up.  Calls use
+// data half (epoch & 1): a rank can only start writing a half again after
+// every peer has passed a barrier of the next call, i.e. after every peer has
+// finished reading that half, so no end-of-call barrier is needed.
+#pragma once
+
+#include <cuda_bf16.h>
+
+#include <cstdint>
+
+#include "sm100.cuh"
+
+namespace w8a8 {
+
+constexpr int kMaxWorld = 8;
+constexpr int kMaxSlots = 8192;
+constexpr size_t kFlagBytes = 2ull * kMaxSlots * kMaxWorld * sizeof(uint32_t);
+constexpr size_t kCtrlBytes = 1024;
+constexpr size_t kHeaderBytes = kFlagBytes + kCtrlBytes;
+
+struct CommView {
+  char* base[kMaxWorld];  // every rank's buffer, as mapped in this process
+  int rank;
+  int world;
+  unsigned long long half_bytes;
+  unsigned int* err;      // device error word
+  long long timeout_ns;
+};
+
+namespace dev {
+
+__device__ __forceinline__ uint32_t* flag_ptr(char* base, int phase, int slot, int src) {
+  return reinterpret_cast<uint32_t*>(base) + (static_cast<size_t>(phase) * kMaxSlots + slot) * kMaxWorld + src;
+}
+
+__device__ __forceinline__ uint32_t* ctrl_ptr(char* base) {
+  return reinterpret_cast<uint32_t*>(base + kFlagBytes);
+}
+
+__device__ __forceinline__ char* half_ptr(const CommView& v, int r, uint32_t epoch) {
+  return v.base[r] + kHeaderBytes + static_cast<size_t>(epoch & 1u) * v.half_bytes;
+}
+
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ uint32_t ld_relaxed_gpu(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Thread `t` (< world) of the calling group tells rank t that this rank has
+// reached (phase, slot) of call `epoch`.  The caller has synchronised the
+// group after its data stores; the system-scope fence makes those stores
+// (cumulatively) visible before the flag.
+__device__ __forceinline__ void signal_peers(const CommView& v, int phase, int slot, uint32_t epoch, int t) {
+  if (t < v.world) {
+    __threadfence_system();
+    st_release_sys(flag_ptr(v.base[t], phase, slot, v.rank), epoch);
+  }
+}
+
+// Thread `t` (< world) waits until rank t has signalled (phase, slot) of call
+// `epoch`.  Bounded by v.timeout_ns; on expiry records where and returns false.
+__device__ __forceinline__ bool wait_peer(const CommView& v, int phase, int slot, uint32_t epoch, int t) {
+  if (t >= v.world) return true;
+  const uint32_t* f = flag_ptr(v.base[v.rank], phase, slot, t);
+  if (ld_acquire_sys(f) == epoch) return true;
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t it = 1;; ++it) {
+    if (ld_acquire_sys(f) == epoch) return true;
+    if ((it & 255u) == 0 && globaltimer_ns() - t0 > static_cast<uint64_t>(v.timeout_ns)) {
+      if (v.err) atomicOr(v.err, 2u /* kErrCommWait */);
+      uint32_t* c = ctrl_ptr(v.base[v.rank]);
+      c[2] = (static_cast<uint32_t>(phase) << 24) | static_cast<uint32_t>(slot);
+      c[3] = static_cast<uint32_t>(t);
+      return false;
+    }
+  }
+}
+
+// 16-byte load that bypasses this SM's L1 (peer data changes between calls).
+__device__ __forceinline__ uint4 ld_volatile_v4(const void* p) {
+  uint4 r;
+  asm volatile("ld.volatile.global.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(p)
+               : "memory");
+  return r;
+}
+
+// fp32 rank-order sum of 8 bf16 lanes from every rank's copy of one 16-byte
+// vector, rounded once to bf16 (the oracle's all_reduce_sum: start from rank
+// 0's value, add ranks 1..p-1 in order).
+__device__ __forceinline__ uint4 sum_ranks_vec8(const CommView& v, uint32_t epoch, size_t byte_off) {
+  float acc[8];
+  {
+    const uint4 raw = ld_volatile_v4(half_ptr(v, 0, epoch) + byte_off);
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 f = __bfloat1622float2(h[j]);
+      acc[2 * j] = f.x;
+      acc[2 * j + 1] = f.y;
+    }
+  }
+  for (int r = 1; r < v.world; ++r) {
+    const uint4 raw = ld_volatile_v4(half_ptr(v, r, epoch) + byte_off);
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 f = __bfloat1622float2(h[j]);
+      acc[2 * j] = __fadd_rn(acc[2 * j], f.x);
+      acc[2 * j + 1] = __fadd_rn(acc[2 * j + 1], f.y);
+    }
+  }
+  uint4 out;
+  __nv_bfloat162* o = reinterpret_cast<__nv_bfloat162*>(&out);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) o[j] = __floats2bfloat162_rn(acc[2 * j], acc[2 * j + 1]);
+  return out;
+}
+
+}  // namespace dev
+}  // namespace w8a8

@@ -1,4 +1,5 @@
-// Kernel 2: W8A8 GEMM on 5th-generation tensor cores (tcgen05, kind::i8).
+// Kernel 2: W8A8 GEMM on 5th-generation tensor cores (tcgen05, kind::i8),
+// optionally fused with the row-parallel all-reduce over NVLink peer memory.
 //
 //   C[M, N] = bf16( (f32(sum_k A[m,k] * B[n,k]) * sa[m]) * sb[n] + bias[n] )
 //
@@ -29,13 +30,23 @@
 // Split-K (few output tiles, e.g. decode): the K blocks of a tile are cut into
 // `splits` ranges handled by different CTAs.  Each adds its int32 partial tile
 // into a workspace with red.global.add (exact and order-independent), then the
-// last CTA to arrive on the tile's counter dequantises the sum, writes C and
-// zeroes the workspace tile and counter again, so the workspace stays zeroed
-// between calls.
+// last CTA to arrive on the tile's counter dequantises the sum, writes the
+// tile and zeroes the workspace tile and counter again, so the workspace stays
+// zeroed between calls.
 //
-// Every mbarrier wait is bounded (%globaltimer); on expiry the CTA raises a
-// shared abort flag and the device error word, drains its in-flight TMA loads
-// and MMAs (bounded too), frees TMEM and exits.
+// Fused all-reduce (row-parallel layers, FUSED = true).  The epilogue writes
+// each finished bf16 partial tile into this rank's IPC-shared buffer (same
+// [M, N] layout as C) and raises the tile's "ready" flag on every rank.  After
+// its GEMM units, CTA b reduces the tiles t with t % grid == b in two shots:
+// it waits for every rank's ready(t), sums its 1/world share of the tile from
+// all ranks in rank order (fp32, one rounding), writes it back in place and
+// raises reduced(t) everywhere; then it waits for every rank's reduced(t) and
+// gathers the shares into C.  Waits happen only after all of the CTA's own
+// signals, so no wait can block a signal another rank needs.
+//
+// Every mbarrier / flag wait is bounded (%globaltimer); on expiry the CTA
+// raises a shared abort flag and the device error word, drains its in-flight
+// TMA loads and MMAs (bounded too), frees TMEM and exits.
 #pragma once
 
 #include <cuda.h>
@@ -43,6 +54,7 @@
 
 #include <cstdint>
 
+#include "comm_dev.cuh"
 #include "sm100.cuh"
 
 namespace w8a8 {
@@ -86,10 +98,7 @@ struct GemmTraits {
   static_assert(kSmemBytes <= 227 * 1024, "shared memory");
 };
 
-__device__ __forceinline__ void unit_coords(const GemmArgs& a, int unit, int& tw, int& tn, int& kb0,
-                                            int& kb1, int& tile) {
-  tile = unit / a.splits;
-  const int split = unit - tile * a.splits;
+__device__ __forceinline__ void tile_coords(const GemmArgs& a, int tile, int& tw, int& tn) {
   if (a.wide_fast) {
     tw = tile % a.tiles_w;
     tn = tile / a.tiles_w;
@@ -97,6 +106,13 @@ __device__ __forceinline__ void unit_coords(const GemmArgs& a, int unit, int& tw
     tn = tile % a.tiles_n;
     tw = tile / a.tiles_n;
   }
+}
+
+__device__ __forceinline__ void unit_coords(const GemmArgs& a, int unit, int& tw, int& tn, int& kb0,
+                                            int& kb1, int& tile) {
+  tile = unit / a.splits;
+  const int split = unit - tile * a.splits;
+  tile_coords(a, tile, tw, tn);
   kb0 = split * a.kb_per_split;
   kb1 = min(a.kblocks, kb0 + a.kb_per_split);
 }
@@ -105,18 +121,20 @@ __device__ __forceinline__ float dequant1(int32_t acc, float sa, float sb) {
   return __fmul_rn(__fmul_rn(__int2float_rn(acc), sa), sb);
 }
 
-// Dequantise 32 accumulators of one TMEM row and store them.
-//   normal: row = token m, the 32 values are channels n0..n0+31.
-//   swap:   row = channel n, the 32 values are tokens m0..m0+31.
+// Dequantise CH accumulators of one TMEM row and store them into `out`
+// ([M, N] bf16, row stride a.ldc).
+//   normal: row = token m, the values are channels col0..col0+CH-1.
+//   swap:   row = channel n, the values are tokens col0..col0+CH-1.
 template <bool SWAP, int CH>
-__device__ __forceinline__ void store_chunk(const GemmArgs& a, int row, int col0, const uint32_t (&v)[32]) {
+__device__ __forceinline__ void store_chunk(const GemmArgs& a, __nv_bfloat16* out, int row, int col0,
+                                            const uint32_t (&v)[32]) {
   if (!SWAP) {
     const int m = row;
     if (m >= a.M) return;
     const float sam = __ldg(a.sa + m);
-    __nv_bfloat16* crow = a.C + static_cast<int64_t>(m) * a.ldc;
+    __nv_bfloat16* crow = out + static_cast<int64_t>(m) * a.ldc;
 #pragma unroll
-    for (int g = 0; g < 4; ++g) {
+    for (int g = 0; g < CH / 8; ++g) {
       const int n = col0 + g * 8;
       if (n >= a.N) break;  // N % 16 == 0: granules are either fully in or out
       uint4 pk;
@@ -150,16 +168,83 @@ __device__ __forceinline__ void store_chunk(const GemmArgs& a, int row, int col0
       if (m >= a.M) break;
       float y = dequant1(static_cast<int32_t>(v[j]), __ldg(a.sa + m), sbn);
       if (a.bias) y = __fadd_rn(y, bn);
-      a.C[static_cast<int64_t>(m) * a.ldc + n] = __float2bfloat16_rn(y);
+      out[static_cast<int64_t>(m) * a.ldc + n] = __float2bfloat16_rn(y);
       if (a.c_i32) a.c_i32[static_cast<int64_t>(m) * a.N + n] = static_cast<int32_t>(v[j]);
     }
   }
 }
 
-template <int BN, int STAGES, bool SWAP>
+// Output rectangle of a tile in C coordinates: rows [m0, m0+hm), columns
+// [n0, n0+wn) with wn a multiple of 8.
+template <int BN, bool SWAP>
+__device__ __forceinline__ void tile_rect(const GemmArgs& a, int tile, int& m0, int& hm, int& n0, int& wn) {
+  int tw, tn;
+  tile_coords(a, tile, tw, tn);
+  if (!SWAP) {
+    m0 = tw * 128;
+    hm = min(128, a.M - m0);
+    n0 = tn * BN;
+    wn = min(BN, a.N - n0);
+  } else {
+    m0 = tn * BN;
+    hm = min(BN, a.M - m0);
+    n0 = tw * 128;
+    wn = min(128, a.N - n0);
+  }
+}
+
+// Two-shot reduction of the tiles this CTA owns (t % gridDim.x == blockIdx.x)
+// across the ranks, by the 128 epilogue threads (index et).  Returns false if a
+// flag wait timed out.
+template <int BN, bool SWAP>
+__device__ bool fused_reduce_tiles(const GemmArgs& a, const CommView& cv, uint32_t epoch, int et) {
+  __nv_bfloat16* mine = reinterpret_cast<__nv_bfloat16*>(dev::half_ptr(cv, cv.rank, epoch));
+  // shot 1: reduce-scatter of every owned tile
+  for (int t = blockIdx.x; t < a.num_tiles; t += gridDim.x) {
+    const bool ok = dev::wait_peer(cv, 0, t, epoch, et);
+    if (dev::named_bar_or(1, 128, !ok)) return false;
+    int m0, hm, n0, wn;
+    tile_rect<BN, SWAP>(a, t, m0, hm, n0, wn);
+    const int vpr = wn >> 3;
+    const int nv = hm * vpr;
+    const int lo = static_cast<int>((static_cast<long long>(nv) * cv.rank) / cv.world);
+    const int hi = static_cast<int>((static_cast<long long>(nv) * (cv.rank + 1)) / cv.world);
+    for (int i = lo + et; i < hi; i += 128) {
+      const int r = i / vpr, c = i - r * vpr;
+      const size_t off = (static_cast<size_t>(m0 + r) * a.N + n0 + c * 8) * 2;
+      const uint4 s = dev::sum_ranks_vec8(cv, epoch, off);
+      *reinterpret_cast<uint4*>(reinterpret_cast<char*>(mine) + off) = s;
+    }
+    dev::named_bar_sync(1, 128);
+    dev::signal_peers(cv, 1, t, epoch, et);
+  }
+  // shot 2: all-gather of every owned tile into C
+  for (int t = blockIdx.x; t < a.num_tiles; t += gridDim.x) {
+    const bool ok = dev::wait_peer(cv, 1, t, epoch, et);
+    if (dev::named_bar_or(1, 128, !ok)) return false;
+    int m0, hm, n0, wn;
+    tile_rect<BN, SWAP>(a, t, m0, hm, n0, wn);
+    const int vpr = wn >> 3;
+    const int nv = hm * vpr;
+    for (int src = 0; src < cv.world; ++src) {
+      const int lo = static_cast<int>((static_cast<long long>(nv) * src) / cv.world);
+      const int hi = static_cast<int>((static_cast<long long>(nv) * (src + 1)) / cv.world);
+      const char* from = dev::half_ptr(cv, src, epoch);
+      for (int i = lo + et; i < hi; i += 128) {
+        const int r = i / vpr, c = i - r * vpr;
+        const size_t idx = static_cast<size_t>(m0 + r) * a.N + n0 + c * 8;
+        *reinterpret_cast<uint4*>(a.C + static_cast<size_t>(m0 + r) * a.ldc + n0 + c * 8) =
+            dev::ld_volatile_v4(from + idx * 2);
+      }
+    }
+  }
+  return true;
+}
+
+template <int BN, int STAGES, bool SWAP, bool FUSED>
 __global__ void __launch_bounds__(192, 1)
     w8a8_gemm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_n,
-                     const GemmArgs args) {
+                     const GemmArgs args, const CommView cv) {
   using T = GemmTraits<BN, STAGES, SWAP>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -177,6 +262,15 @@ __global__ void __launch_bounds__(192, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+
+  // Fused mode: the call's epoch (published by the previous call's last CTA)
+  // selects the data half; partial tiles go there instead of C.
+  uint32_t epoch = 0;
+  __nv_bfloat16* out = args.C;
+  if constexpr (FUSED) {
+    epoch = dev::ld_relaxed_gpu(dev::ctrl_ptr(cv.base[cv.rank])) + 1u;
+    out = reinterpret_cast<__nv_bfloat16*>(dev::half_ptr(cv, cv.rank, epoch));
+  }
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -313,15 +407,20 @@ __global__ void __launch_bounds__(192, 1)
     const int et = threadIdx.x - 64;  // 0..127 among the epilogue threads
     int acc = 0;
     uint32_t acc_phase = 0;
+    bool aborted = false;
     for (int unit = blockIdx.x; unit < args.units; unit += gridDim.x) {
       int tw, tn, kb0, kb1, tile;
       unit_coords(args, unit, tw, tn, kb0, kb1, tile);
       const bool ok = dev::mbar_wait(dev::smem_u32(acc_full + acc), acc_phase, abort_flag, args.err,
                                      kErrGemmWait, tmo);
-      if (dev::named_bar_or(1, 128, !ok)) break;  // uniform exit of all epilogue threads
+      if (dev::named_bar_or(1, 128, !ok)) {  // uniform exit of all epilogue threads
+        aborted = true;
+        break;
+      }
       dev::tc_fence_after();
       const uint32_t t_acc = tmem_base + lane_base + static_cast<uint32_t>(acc * T::kAccCols);
       const int row = tw * T::kBM + row_in_tile;
+      bool wrote_tile = true;
       if (args.splits == 1) {
 #pragma unroll 1
         for (int c = 0; c < T::kChunks; ++c) {
@@ -332,7 +431,7 @@ __global__ void __launch_bounds__(192, 1)
             dev::tc_fence_before();
             dev::mbar_arrive(dev::smem_u32(acc_empty + acc));
           }
-          store_chunk<SWAP, T::kChunk>(args, row, tn * BN + c * T::kChunk, v);
+          store_chunk<SWAP, T::kChunk>(args, out, row, tn * BN + c * T::kChunk, v);
         }
       } else {
         int32_t* wtile = args.ws + static_cast<int64_t>(tile) * (T::kBM * BN);
@@ -356,8 +455,8 @@ __global__ void __launch_bounds__(192, 1)
           *last_flag = (prev == static_cast<uint32_t>(args.splits - 1)) ? 1 : 0;
         }
         dev::named_bar_sync(1, 128);
-        const bool last = *last_flag != 0;
-        if (last) {
+        wrote_tile = *last_flag != 0;
+        if (wrote_tile) {
           __threadfence();
 #pragma unroll 1
           for (int c = 0; c < T::kChunks; ++c) {
@@ -372,12 +471,19 @@ __global__ void __launch_bounds__(192, 1)
                 v[j] = 0u;
               }
             }
-            store_chunk<SWAP, T::kChunk>(args, row, tn * BN + c * T::kChunk, v);
+            store_chunk<SWAP, T::kChunk>(args, out, row, tn * BN + c * T::kChunk, v);
           }
           if (et == 0) args.counters[tile] = 0u;
         }
         // last_flag is rewritten by the next tile: keep every reader ahead of it
         dev::named_bar_sync(1, 128);
+      }
+      if constexpr (FUSED) {
+        if (wrote_tile) {
+          // all 128 threads' partial stores precede the ready flag
+          dev::named_bar_sync(1, 128);
+          dev::signal_peers(cv, 0, tile, epoch, et);
+        }
       }
       if (++acc == 2) {
         acc = 0;
@@ -385,12 +491,28 @@ __global__ void __launch_bounds__(192, 1)
       }
     }
     dev::tc_fence_before();
+    if constexpr (FUSED) {
+      if (!aborted) fused_reduce_tiles<BN, SWAP>(args, cv, epoch, et);
+    }
   }
 
   __syncthreads();
   if (warp == 1) {
     dev::tc_fence_after();
     dev::tmem_dealloc(tmem_base, T::kTmemCols);
+  }
+  if constexpr (FUSED) {
+    // The last CTA of the call publishes the epoch for the next call.
+    if (threadIdx.x == 0) {
+      uint32_t* c = dev::ctrl_ptr(cv.base[cv.rank]);
+      __threadfence();
+      const uint32_t done = atomicAdd(c + 1, 1u);
+      if (done == gridDim.x - 1) {
+        c[1] = 0u;
+        __threadfence();
+        atomicExch(c, epoch);
+      }
+    }
   }
 }
 
