@@ -112,6 +112,9 @@ size_t w8a8_comm_handle_bytes(void);
 int w8a8_comm_create(int rank, int world, int device, size_t max_bytes, w8a8_comm** comm,
                      void* handle_out);
 int w8a8_comm_open_peers(w8a8_comm* comm, const void* all_handles);
+/* Algorithm of w8a8_all_reduce: 0 = automatic (one-shot for world 2 or small
+ * tensors, two-shot otherwise), 1 = always one-shot, 2 = always two-shot. */
+int w8a8_comm_set_mode(w8a8_comm* comm, int mode);
 /* Bounded-wait budget of every device-side flag wait (default 10 s). */
 int w8a8_comm_set_timeout_ms(w8a8_comm* comm, int64_t timeout_ms);
 

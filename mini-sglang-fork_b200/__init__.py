@@ -10,7 +10,7 @@ The directory name is not a Python identifier; import it with
 """
 from __future__ import annotations
 
-from . import _lib, distributed, layers, ops
+from . import _lib, comm, distributed, layers, ops
 from ._lib import W8A8Error
 from .distributed import (DistributedCommunicator, DistributedInfo, destroy_distributed,
                           enable_peer_mem_distributed, get_tp_info, reset_tp_info, set_tp_info,

@@ -22,6 +22,7 @@
 
 #include "comm_dev.cuh"
 #include "common.cuh"
+#include "gemm_api.h"
 #include "gemm_plan.h"
 
 namespace {
@@ -50,6 +51,7 @@ struct w8a8_comm {
   char* peers[w8a8::kMaxWorld] = {nullptr};
   bool opened = false;
   long long timeout_ns = 10000000000LL;  // 10 s
+  int mode = 0;                           // 0 auto, 1 one-shot, 2 two-shot
 };
 
 namespace w8a8 {
@@ -246,6 +248,13 @@ int w8a8_comm_open_peers(w8a8_comm* c, const void* all_handles) {
   return W8A8_OK;
 }
 
+int w8a8_comm_set_mode(w8a8_comm* c, int mode) {
+  W8A8_REQUIRE(c != nullptr, W8A8_ERR_INVALID_ARG, "comm_set_mode: null comm");
+  W8A8_REQUIRE(mode >= 0 && mode <= 2, W8A8_ERR_INVALID_ARG, "comm_set_mode: mode %d not in {0, 1, 2}", mode);
+  c->mode = mode;
+  return W8A8_OK;
+}
+
 int w8a8_comm_set_timeout_ms(w8a8_comm* c, int64_t timeout_ms) {
   W8A8_REQUIRE(c != nullptr, W8A8_ERR_INVALID_ARG, "comm_set_timeout_ms: null comm");
   W8A8_REQUIRE(timeout_ms > 0 && timeout_ms <= 600000, W8A8_ERR_INVALID_ARG,
@@ -271,7 +280,7 @@ int w8a8_all_reduce(w8a8_comm* c, void* x, int64_t numel, void* stream) {
   if (!err) return W8A8_ERR_CUDA;
   const CommView v = make_view(c, err);
   const long long nvec = numel / 8;
-  const bool one = use_one_shot(c->world, bytes);
+  const bool one = c->mode == 1 || (c->mode == 0 && use_one_shot(c->world, bytes));
   const long long per_chunk = one ? nvec : (nvec + c->world - 1) / c->world;
   int nsm = sm_count();
   if (nsm <= 0) nsm = 148;
@@ -281,6 +290,22 @@ int w8a8_all_reduce(w8a8_comm* c, void* x, int64_t numel, void* stream) {
       v, static_cast<uint4*>(x), nvec, one ? 0 : 1);
   W8A8_CUDA_TRY(cudaGetLastError());
   return W8A8_OK;
+}
+
+int w8a8_gemm_allreduce(w8a8_comm* c, const int8_t* A, const int8_t* B, const float* sa, const float* sb,
+                        const void* bias, void* C, int64_t M, int64_t N, int64_t K, void* workspace,
+                        size_t workspace_bytes, void* stream) {
+  using namespace w8a8;
+  int rc = comm_ready(c);
+  if (rc) return rc;
+  if (c->world == 1)
+    return run_gemm(A, B, sa, sb, bias, C, nullptr, M, N, K, 0, 0, workspace, workspace_bytes,
+                    static_cast<cudaStream_t>(stream), kDefaultGemmTimeoutNs, nullptr);
+  unsigned int* err = device_error_word();
+  if (!err) return W8A8_ERR_CUDA;
+  const CommView v = make_view(c, err);
+  return run_gemm(A, B, sa, sb, bias, C, nullptr, M, N, K, 0, 0, workspace, workspace_bytes,
+                  static_cast<cudaStream_t>(stream), c->timeout_ns, &v);
 }
 
 int w8a8_comm_status(w8a8_comm* c, int* device_error) {

@@ -9,6 +9,7 @@
 
 #include "common.cuh"
 #include "gemm_sm100.cuh"
+#include "gemm_api.h"
 #include "gemm_plan.h"
 
 namespace w8a8 {
@@ -49,11 +50,11 @@ int encode_operand(CUtensorMap* tm, const void* base, int64_t rows, int64_t K, i
   return W8A8_OK;
 }
 
-template <int BN, int STAGES, bool SWAP>
+template <int BN, int STAGES, bool SWAP, bool FUSED>
 int launch_variant(const GemmPlan& p, const CUtensorMap& tw, const CUtensorMap& tn, const GemmArgs& args,
-                   cudaStream_t stream) {
+                   const CommView& cv, cudaStream_t stream) {
   using T = GemmTraits<BN, STAGES, SWAP>;
-  auto kern = w8a8_gemm_kernel<BN, STAGES, SWAP>;
+  auto kern = w8a8_gemm_kernel<BN, STAGES, SWAP, FUSED>;
   static std::mutex mu;
   static bool configured[64] = {false};
   const int dev = current_device();
@@ -65,7 +66,7 @@ int launch_variant(const GemmPlan& p, const CUtensorMap& tw, const CUtensorMap& 
       configured[dev] = true;
     }
   }
-  kern<<<p.grid, T::kThreads, T::kSmemBytes, stream>>>(tw, tn, args);
+  kern<<<p.grid, T::kThreads, T::kSmemBytes, stream>>>(tw, tn, args, cv);
   W8A8_CUDA_TRY(cudaGetLastError());
   return W8A8_OK;
 }
@@ -87,9 +88,23 @@ int validate_gemm_args(const int8_t* A, const int8_t* B, const float* sa, const 
   return W8A8_OK;
 }
 
+template <bool FUSED>
+int dispatch_variant(const GemmPlan& p, const CUtensorMap& tw, const CUtensorMap& tn, const GemmArgs& args,
+                     const CommView& cv, cudaStream_t stream) {
+  switch (p.variant) {
+    case 1: return launch_variant<256, 4, false, FUSED>(p, tw, tn, args, cv, stream);
+    case 2: return launch_variant<128, 6, false, FUSED>(p, tw, tn, args, cv, stream);
+    case 3: return launch_variant<16, 10, true, FUSED>(p, tw, tn, args, cv, stream);
+    case 4: return launch_variant<32, 9, true, FUSED>(p, tw, tn, args, cv, stream);
+    case 5: return launch_variant<64, 8, true, FUSED>(p, tw, tn, args, cv, stream);
+    case 6: return launch_variant<128, 6, true, FUSED>(p, tw, tn, args, cv, stream);
+    default: return fail(W8A8_ERR_INVALID_ARG, "gemm: unknown variant %d", p.variant);
+  }
+}
+
 int run_gemm(const int8_t* A, const int8_t* B, const float* sa, const float* sb, const void* bias, void* C,
              int32_t* c_i32, int64_t M, int64_t N, int64_t K, int variant, int splits, void* workspace,
-             size_t workspace_bytes, cudaStream_t stream, long long timeout_ns) {
+             size_t workspace_bytes, cudaStream_t stream, long long timeout_ns, const CommView* comm) {
   W8A8_REQUIRE(M >= 0 && N >= 0 && K >= 0, W8A8_ERR_INVALID_ARG, "gemm: negative shape");
   if (M == 0) return W8A8_OK;  // empty batch: nothing to compute (its tensors may be null)
   int rc = validate_gemm_args(A, B, sa, sb, C, M, N, K);
@@ -101,6 +116,14 @@ int run_gemm(const int8_t* A, const int8_t* B, const float* sa, const float* sb,
   GemmPlan p;
   rc = plan_gemm(M, N, K, variant, splits, workspace_bytes, sm_count(), &p);
   W8A8_REQUIRE(rc == 0, W8A8_ERR_WORKSPACE, "gemm: %s", plan_error(rc));
+  if (comm) {
+    W8A8_REQUIRE(p.num_tiles <= kMaxSlots, W8A8_ERR_UNSUPPORTED,
+                 "gemm_allreduce: %d output tiles exceed the %d flag slots", p.num_tiles, kMaxSlots);
+    W8A8_REQUIRE(static_cast<unsigned long long>(M) * N * 2 <= comm->half_bytes, W8A8_ERR_INVALID_ARG,
+                 "gemm_allreduce: output of %lld x %lld bf16 exceeds the communicator's max_bytes %llu",
+                 (long long)M, (long long)N, comm->half_bytes);
+    W8A8_REQUIRE(c_i32 == nullptr, W8A8_ERR_INVALID_ARG, "gemm_allreduce: no int32 output in fused mode");
+  }
   if (p.splits > 1) {
     W8A8_REQUIRE(workspace != nullptr && workspace_bytes >= p.ws_bytes, W8A8_ERR_WORKSPACE,
                  "gemm: split-K needs a zeroed workspace of %zu bytes", p.ws_bytes);
@@ -145,15 +168,10 @@ int run_gemm(const int8_t* A, const int8_t* B, const float* sa, const float* sb,
   args.units = p.units;
   args.wide_fast = p.wide_fast;
 
-  switch (p.variant) {
-    case 1: return launch_variant<256, 4, false>(p, tw, tn, args, stream);
-    case 2: return launch_variant<128, 6, false>(p, tw, tn, args, stream);
-    case 3: return launch_variant<16, 10, true>(p, tw, tn, args, stream);
-    case 4: return launch_variant<32, 9, true>(p, tw, tn, args, stream);
-    case 5: return launch_variant<64, 8, true>(p, tw, tn, args, stream);
-    case 6: return launch_variant<128, 6, true>(p, tw, tn, args, stream);
-    default: return fail(W8A8_ERR_INVALID_ARG, "gemm: unknown variant %d", p.variant);
-  }
+  if (comm) return dispatch_variant<true>(p, tw, tn, args, *comm, stream);
+  CommView none;
+  std::memset(&none, 0, sizeof(none));
+  return dispatch_variant<false>(p, tw, tn, args, none, stream);
 }
 
 }  // namespace w8a8
@@ -191,7 +209,7 @@ int w8a8_gemm(const int8_t* A, const int8_t* B, const float* sa, const float* sb
               int32_t* c_i32, int64_t M, int64_t N, int64_t K, void* workspace, size_t workspace_bytes,
               void* stream) {
   return w8a8::run_gemm(A, B, sa, sb, bias, C, c_i32, M, N, K, 0, 0, workspace, workspace_bytes,
-                        static_cast<cudaStream_t>(stream), w8a8::kDefaultGemmTimeoutNs);
+                        static_cast<cudaStream_t>(stream), w8a8::kDefaultGemmTimeoutNs, nullptr);
 }
 
 int w8a8_gemm_config(const int8_t* A, const int8_t* B, const float* sa, const float* sb, const void* bias,
@@ -201,7 +219,7 @@ int w8a8_gemm_config(const int8_t* A, const int8_t* B, const float* sa, const fl
                variant);
   W8A8_REQUIRE(splits >= 0, W8A8_ERR_INVALID_ARG, "gemm_config: negative splits");
   return w8a8::run_gemm(A, B, sa, sb, bias, C, c_i32, M, N, K, variant, splits, workspace, workspace_bytes,
-                        static_cast<cudaStream_t>(stream), w8a8::kDefaultGemmTimeoutNs);
+                        static_cast<cudaStream_t>(stream), w8a8::kDefaultGemmTimeoutNs, nullptr);
 }
 
 }  // extern "C"

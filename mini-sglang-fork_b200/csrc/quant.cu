@@ -2,22 +2,30 @@
 // SiLU*mul (the silu_and_mul step between gate_up and down in GatedMLP,
 // M/models/utils.py:44-50 and M/layers/activation.py:9-12 of mini-sglang).
 //
-// One CTA per row.  The row is read once with 128-bit loads into registers
-// (VPT 16-byte vectors per thread), reduced to its absmax with warp shuffles
-// plus one shared-memory step, then quantised from registers and written with
-// 64-bit stores — HBM traffic is exactly 2K bytes in + K bytes + 4 out per
-// row.  Arithmetic convention (bit-exact with the CPU oracle):
+// One CTA per row; the row is read once from HBM with 128-bit loads, reduced
+// to its absmax (warp shuffles + one shared-memory step), then quantised from
+// on-chip storage and written with 64-bit stores, so HBM traffic is exactly
+// the algorithmic 2K (or 4I) bytes in and K (+4) bytes out per row.
+//   rows of <= 1024 vectors: kept in registers (VPT vectors per thread,
+//                            <= 256 threads, many CTAs per SM);
+//   longer rows:             staged in shared memory (512 threads, up to
+//                            64 KB per CTA, >= 3 CTAs per SM), so occupancy
+//                            does not collapse on 25600-wide rows.
+// Arithmetic convention (bit-exact with the CPU oracle):
 //   s = fp32(amax) / 127.0f (IEEE divide), q = clamp(rint_even(x / s), +-127),
 //   q = 0 for an all-zero row.
 #include <cuda_bf16.h>
 
 #include <cstdint>
+#include <mutex>
 
 #include "common.cuh"
 
 namespace {
 
-constexpr int kMaxThreads = 512;
+constexpr int kRegThreads = 256;
+constexpr int kSmemThreads = 512;
+constexpr int kMaxVec = 4096;  // 16-byte vectors per row (K <= 32768)
 
 __device__ __forceinline__ float warp_max(float v) {
 #pragma unroll
@@ -33,8 +41,7 @@ __device__ __forceinline__ float block_max(float v, float* red) {
   __syncthreads();
   const int nw = (blockDim.x + 31) >> 5;
   float r = (lane < nw) ? red[lane] : 0.0f;
-  r = warp_max(r);
-  return r;
+  return warp_max(r);
 }
 
 __device__ __forceinline__ int8_t quant_one(float v, float s) {
@@ -72,35 +79,6 @@ __device__ __forceinline__ float vec8_absmax(const uint4& raw) {
   return m;
 }
 
-template <int VPT>
-__global__ void __launch_bounds__(kMaxThreads) quant_rows_kernel(const __nv_bfloat16* __restrict__ x,
-                                                                 int64_t ldx, int8_t* __restrict__ q,
-                                                                 float* __restrict__ scale, int K) {
-  __shared__ float red[32];
-  const int64_t row = blockIdx.x;
-  const int nvec = K >> 3;
-  const uint4* xr = reinterpret_cast<const uint4*>(x + row * ldx);
-  uint4 buf[VPT];
-  float amax = 0.0f;
-#pragma unroll
-  for (int i = 0; i < VPT; ++i) {
-    const int vi = threadIdx.x + i * blockDim.x;
-    if (vi < nvec) {
-      buf[i] = __ldcs(xr + vi);
-      amax = fmaxf(amax, vec8_absmax(buf[i]));
-    }
-  }
-  amax = block_max(amax, red);
-  const float s = __fdiv_rn(amax, 127.0f);
-  uint2* qr = reinterpret_cast<uint2*>(q + row * static_cast<int64_t>(K));
-#pragma unroll
-  for (int i = 0; i < VPT; ++i) {
-    const int vi = threadIdx.x + i * blockDim.x;
-    if (vi < nvec) qr[vi] = quant_vec8(buf[i], s);
-  }
-  if (threadIdx.x == 0) scale[row] = s;
-}
-
 // y = bf16(silu(g) * u) for 8 lanes, silu(g) = g / (1 + exp(-g)) in fp32.
 __device__ __forceinline__ uint4 silu_mul_vec8(const uint4& graw, const uint4& uraw) {
   const __nv_bfloat162* g = reinterpret_cast<const __nv_bfloat162*>(&graw);
@@ -118,54 +96,129 @@ __device__ __forceinline__ uint4 silu_mul_vec8(const uint4& graw, const uint4& u
   return out;
 }
 
-template <int VPT>
-__global__ void __launch_bounds__(kMaxThreads) silu_mul_quant_kernel(
-    const __nv_bfloat16* __restrict__ gu, int64_t ld, int8_t* __restrict__ q,
-    float* __restrict__ scale, __nv_bfloat16* __restrict__ y_out, int I) {
+// Row source: the plain bf16 row (SILU = false) or SiLU*mul of the gate / up
+// halves of a gate_up row (SILU = true).
+template <bool SILU>
+struct RowSrc {
+  const uint4* a;
+  const uint4* b;
+  __device__ __forceinline__ RowSrc(const __nv_bfloat16* base, int64_t row, int64_t ld, int width) {
+    a = reinterpret_cast<const uint4*>(base + row * ld);
+    b = reinterpret_cast<const uint4*>(base + row * ld + width);
+  }
+  __device__ __forceinline__ uint4 load(int vi) const {
+    if constexpr (SILU) {
+      return silu_mul_vec8(__ldcs(a + vi), __ldcs(b + vi));
+    } else {
+      return __ldcs(a + vi);
+    }
+  }
+};
+
+// Register path: VPT vectors per thread held in registers.
+template <int VPT, bool SILU>
+__global__ void __launch_bounds__(kRegThreads) rows_reg_kernel(const __nv_bfloat16* __restrict__ in, int64_t ld,
+                                                               int8_t* __restrict__ q, float* __restrict__ scale,
+                                                               __nv_bfloat16* __restrict__ y_out, int width) {
   __shared__ float red[32];
   const int64_t row = blockIdx.x;
-  const int nvec = I >> 3;
-  const uint4* gr = reinterpret_cast<const uint4*>(gu + row * ld);
-  const uint4* ur = reinterpret_cast<const uint4*>(gu + row * ld + I);
+  const int nvec = width >> 3;
+  const RowSrc<SILU> src(in, row, ld, width);
   uint4 buf[VPT];
   float amax = 0.0f;
 #pragma unroll
   for (int i = 0; i < VPT; ++i) {
     const int vi = threadIdx.x + i * blockDim.x;
     if (vi < nvec) {
-      buf[i] = silu_mul_vec8(__ldcs(gr + vi), __ldcs(ur + vi));
+      buf[i] = src.load(vi);
       amax = fmaxf(amax, vec8_absmax(buf[i]));
     }
   }
   amax = block_max(amax, red);
   const float s = __fdiv_rn(amax, 127.0f);
-  uint2* qr = reinterpret_cast<uint2*>(q + row * static_cast<int64_t>(I));
-  uint4* yr = y_out ? reinterpret_cast<uint4*>(y_out + row * static_cast<int64_t>(I)) : nullptr;
+  uint2* qr = reinterpret_cast<uint2*>(q + row * static_cast<int64_t>(width));
+  uint4* yr = y_out ? reinterpret_cast<uint4*>(y_out + row * static_cast<int64_t>(width)) : nullptr;
 #pragma unroll
   for (int i = 0; i < VPT; ++i) {
     const int vi = threadIdx.x + i * blockDim.x;
     if (vi < nvec) {
       qr[vi] = quant_vec8(buf[i], s);
-      if (yr) yr[vi] = buf[i];
+      if (SILU && yr) yr[vi] = buf[i];
     }
   }
   if (threadIdx.x == 0) scale[row] = s;
 }
 
-// Vectors per thread and block size for a row of `nvec` 16-byte vectors:
-// the fewest vectors per thread that keep the CTA at <= 256 threads, else 8
-// vectors per thread with up to kMaxThreads threads.
-bool pick_row_shape(int nvec, int* vpt, int* threads) {
-  static const int kVpt[] = {1, 2, 4, 8};
-  for (int v : kVpt) {
-    const int need = (nvec + v - 1) / v;
-    if (need <= 256 || (v == 8 && need <= kMaxThreads)) {
-      *vpt = v;
-      *threads = need < 32 ? 32 : ((need + 31) / 32) * 32;
-      return true;
-    }
+// Shared-memory path: the row (or the SiLU*mul product) is staged on chip.
+template <bool SILU>
+__global__ void __launch_bounds__(kSmemThreads) rows_smem_kernel(const __nv_bfloat16* __restrict__ in, int64_t ld,
+                                                                 int8_t* __restrict__ q, float* __restrict__ scale,
+                                                                 __nv_bfloat16* __restrict__ y_out, int width) {
+  extern __shared__ uint4 stage[];
+  __shared__ float red[32];
+  const int64_t row = blockIdx.x;
+  const int nvec = width >> 3;
+  const RowSrc<SILU> src(in, row, ld, width);
+  float amax = 0.0f;
+  int vi = threadIdx.x;
+  // four independent loads in flight per thread
+  for (; vi + 3 * kSmemThreads < nvec; vi += 4 * kSmemThreads) {
+    uint4 v0 = src.load(vi), v1 = src.load(vi + kSmemThreads);
+    uint4 v2 = src.load(vi + 2 * kSmemThreads), v3 = src.load(vi + 3 * kSmemThreads);
+    stage[vi] = v0;
+    stage[vi + kSmemThreads] = v1;
+    stage[vi + 2 * kSmemThreads] = v2;
+    stage[vi + 3 * kSmemThreads] = v3;
+    amax = fmaxf(fmaxf(amax, vec8_absmax(v0)), fmaxf(vec8_absmax(v1), fmaxf(vec8_absmax(v2), vec8_absmax(v3))));
   }
-  return false;
+  for (; vi < nvec; vi += kSmemThreads) {
+    const uint4 v = src.load(vi);
+    stage[vi] = v;
+    amax = fmaxf(amax, vec8_absmax(v));
+  }
+  amax = block_max(amax, red);  // its __syncthreads also publishes `stage`
+  const float s = __fdiv_rn(amax, 127.0f);
+  uint2* qr = reinterpret_cast<uint2*>(q + row * static_cast<int64_t>(width));
+  uint4* yr = y_out ? reinterpret_cast<uint4*>(y_out + row * static_cast<int64_t>(width)) : nullptr;
+  for (int i = threadIdx.x; i < nvec; i += kSmemThreads) {
+    const uint4 v = stage[i];
+    qr[i] = quant_vec8(v, s);
+    if (SILU && yr) yr[i] = v;
+  }
+  if (threadIdx.x == 0) scale[row] = s;
+}
+
+template <bool SILU>
+int launch_rows(const __nv_bfloat16* in, int64_t ld, int8_t* q, float* scale, __nv_bfloat16* y, int64_t M,
+                int width, cudaStream_t s) {
+  const int nvec = width / 8;
+  const dim3 grid(static_cast<unsigned>(M));
+  if (nvec <= 4 * kRegThreads) {
+    const int vpt = nvec <= kRegThreads ? 1 : (nvec <= 2 * kRegThreads ? 2 : 4);
+    const int need = (nvec + vpt - 1) / vpt;
+    const int threads = need < 32 ? 32 : ((need + 31) / 32) * 32;
+    switch (vpt) {
+      case 1: rows_reg_kernel<1, SILU><<<grid, threads, 0, s>>>(in, ld, q, scale, y, width); break;
+      case 2: rows_reg_kernel<2, SILU><<<grid, threads, 0, s>>>(in, ld, q, scale, y, width); break;
+      default: rows_reg_kernel<4, SILU><<<grid, threads, 0, s>>>(in, ld, q, scale, y, width); break;
+    }
+  } else {
+    static std::mutex mu;
+    static bool configured[64] = {false};
+    const int dev = w8a8::current_device();
+    W8A8_REQUIRE(dev >= 0 && dev < 64, W8A8_ERR_CUDA, "no current device");
+    {
+      std::lock_guard<std::mutex> lk(mu);
+      if (!configured[dev]) {
+        W8A8_CUDA_TRY(cudaFuncSetAttribute(rows_smem_kernel<SILU>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           kMaxVec * 16));
+        configured[dev] = true;
+      }
+    }
+    rows_smem_kernel<SILU><<<grid, kSmemThreads, nvec * 16, s>>>(in, ld, q, scale, y, width);
+  }
+  W8A8_CUDA_TRY(cudaGetLastError());
+  return W8A8_OK;
 }
 
 }  // namespace
@@ -185,20 +238,10 @@ int w8a8_quant_per_token(const void* x, int64_t ldx, int8_t* q, float* scale, in
   W8A8_REQUIRE(M <= 0x7fffffff, W8A8_ERR_UNSUPPORTED, "quant_per_token: M=%lld too large", (long long)M);
   W8A8_REQUIRE(W8A8_ALIGNED16(x) && W8A8_ALIGNED16(q), W8A8_ERR_ALIGNMENT,
                "quant_per_token: x and q must be 16-byte aligned");
-  int vpt = 0, threads = 0;
-  W8A8_REQUIRE(pick_row_shape(static_cast<int>(K / 8), &vpt, &threads), W8A8_ERR_UNSUPPORTED,
-               "quant_per_token: K=%lld exceeds the 32768 limit", (long long)K);
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  const auto* xb = static_cast<const __nv_bfloat16*>(x);
-  const dim3 grid(static_cast<unsigned>(M));
-  switch (vpt) {
-    case 1: quant_rows_kernel<1><<<grid, threads, 0, s>>>(xb, ldx, q, scale, (int)K); break;
-    case 2: quant_rows_kernel<2><<<grid, threads, 0, s>>>(xb, ldx, q, scale, (int)K); break;
-    case 4: quant_rows_kernel<4><<<grid, threads, 0, s>>>(xb, ldx, q, scale, (int)K); break;
-    default: quant_rows_kernel<8><<<grid, threads, 0, s>>>(xb, ldx, q, scale, (int)K); break;
-  }
-  W8A8_CUDA_TRY(cudaGetLastError());
-  return W8A8_OK;
+  W8A8_REQUIRE(K / 8 <= kMaxVec, W8A8_ERR_UNSUPPORTED, "quant_per_token: K=%lld exceeds the 32768 limit",
+               (long long)K);
+  return launch_rows<false>(static_cast<const __nv_bfloat16*>(x), ldx, q, scale, nullptr, M, static_cast<int>(K),
+                            static_cast<cudaStream_t>(stream));
 }
 
 int w8a8_silu_mul_quant(const void* gate_up, int64_t ld, int8_t* q, float* scale, void* y_out,
@@ -213,21 +256,11 @@ int w8a8_silu_mul_quant(const void* gate_up, int64_t ld, int8_t* q, float* scale
   W8A8_REQUIRE(M <= 0x7fffffff, W8A8_ERR_UNSUPPORTED, "silu_mul_quant: M too large");
   W8A8_REQUIRE(W8A8_ALIGNED16(gate_up) && W8A8_ALIGNED16(q) && W8A8_ALIGNED16(y_out), W8A8_ERR_ALIGNMENT,
                "silu_mul_quant: gate_up, q and y_out must be 16-byte aligned");
-  int vpt = 0, threads = 0;
-  W8A8_REQUIRE(pick_row_shape(static_cast<int>(I / 8), &vpt, &threads), W8A8_ERR_UNSUPPORTED,
-               "silu_mul_quant: I=%lld exceeds the 32768 limit", (long long)I);
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  const auto* g = static_cast<const __nv_bfloat16*>(gate_up);
-  auto* y = static_cast<__nv_bfloat16*>(y_out);
-  const dim3 grid(static_cast<unsigned>(M));
-  switch (vpt) {
-    case 1: silu_mul_quant_kernel<1><<<grid, threads, 0, s>>>(g, ld, q, scale, y, (int)I); break;
-    case 2: silu_mul_quant_kernel<2><<<grid, threads, 0, s>>>(g, ld, q, scale, y, (int)I); break;
-    case 4: silu_mul_quant_kernel<4><<<grid, threads, 0, s>>>(g, ld, q, scale, y, (int)I); break;
-    default: silu_mul_quant_kernel<8><<<grid, threads, 0, s>>>(g, ld, q, scale, y, (int)I); break;
-  }
-  W8A8_CUDA_TRY(cudaGetLastError());
-  return W8A8_OK;
+  W8A8_REQUIRE(I / 8 <= kMaxVec, W8A8_ERR_UNSUPPORTED, "silu_mul_quant: I=%lld exceeds the 32768 limit",
+               (long long)I);
+  return launch_rows<true>(static_cast<const __nv_bfloat16*>(gate_up), ld, q, scale,
+                           static_cast<__nv_bfloat16*>(y_out), M, static_cast<int>(I),
+                           static_cast<cudaStream_t>(stream));
 }
 
 }  // extern "C"
