@@ -77,27 +77,30 @@ int w8a8_silu_mul_quant(const void* gate_up, int64_t ld, int8_t* q, float* scale
  * c_i32 (nullable) receives the exact int32 accumulator [M, N].
  * Replaces F.linear in _LinearTPImpl.forward (M/layers/linear.py:31-32).
  * Needs K % 16 == 0, N % 16 == 0, 16-byte aligned A, B, C.
- * `workspace` (zero-initialised once by the caller, left zeroed by every
- * successful call) serves split-K; w8a8_gemm_workspace_size() gives the bytes
- * a shape needs with the default heuristics (0 = none needed). */
+ * Schedule: stream-K over one persistent CTA per SM.  `workspace` holds the
+ * int32 partial tiles of tiles cut between two CTAs plus one counter per tile;
+ * the caller zero-initialises it once and every successful call leaves the
+ * counters zero again.  w8a8_gemm_workspace_size() gives the bytes a shape
+ * needs (0 = none); with less, ranges are rounded to whole tiles. */
 size_t w8a8_gemm_workspace_size(int64_t M, int64_t N, int64_t K);
 int w8a8_gemm(const int8_t* A, const int8_t* B, const float* sa, const float* sb,
               const void* bias, void* C, int32_t* c_i32, int64_t M, int64_t N, int64_t K,
               void* workspace, size_t workspace_bytes, void* stream);
 
-/* Same as w8a8_gemm with an explicit tile configuration (for tests and
- * tuning): variant 0 = auto, 1 = 128x256 tiles, 2 = 128x128 tiles,
- * 3..6 = weight-stationary (swap-AB) 128 x {16,32,64,128}; splits = 0 auto,
- * else the split-K factor. */
+/* Same as w8a8_gemm with an explicit configuration (for tests and tuning):
+ * variant 0 = auto, 1 = 128x256 tiles, 2 = 128x128 tiles, 3..6 =
+ * weight-stationary (swap-AB) 128 x {16,32,64,128}; ctas = 0 for one CTA per
+ * SM, else the number of persistent CTAs (at most one per SM). */
 int w8a8_gemm_config(const int8_t* A, const int8_t* B, const float* sa, const float* sb,
                      const void* bias, void* C, int32_t* c_i32, int64_t M, int64_t N,
-                     int64_t K, int variant, int splits, void* workspace,
+                     int64_t K, int variant, int ctas, void* workspace,
                      size_t workspace_bytes, void* stream);
 
-/* Host-only planner query (no GPU needed): the tile configuration w8a8_gemm
- * would use for a shape on a device with num_sms SMs.  out[8] receives
- * {variant, BN, swap, tiles, splits, k-blocks per split, CTAs, workspace bytes}. */
-int w8a8_gemm_plan(int64_t M, int64_t N, int64_t K, int variant, int splits, size_t workspace_bytes,
+/* Host-only planner query (no GPU needed): the configuration w8a8_gemm would
+ * use for a shape on a device with num_sms SMs.  out[8] receives
+ * {variant, BN, swap, tiles, CTAs, k-blocks per tile, partition granularity
+ * in k-blocks, workspace bytes}. */
+int w8a8_gemm_plan(int64_t M, int64_t N, int64_t K, int variant, int ctas, size_t workspace_bytes,
                    int num_sms, int64_t* out);
 
 /* ---------------------------------------------------------------- kernel 3

@@ -88,6 +88,8 @@ __device__ __forceinline__ bool cta_barrier(const CommView& v, int phase, int sl
 // x: nvec 16-byte vectors (8 bf16 each), in place.
 __global__ void __launch_bounds__(kArThreads) allreduce_kernel(CommView v, uint4* x, long long nvec,
                                                                int two_shot) {
+  dev::griddep_wait();  // x and the epoch word come from earlier kernels
+  dev::griddep_launch();
   const uint32_t epoch = dev::ld_relaxed_gpu(dev::ctrl_ptr(v.base[v.rank])) + 1u;
   uint4* mine = reinterpret_cast<uint4*>(dev::half_ptr(v, v.rank, epoch));
   const int slot = blockIdx.x;
@@ -286,9 +288,8 @@ int w8a8_all_reduce(w8a8_comm* c, void* x, int64_t numel, void* stream) {
   if (nsm <= 0) nsm = 148;
   long long grid = (per_chunk + kArThreads * 2 - 1) / (kArThreads * 2);
   grid = grid < 1 ? 1 : (grid > 2 * nsm ? 2 * nsm : grid);
-  allreduce_kernel<<<static_cast<unsigned>(grid), kArThreads, 0, static_cast<cudaStream_t>(stream)>>>(
-      v, static_cast<uint4*>(x), nvec, one ? 0 : 1);
-  W8A8_CUDA_TRY(cudaGetLastError());
+  W8A8_CUDA_TRY(launch_pdl(allreduce_kernel, dim3(static_cast<unsigned>(grid)), dim3(kArThreads), 0,
+                           static_cast<cudaStream_t>(stream), v, static_cast<uint4*>(x), nvec, one ? 0 : 1));
   return W8A8_OK;
 }
 

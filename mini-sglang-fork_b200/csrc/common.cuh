@@ -51,3 +51,25 @@ constexpr long long kDefaultGemmTimeoutNs = 4000000000LL;  // 4 s
 
 // 16-byte alignment test of a device pointer.
 #define W8A8_ALIGNED16(p) ((reinterpret_cast<uintptr_t>(p) & 15u) == 0)
+
+namespace w8a8 {
+
+// Launch with programmatic stream serialisation (PDL): the kernel may begin
+// its prologue while the previous kernel of the stream drains; it must call
+// dev::griddep_wait() before touching that kernel's inputs or outputs.
+template <typename Kernel, typename... Args>
+cudaError_t launch_pdl(Kernel kernel, dim3 grid, dim3 block, size_t smem, cudaStream_t stream, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+
+}  // namespace w8a8

@@ -66,8 +66,7 @@ int launch_variant(const GemmPlan& p, const CUtensorMap& tw, const CUtensorMap& 
       configured[dev] = true;
     }
   }
-  kern<<<p.grid, T::kThreads, T::kSmemBytes, stream>>>(tw, tn, args, cv);
-  W8A8_CUDA_TRY(cudaGetLastError());
+  W8A8_CUDA_TRY(launch_pdl(kern, dim3(p.grid), dim3(T::kThreads), T::kSmemBytes, stream, tw, tn, args, cv));
   return W8A8_OK;
 }
 
@@ -103,7 +102,7 @@ int dispatch_variant(const GemmPlan& p, const CUtensorMap& tw, const CUtensorMap
 }
 
 int run_gemm(const int8_t* A, const int8_t* B, const float* sa, const float* sb, const void* bias, void* C,
-             int32_t* c_i32, int64_t M, int64_t N, int64_t K, int variant, int splits, void* workspace,
+             int32_t* c_i32, int64_t M, int64_t N, int64_t K, int variant, int ctas, void* workspace,
              size_t workspace_bytes, cudaStream_t stream, long long timeout_ns, const CommView* comm) {
   W8A8_REQUIRE(M >= 0 && N >= 0 && K >= 0, W8A8_ERR_INVALID_ARG, "gemm: negative shape");
   if (M == 0) return W8A8_OK;  // empty batch: nothing to compute (its tensors may be null)
@@ -114,8 +113,8 @@ int run_gemm(const int8_t* A, const int8_t* B, const float* sa, const float* sb,
                device_cc_major());
   W8A8_REQUIRE(W8A8_ALIGNED16(c_i32), W8A8_ERR_ALIGNMENT, "gemm: c_i32 must be 16-byte aligned");
   GemmPlan p;
-  rc = plan_gemm(M, N, K, variant, splits, workspace_bytes, sm_count(), &p);
-  W8A8_REQUIRE(rc == 0, W8A8_ERR_WORKSPACE, "gemm: %s", plan_error(rc));
+  rc = plan_gemm(M, N, K, variant, ctas, workspace_bytes, sm_count(), &p);
+  W8A8_REQUIRE(rc == 0, W8A8_ERR_INVALID_ARG, "gemm: %s", plan_error(rc));
   if (comm) {
     W8A8_REQUIRE(p.num_tiles <= kMaxSlots, W8A8_ERR_UNSUPPORTED,
                  "gemm_allreduce: %d output tiles exceed the %d flag slots", p.num_tiles, kMaxSlots);
@@ -124,9 +123,9 @@ int run_gemm(const int8_t* A, const int8_t* B, const float* sa, const float* sb,
                  (long long)M, (long long)N, comm->half_bytes);
     W8A8_REQUIRE(c_i32 == nullptr, W8A8_ERR_INVALID_ARG, "gemm_allreduce: no int32 output in fused mode");
   }
-  if (p.splits > 1) {
+  if (p.cut_tiles) {
     W8A8_REQUIRE(workspace != nullptr && workspace_bytes >= p.ws_bytes, W8A8_ERR_WORKSPACE,
-                 "gemm: split-K needs a zeroed workspace of %zu bytes", p.ws_bytes);
+                 "gemm: stream-K needs a workspace of %zu bytes with zeroed counters", p.ws_bytes);
     W8A8_REQUIRE((reinterpret_cast<uintptr_t>(workspace) & 255u) == 0, W8A8_ERR_ALIGNMENT,
                  "gemm: workspace must be 256-byte aligned");
   }
@@ -150,8 +149,8 @@ int run_gemm(const int8_t* A, const int8_t* B, const float* sa, const float* sb,
   args.bias = static_cast<const __nv_bfloat16*>(bias);
   args.C = static_cast<__nv_bfloat16*>(C);
   args.c_i32 = c_i32;
-  args.counters = p.splits > 1 ? static_cast<uint32_t*>(workspace) : nullptr;
-  args.ws = p.splits > 1 ? reinterpret_cast<int32_t*>(static_cast<char*>(workspace) + p.ws_counter_bytes)
+  args.counters = p.cut_tiles ? static_cast<uint32_t*>(workspace) : nullptr;
+  args.ws = p.cut_tiles ? reinterpret_cast<int32_t*>(static_cast<char*>(workspace) + p.ws_counter_bytes)
                          : nullptr;
   args.err = err;
   args.timeout_ns = timeout_ns;
@@ -162,8 +161,8 @@ int run_gemm(const int8_t* A, const int8_t* B, const float* sa, const float* sb,
   args.tiles_w = p.tiles_w;
   args.tiles_n = p.tiles_n;
   args.num_tiles = p.num_tiles;
-  args.splits = p.splits;
-  args.kb_per_split = p.kb_per_split;
+  args.dp_tiles = p.dp_tiles;
+  args.gran = p.gran;
   args.kblocks = p.kblocks;
   args.units = p.units;
   args.wide_fast = p.wide_fast;
@@ -184,23 +183,23 @@ size_t w8a8_gemm_workspace_size(int64_t M, int64_t N, int64_t K) {
   int nsm = w8a8::sm_count();
   if (nsm <= 0) nsm = 148;
   if (w8a8::plan_gemm(M, N, K, 0, 0, static_cast<size_t>(-1), nsm, &p) != 0) return 0;
-  return p.splits > 1 ? p.ws_bytes : 0;
+  return p.ws_bytes;
 }
 
-int w8a8_gemm_plan(int64_t M, int64_t N, int64_t K, int variant, int splits, size_t workspace_bytes,
+int w8a8_gemm_plan(int64_t M, int64_t N, int64_t K, int variant, int ctas, size_t workspace_bytes,
                    int num_sms, int64_t* out) {
   W8A8_REQUIRE(out != nullptr, W8A8_ERR_INVALID_ARG, "gemm_plan: out is null");
   w8a8::GemmPlan p;
-  const int rc = w8a8::plan_gemm(M, N, K, variant, splits, workspace_bytes, num_sms, &p);
-  W8A8_REQUIRE(rc == 0, rc == 2 ? W8A8_ERR_WORKSPACE : W8A8_ERR_INVALID_ARG, "gemm_plan: %s",
+  const int rc = w8a8::plan_gemm(M, N, K, variant, ctas, workspace_bytes, num_sms, &p);
+  W8A8_REQUIRE(rc == 0, W8A8_ERR_INVALID_ARG, "gemm_plan: %s",
                w8a8::plan_error(rc));
   out[0] = p.variant;
   out[1] = p.bn;
   out[2] = p.swap ? 1 : 0;
   out[3] = p.num_tiles;
-  out[4] = p.splits;
-  out[5] = p.kb_per_split;
-  out[6] = p.grid;
+  out[4] = p.grid;
+  out[5] = p.kblocks;
+  out[6] = p.gran;
   out[7] = static_cast<int64_t>(p.ws_bytes);
   return W8A8_OK;
 }
@@ -213,12 +212,12 @@ int w8a8_gemm(const int8_t* A, const int8_t* B, const float* sa, const float* sb
 }
 
 int w8a8_gemm_config(const int8_t* A, const int8_t* B, const float* sa, const float* sb, const void* bias,
-                     void* C, int32_t* c_i32, int64_t M, int64_t N, int64_t K, int variant, int splits,
+                     void* C, int32_t* c_i32, int64_t M, int64_t N, int64_t K, int variant, int ctas,
                      void* workspace, size_t workspace_bytes, void* stream) {
   W8A8_REQUIRE(variant >= 0 && variant <= 6, W8A8_ERR_INVALID_ARG, "gemm_config: variant %d out of range",
                variant);
-  W8A8_REQUIRE(splits >= 0, W8A8_ERR_INVALID_ARG, "gemm_config: negative splits");
-  return w8a8::run_gemm(A, B, sa, sb, bias, C, c_i32, M, N, K, variant, splits, workspace, workspace_bytes,
+  W8A8_REQUIRE(ctas >= 0, W8A8_ERR_INVALID_ARG, "gemm_config: negative ctas");
+  return w8a8::run_gemm(A, B, sa, sb, bias, C, c_i32, M, N, K, variant, ctas, workspace, workspace_bytes,
                         static_cast<cudaStream_t>(stream), w8a8::kDefaultGemmTimeoutNs, nullptr);
 }
 

@@ -14,7 +14,7 @@ namespace w8a8 {
 // comm == nullptr: plain GEMM into C.  comm != nullptr: every rank's partial
 // goes through the communicator's buffers and C receives the all-reduced sum.
 int run_gemm(const int8_t* A, const int8_t* B, const float* sa, const float* sb, const void* bias, void* C,
-             int32_t* c_i32, int64_t M, int64_t N, int64_t K, int variant, int splits, void* workspace,
+             int32_t* c_i32, int64_t M, int64_t N, int64_t K, int variant, int ctas, void* workspace,
              size_t workspace_bytes, cudaStream_t stream, long long timeout_ns, const CommView* comm);
 
 }  // namespace w8a8

@@ -4,8 +4,11 @@
 // Variants (BM = 128 rows of the "wide" operand per tile, BK = 128):
 //   1: normal, BN = 256   2: normal, BN = 128
 //   3..6: weight-stationary (swap), BN = 16 / 32 / 64 / 128 token columns
-// Split-K factor: the smallest-penalty factor maximising the share of busy
-// CTAs in the last round of the persistent schedule.
+// Schedule: stream-K over G persistent CTAs (one per SM by default).  The
+// k-block iterations of all tiles are split evenly between the CTAs; tiles cut
+// by a CTA boundary are finished through the workspace (two int32 tile slots
+// per CTA plus one counter per tile).  Without room for that workspace the
+// ranges are rounded to whole tiles (no cut tiles, no workspace).
 #pragma once
 
 #include <cstddef>
@@ -18,11 +21,15 @@ struct GemmPlan {
   int bn;
   bool swap;
   int tiles_w, tiles_n, num_tiles;
-  int kblocks, splits, kb_per_split;
-  int units, grid;
+  int kblocks;
+  int dp_tiles;             // leading whole tiles in grid-stride order
+  int gran;                 // stream-K granularity in k blocks: 1 or kblocks
+  long long units;          // (num_tiles - dp_tiles) * kblocks / gran
+  int grid;                 // persistent CTAs
   int wide_fast;
+  bool cut_tiles;           // some tile is shared by two or more CTAs
   size_t ws_counter_bytes;  // tile counters at the workspace head
-  size_t ws_bytes;          // total workspace bytes needed (0 if splits == 1)
+  size_t ws_bytes;          // total workspace bytes needed (0 if no tile is cut)
 };
 
 inline int variant_bn(int v) {
@@ -35,17 +42,23 @@ inline bool variant_swap(int v) { return v >= 3; }
 inline const char* plan_error(int rc) {
   switch (rc) {
     case 1: return "invalid shape or variant";
-    case 2: return "split-K workspace too small for the requested split factor";
     default: return "unknown planning error";
   }
 }
 
 inline size_t round_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
-// Returns 0 and fills *p; nonzero on invalid input.
-inline int plan_gemm(int64_t M, int64_t N, int64_t K, int variant, int splits_req, size_t ws_avail, int nsm,
+// The workspace starts with a counter region of fixed size, whatever the
+// shape, so counters left at zero by one call are never overlapped by another
+// call's partial tiles.
+constexpr int kMaxCounterTiles = 65536;
+constexpr size_t kCounterBytes = static_cast<size_t>(kMaxCounterTiles) * 4;
+
+// Returns 0 and fills *p; nonzero on invalid input.  ctas_req = 0 picks one
+// CTA per SM.
+inline int plan_gemm(int64_t M, int64_t N, int64_t K, int variant, int ctas_req, size_t ws_avail, int nsm,
                      GemmPlan* p) {
-  if (M <= 0 || N <= 0 || K <= 0 || nsm <= 0) return 1;
+  if (M <= 0 || N <= 0 || K <= 0 || nsm <= 0 || ctas_req < 0) return 1;
   int v = variant;
   if (v == 0) {
     if (M <= 16) {
@@ -69,41 +82,35 @@ inline int plan_gemm(int64_t M, int64_t N, int64_t K, int variant, int splits_re
   p->tiles_n = static_cast<int>((rows_n + p->bn - 1) / p->bn);
   p->num_tiles = p->tiles_w * p->tiles_n;
   p->kblocks = static_cast<int>((K + 127) / 128);
+  const long long total_iters = static_cast<long long>(p->num_tiles) * p->kblocks;
+  long long g = ctas_req > 0 ? (ctas_req < nsm ? ctas_req : nsm) : nsm;
+  if (g > total_iters) g = total_iters;
+  // whole tiles for every CTA first, stream-K over the remainder
+  p->dp_tiles = static_cast<int>((p->num_tiles / g) * g);
+  const long long iters = static_cast<long long>(p->num_tiles - p->dp_tiles) * p->kblocks;
 
-  auto ws_need = [&](int s) -> size_t {
-    if (s <= 1) return 0;
-    const size_t counters = round_up(static_cast<size_t>(p->num_tiles) * 4, 256);
-    return counters + static_cast<size_t>(p->num_tiles) * 128 * p->bn * 4;
-  };
-
-  int s = 1;
-  if (splits_req > 0) {
-    s = splits_req < p->kblocks ? splits_req : p->kblocks;
-    if (s > 1 && ws_need(s) > ws_avail) return 2;
-  } else {
-    // Each split keeps >= 4 K blocks (512 bytes of K) so the pipeline fills.
-    const int smax = p->kblocks / 4 < 16 ? p->kblocks / 4 : 16;
-    double best = -1.0;
-    for (int c = 1; c <= (smax > 1 ? smax : 1); ++c) {
-      if (c > 1 && ws_need(c) > ws_avail) break;
-      const int64_t units = static_cast<int64_t>(p->num_tiles) * c;
-      const int64_t rounds = (units + nsm - 1) / nsm;
-      const double eff = static_cast<double>(units) / static_cast<double>(rounds * nsm);
-      const double score = eff - 0.01 * (c - 1);
-      if (score > best + 1e-9) {
-        best = score;
-        s = c;
-      }
+  // Does an even split of the remaining iterations cut any tile?
+  bool cut = false;
+  for (long long c = 1; c < g && iters > 0 && !cut; ++c) cut = ((c * iters / g) % p->kblocks) != 0;
+  const size_t need = kCounterBytes + 2 * static_cast<size_t>(g) * 128 * p->bn * 4;
+  if (cut && (need > ws_avail || p->num_tiles > kMaxCounterTiles)) {
+    // no room to finish cut tiles: whole-tile ranges
+    p->gran = p->kblocks;
+    if (g > p->num_tiles) {
+      g = p->num_tiles;
+      p->dp_tiles = p->num_tiles;
     }
+    cut = false;
+  } else {
+    p->gran = 1;
   }
-  p->kb_per_split = (p->kblocks + s - 1) / s;
-  p->splits = (p->kblocks + p->kb_per_split - 1) / p->kb_per_split;
-  p->units = p->num_tiles * p->splits;
-  p->grid = p->units < nsm ? p->units : nsm;
+  p->grid = static_cast<int>(g);
+  p->units = (static_cast<long long>(p->num_tiles - p->dp_tiles) * p->kblocks) / p->gran;
+  p->cut_tiles = cut;
+  p->ws_counter_bytes = cut ? kCounterBytes : 0;
+  p->ws_bytes = cut ? need : 0;
   // Keep the smaller operand L2-resident: walk it fastest.
   p->wide_fast = (rows_w <= rows_n) ? 1 : 0;
-  p->ws_counter_bytes = p->splits > 1 ? round_up(static_cast<size_t>(p->num_tiles) * 4, 256) : 0;
-  p->ws_bytes = ws_need(p->splits);
   return 0;
 }
 

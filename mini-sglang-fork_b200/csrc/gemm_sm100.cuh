@@ -27,22 +27,27 @@
 // handful of tokens; the math is unchanged (C^T = B . A^T) and the epilogue
 // writes C[m, n] with n along the 32 lanes of a warp.
 //
-// Split-K (few output tiles, e.g. decode): the K blocks of a tile are cut into
-// `splits` ranges handled by different CTAs.  Each adds its int32 partial tile
-// into a workspace with red.global.add (exact and order-independent), then the
-// last CTA to arrive on the tile's counter dequantises the sum, writes the
-// tile and zeroes the workspace tile and counter again, so the workspace stays
-// zeroed between calls.
+// Schedule (hybrid data-parallel + stream-K).  With T tiles and G CTAs, the
+// first G*floor(T/G) tiles are dealt whole in grid-stride order; the k-block
+// iterations of the last T mod G tiles are laid end to end and CTA c takes the
+// contiguous range [c*L/G, (c+1)*L/G) of them (rounded to whole tiles in
+// tile-granular mode), so every CTA streams the same number of k blocks
+// whatever the tile count.  A range cut inside a tile leaves a partial
+// fragment: its int32 accumulator goes to a per-CTA workspace slot with plain
+// coalesced stores, the fragment's arrival is counted on the tile's counter,
+// and the last arriving fragment adds the other slots (int32, exact in any
+// order), dequantises, writes the tile and resets the counter, so the counters
+// stay zero between calls.
 //
 // Fused all-reduce (row-parallel layers, FUSED = true).  The epilogue writes
 // each finished bf16 partial tile into this rank's IPC-shared buffer (same
 // [M, N] layout as C) and raises the tile's "ready" flag on every rank.  After
-// its GEMM units, CTA b reduces the tiles t with t % grid == b in two shots:
-// it waits for every rank's ready(t), sums its 1/world share of the tile from
-// all ranks in rank order (fp32, one rounding), writes it back in place and
-// raises reduced(t) everywhere; then it waits for every rank's reduced(t) and
-// gathers the shares into C.  Waits happen only after all of the CTA's own
-// signals, so no wait can block a signal another rank needs.
+// its GEMM work, CTA b reduces the tiles t with t % G == b in two shots: it
+// waits for every rank's ready(t), sums its 1/world share of the tile from all
+// ranks in rank order (fp32, one rounding), writes it back in place and raises
+// reduced(t) everywhere; then it waits for every rank's reduced(t) and gathers
+// the shares into C.  Waits happen only after all of the CTA's own signals, so
+// no wait can block a signal another rank needs.
 //
 // Every mbarrier / flag wait is bounded (%globaltimer); on expiry the CTA
 // raises a shared abort flag and the device error word, drains its in-flight
@@ -65,15 +70,17 @@ struct GemmArgs {
   const __nv_bfloat16* bias;  // [N] or null
   __nv_bfloat16* C;           // [M, N] bf16 output (row stride ldc)
   int32_t* c_i32;             // [M, N] int32 accumulator output or null
-  int32_t* ws;                // split-K workspace (zeroed)
-  uint32_t* counters;         // split-K tile arrival counters (zeroed)
+  int32_t* ws;                // stream-K partial slots, 2 per CTA
+  uint32_t* counters;         // per-tile fragment arrival counters (zeroed)
   unsigned int* err;          // device error word
   long long timeout_ns;
   int M, N, K;
   int ldc;
   int tiles_w, tiles_n;       // tiles along the 128-row side / the BN side
-  int num_tiles, splits, kb_per_split, kblocks;
-  int units;                  // num_tiles * splits
+  int num_tiles, kblocks;
+  int dp_tiles;               // leading tiles done whole, in grid-stride order
+  int gran;                   // stream-K granularity in k blocks (1, or kblocks = whole tiles)
+  long long units;            // (num_tiles - dp_tiles) * kblocks / gran
   int wide_fast;              // raster: 1 = consecutive tiles walk the 128-row side
 };
 
@@ -108,14 +115,48 @@ __device__ __forceinline__ void tile_coords(const GemmArgs& a, int tile, int& tw
   }
 }
 
-__device__ __forceinline__ void unit_coords(const GemmArgs& a, int unit, int& tw, int& tn, int& kb0,
-                                            int& kb1, int& tile) {
-  tile = unit / a.splits;
-  const int split = unit - tile * a.splits;
-  tile_coords(a, tile, tw, tn);
-  kb0 = split * a.kb_per_split;
-  kb1 = min(a.kblocks, kb0 + a.kb_per_split);
+// Hybrid schedule: tiles [0, dp_tiles) are whole-tile work dealt out in
+// grid-stride order (CTA c takes c, c+G, ...), which keeps the tiles in flight
+// together adjacent for L2 reuse; the k-block iterations of the remaining
+// tiles are split evenly (stream-K).  sk_begin(c) is the first stream-K
+// iteration of CTA c (global iteration index).
+__device__ __forceinline__ long long sk_begin(const GemmArgs& a, int c) {
+  return static_cast<long long>(a.dp_tiles) * a.kblocks +
+         (static_cast<long long>(c) * a.units / gridDim.x) * a.gran;
 }
+
+// The CTA whose stream-K range holds iteration x: max{c : sk_begin(c) <= x}.
+__device__ __forceinline__ int sk_owner(const GemmArgs& a, long long x) {
+  const long long rel = x - static_cast<long long>(a.dp_tiles) * a.kblocks;
+  return static_cast<int>(((rel / a.gran + 1) * gridDim.x - 1) / a.units);
+}
+
+// Iterates the fragments (tile, [kb0, kb1)) of this CTA: its whole tiles of
+// the data-parallel part, then its stream-K range.
+struct FragmentWalk {
+  int dp_tile, dp_tiles;
+  long long it, end;
+  int kblocks;
+  __device__ __forceinline__ FragmentWalk(const GemmArgs& a)
+      : dp_tile(blockIdx.x), dp_tiles(a.dp_tiles), it(sk_begin(a, blockIdx.x)),
+        end(sk_begin(a, blockIdx.x + 1)), kblocks(a.kblocks) {}
+  __device__ __forceinline__ bool next(int& tile, int& kb0, int& kb1) {
+    if (dp_tile < dp_tiles) {
+      tile = dp_tile;
+      kb0 = 0;
+      kb1 = kblocks;
+      dp_tile += gridDim.x;
+      return true;
+    }
+    if (it >= end) return false;
+    tile = static_cast<int>(it / kblocks);
+    kb0 = static_cast<int>(it - static_cast<long long>(tile) * kblocks);
+    const long long left = end - it;
+    kb1 = left < kblocks - kb0 ? kb0 + static_cast<int>(left) : kblocks;
+    it += kb1 - kb0;
+    return true;
+  }
+};
 
 __device__ __forceinline__ float dequant1(int32_t acc, float sa, float sb) {
   return __fmul_rn(__fmul_rn(__int2float_rn(acc), sa), sb);
@@ -263,15 +304,6 @@ __global__ void __launch_bounds__(192, 1)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
 
-  // Fused mode: the call's epoch (published by the previous call's last CTA)
-  // selects the data half; partial tiles go there instead of C.
-  uint32_t epoch = 0;
-  __nv_bfloat16* out = args.C;
-  if constexpr (FUSED) {
-    epoch = dev::ld_relaxed_gpu(dev::ctrl_ptr(cv.base[cv.rank])) + 1u;
-    out = reinterpret_cast<__nv_bfloat16*>(dev::half_ptr(cv, cv.rank, epoch));
-  }
-
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       dev::mbar_init(dev::smem_u32(full + s), 1);
@@ -299,6 +331,15 @@ __global__ void __launch_bounds__(192, 1)
   dev::tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   const long long tmo = args.timeout_ns;
+  // This grid is resident (one CTA per SM): the next kernel may start its
+  // prologue now; it waits for our completion before touching our data.
+  dev::griddep_launch();
+
+  // Fused mode: the call's epoch (published by the previous call's last CTA,
+  // so read after griddep_wait) selects the data half; partial tiles go there
+  // instead of C.
+  uint32_t epoch = 0;
+  __nv_bfloat16* out = args.C;
 
   if (warp == 0) {
     if (lane == 0) {
@@ -308,29 +349,61 @@ __global__ void __launch_bounds__(192, 1)
       // both operands across tiles and keeps the default policy.
       const uint64_t pol_w = dev::policy_evict_first();
       const uint64_t pol_n = dev::policy_evict_last();
+      // The weight operand never depends on the previous kernel: the weight
+      // half of the first stages is requested before griddep_wait.
+      auto load_weights = [&](int stg, int kb, int tw, int tn) {
+        const uint32_t fb = dev::smem_u32(full + stg);
+        if constexpr (SWAP) {
+          dev::tma_load_2d_hint(dev::smem_u32(s_w + stg * T::kTileWBytes), &tm_w, fb, kb * T::kBK, tw * T::kBM,
+                                pol_w);
+        } else {
+          dev::tma_load_2d(dev::smem_u32(s_n + stg * T::kTileNBytes), &tm_n, fb, kb * T::kBK, tn * BN);
+        }
+      };
+      auto load_tokens = [&](int stg, int kb, int tw, int tn) {
+        const uint32_t fb = dev::smem_u32(full + stg);
+        if constexpr (SWAP) {
+          dev::tma_load_2d_hint(dev::smem_u32(s_n + stg * T::kTileNBytes), &tm_n, fb, kb * T::kBK, tn * BN,
+                                pol_n);
+        } else {
+          dev::tma_load_2d(dev::smem_u32(s_w + stg * T::kTileWBytes), &tm_w, fb, kb * T::kBK, tw * T::kBM);
+        }
+      };
       int stage = 0;
       uint32_t phase = 0;
       uint32_t issued_mask = 0, issued_phase = 0;
       bool ok = true;
-      for (int unit = blockIdx.x; unit < args.units && ok; unit += gridDim.x) {
-        int tw, tn, kb0, kb1, tile;
-        unit_coords(args, unit, tw, tn, kb0, kb1, tile);
+      FragmentWalk walk(args);
+      int tile, kb0, kb1;
+      bool have = walk.next(tile, kb0, kb1);
+      int pre = 0;
+      if (have) {
+        int tw, tn;
+        tile_coords(args, tile, tw, tn);
+        pre = min(STAGES, kb1 - kb0);
+        for (int i = 0; i < pre; ++i) {
+          dev::mbar_expect_tx(dev::smem_u32(full + i), T::kStageBytes);
+          load_weights(i, kb0 + i, tw, tn);
+        }
+      }
+      dev::griddep_wait();
+      for (; ok && have; have = walk.next(tile, kb0, kb1)) {
+        int tw, tn;
+        tile_coords(args, tile, tw, tn);
         for (int kb = kb0; kb < kb1; ++kb) {
-          if (!dev::mbar_wait(dev::smem_u32(empty + stage), phase ^ 1u, abort_flag, args.err,
-                              kErrGemmWait, tmo)) {
-            ok = false;
-            break;
-          }
-          const uint32_t fb = dev::smem_u32(full + stage);
-          dev::mbar_expect_tx(fb, T::kStageBytes);
-          if constexpr (SWAP) {
-            dev::tma_load_2d_hint(dev::smem_u32(s_w + stage * T::kTileWBytes), &tm_w, fb, kb * T::kBK,
-                                  tw * T::kBM, pol_w);
-            dev::tma_load_2d_hint(dev::smem_u32(s_n + stage * T::kTileNBytes), &tm_n, fb, kb * T::kBK,
-                                  tn * BN, pol_n);
+          if (pre > 0) {
+            // stage already armed with its weight half before griddep_wait
+            --pre;
+            load_tokens(stage, kb, tw, tn);
           } else {
-            dev::tma_load_2d(dev::smem_u32(s_w + stage * T::kTileWBytes), &tm_w, fb, kb * T::kBK, tw * T::kBM);
-            dev::tma_load_2d(dev::smem_u32(s_n + stage * T::kTileNBytes), &tm_n, fb, kb * T::kBK, tn * BN);
+            if (!dev::mbar_wait(dev::smem_u32(empty + stage), phase ^ 1u, abort_flag, args.err,
+                                kErrGemmWait, tmo)) {
+              ok = false;
+              break;
+            }
+            dev::mbar_expect_tx(dev::smem_u32(full + stage), T::kStageBytes);
+            load_weights(stage, kb, tw, tn);
+            load_tokens(stage, kb, tw, tn);
           }
           issued_mask |= 1u << stage;
           issued_phase = (issued_phase & ~(1u << stage)) | (phase << stage);
@@ -352,14 +425,15 @@ __global__ void __launch_bounds__(192, 1)
   } else if (warp == 1) {
     if (lane == 0) {
       // ------------------------------------------------------- MMA issuer
+      dev::griddep_wait();
       int stage = 0;
       uint32_t phase = 0;
       int acc = 0;
       uint32_t acc_phase = 0;
       bool ok = true;
-      for (int unit = blockIdx.x; unit < args.units && ok; unit += gridDim.x) {
-        int tw, tn, kb0, kb1, tile;
-        unit_coords(args, unit, tw, tn, kb0, kb1, tile);
+      FragmentWalk walk(args);
+      int tile, kb0, kb1;
+      while (ok && walk.next(tile, kb0, kb1)) {
         if (!dev::mbar_wait(dev::smem_u32(acc_empty + acc), acc_phase ^ 1u, abort_flag, args.err,
                             kErrGemmWait, tmo)) {
           break;
@@ -401,16 +475,24 @@ __global__ void __launch_bounds__(192, 1)
     }
   } else {
     // ------------------------------------------------------------ epilogue
+    dev::griddep_wait();
+    if constexpr (FUSED) {
+      epoch = dev::ld_relaxed_gpu(dev::ctrl_ptr(cv.base[cv.rank])) + 1u;
+      out = reinterpret_cast<__nv_bfloat16*>(dev::half_ptr(cv, cv.rank, epoch));
+    }
     const int quarter = warp & 3;
     const int row_in_tile = quarter * 32 + lane;
     const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
     const int et = threadIdx.x - 64;  // 0..127 among the epilogue threads
+    const long long my_begin = sk_begin(args, blockIdx.x);
     int acc = 0;
     uint32_t acc_phase = 0;
     bool aborted = false;
-    for (int unit = blockIdx.x; unit < args.units; unit += gridDim.x) {
-      int tw, tn, kb0, kb1, tile;
-      unit_coords(args, unit, tw, tn, kb0, kb1, tile);
+    FragmentWalk walk(args);
+    int tile, kb0, kb1;
+    while (walk.next(tile, kb0, kb1)) {
+      int tw, tn;
+      tile_coords(args, tile, tw, tn);
       const bool ok = dev::mbar_wait(dev::smem_u32(acc_full + acc), acc_phase, abort_flag, args.err,
                                      kErrGemmWait, tmo);
       if (dev::named_bar_or(1, 128, !ok)) {  // uniform exit of all epilogue threads
@@ -421,7 +503,8 @@ __global__ void __launch_bounds__(192, 1)
       const uint32_t t_acc = tmem_base + lane_base + static_cast<uint32_t>(acc * T::kAccCols);
       const int row = tw * T::kBM + row_in_tile;
       bool wrote_tile = true;
-      if (args.splits == 1) {
+      if (kb0 == 0 && kb1 == args.kblocks) {
+        // whole tile in this CTA: dequantise straight from TMEM
 #pragma unroll 1
         for (int c = 0; c < T::kChunks; ++c) {
           uint32_t v[32];
@@ -434,7 +517,10 @@ __global__ void __launch_bounds__(192, 1)
           store_chunk<SWAP, T::kChunk>(args, out, row, tn * BN + c * T::kChunk, v);
         }
       } else {
-        int32_t* wtile = args.ws + static_cast<int64_t>(tile) * (T::kBM * BN);
+        // partial fragment: park the int32 tile in this CTA's slot
+        const long long tile_begin = static_cast<long long>(tile) * args.kblocks;
+        const int slot = 2 * blockIdx.x + (my_begin < tile_begin ? 1 : 0);
+        int32_t* wslot = args.ws + static_cast<int64_t>(slot) * (T::kBM * BN);
 #pragma unroll 1
         for (int c = 0; c < T::kChunks; ++c) {
           uint32_t v[32];
@@ -446,13 +532,15 @@ __global__ void __launch_bounds__(192, 1)
           }
 #pragma unroll
           for (int j = 0; j < T::kChunk; ++j)
-            atomicAdd(wtile + (c * T::kChunk + j) * T::kBM + row_in_tile, static_cast<int32_t>(v[j]));
+            __stcg(wslot + (c * T::kChunk + j) * T::kBM + row_in_tile, static_cast<int32_t>(v[j]));
         }
         __threadfence();
         dev::named_bar_sync(1, 128);
+        const int c_first = sk_owner(args, tile_begin);
+        const int c_last = sk_owner(args, tile_begin + args.kblocks - 1);
         if (et == 0) {
           const uint32_t prev = atomicAdd(args.counters + tile, 1u);
-          *last_flag = (prev == static_cast<uint32_t>(args.splits - 1)) ? 1 : 0;
+          *last_flag = (prev == static_cast<uint32_t>(c_last - c_first)) ? 1 : 0;
         }
         dev::named_bar_sync(1, 128);
         wrote_tile = *last_flag != 0;
@@ -462,20 +550,20 @@ __global__ void __launch_bounds__(192, 1)
           for (int c = 0; c < T::kChunks; ++c) {
             uint32_t v[32];
 #pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              if (j < T::kChunk) {
-                int32_t* p = wtile + (c * T::kChunk + j) * T::kBM + row_in_tile;
-                v[j] = static_cast<uint32_t>(__ldcg(p));
-                __stcg(p, 0);
-              } else {
-                v[j] = 0u;
-              }
+            for (int j = 0; j < 32; ++j) v[j] = 0u;
+            for (int cta = c_first; cta <= c_last; ++cta) {
+              const int s = 2 * cta + (sk_begin(args, cta) < tile_begin ? 1 : 0);
+              const int32_t* p = args.ws + static_cast<int64_t>(s) * (T::kBM * BN) + (c * T::kChunk) * T::kBM +
+                                 row_in_tile;
+#pragma unroll
+              for (int j = 0; j < T::kChunk; ++j)
+                v[j] = static_cast<uint32_t>(static_cast<int32_t>(v[j]) + __ldcg(p + j * T::kBM));
             }
             store_chunk<SWAP, T::kChunk>(args, out, row, tn * BN + c * T::kChunk, v);
           }
           if (et == 0) args.counters[tile] = 0u;
         }
-        // last_flag is rewritten by the next tile: keep every reader ahead of it
+        // last_flag is rewritten by the next fragment: keep every reader ahead of it
         dev::named_bar_sync(1, 128);
       }
       if constexpr (FUSED) {
@@ -502,8 +590,9 @@ __global__ void __launch_bounds__(192, 1)
     dev::tmem_dealloc(tmem_base, T::kTmemCols);
   }
   if constexpr (FUSED) {
-    // The last CTA of the call publishes the epoch for the next call.
-    if (threadIdx.x == 0) {
+    // The last CTA of the call publishes the epoch for the next call (thread
+    // 64 is an epilogue thread, which read the epoch after griddep_wait).
+    if (threadIdx.x == 64) {
       uint32_t* c = dev::ctrl_ptr(cv.base[cv.rank]);
       __threadfence();
       const uint32_t done = atomicAdd(c + 1, 1u);

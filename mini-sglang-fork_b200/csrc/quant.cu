@@ -20,6 +20,7 @@
 #include <mutex>
 
 #include "common.cuh"
+#include "sm100.cuh"
 
 namespace {
 
@@ -44,21 +45,32 @@ __device__ __forceinline__ float block_max(float v, float* red) {
   return warp_max(r);
 }
 
-__device__ __forceinline__ int8_t quant_one(float v, float s) {
+// q = clamp(rint_even(fl(v / s)), -127, 127) without an IEEE divide on the
+// common path.  With Q = v/s exact, |Q| < 127.5: fl(v/s) = Q(1+d1),
+// inv = fl(1/s) = (1/s)(1+d2), r = fl(v * inv) = Q(1+d2)(1+d3), |di| <= 2^-24,
+// so |r - fl(v/s)| <= 127.5 * 3 * 2^-24 < 2.3e-5.  If rint(r) and
+// rint(fl(v/s)) differed, a half-integer would lie between them, i.e. within
+// 2.3e-5 of r; so outside a 6.1e-5 band around half-integers the cheap
+// rint(r) is exact, and inside it the quotient is taken with the IEEE divide.
+// `inv` is only used when s > 0.
+__device__ __forceinline__ int8_t quant_one(float v, float s, float inv) {
   if (s == 0.0f) return 0;
-  int q = __float2int_rn(__fdiv_rn(v, s));
+  const float r = __fmul_rn(v, inv);
+  const float f = r - floorf(r);
+  const float t = fabsf(f - 0.5f) < 6.1e-5f ? __fdiv_rn(v, s) : r;
+  int q = __float2int_rn(t);
   q = q > 127 ? 127 : (q < -127 ? -127 : q);
   return static_cast<int8_t>(q);
 }
 
-__device__ __forceinline__ uint2 quant_vec8(const uint4& raw, float s) {
+__device__ __forceinline__ uint2 quant_vec8(const uint4& raw, float s, float inv) {
   const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw);
   uint32_t lo = 0, hi = 0;
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
     float2 f = __bfloat1622float2(h[j]);
-    uint32_t b0 = static_cast<uint8_t>(quant_one(f.x, s));
-    uint32_t b1 = static_cast<uint8_t>(quant_one(f.y, s));
+    uint32_t b0 = static_cast<uint8_t>(quant_one(f.x, s, inv));
+    uint32_t b1 = static_cast<uint8_t>(quant_one(f.y, s, inv));
     uint32_t pair = b0 | (b1 << 8);
     if (j < 2)
       lo |= pair << (16 * j);
@@ -80,6 +92,9 @@ __device__ __forceinline__ float vec8_absmax(const uint4& raw) {
 }
 
 // y = bf16(silu(g) * u) for 8 lanes, silu(g) = g / (1 + exp(-g)) in fp32.
+// The fp32 value is rounded to bf16 (8 significand bits) at the end, so the
+// fast divide's couple of fp32 ulps almost never reach the bf16 result; the
+// quantiser then works on the bf16 values exactly.
 __device__ __forceinline__ uint4 silu_mul_vec8(const uint4& graw, const uint4& uraw) {
   const __nv_bfloat162* g = reinterpret_cast<const __nv_bfloat162*>(&graw);
   const __nv_bfloat162* u = reinterpret_cast<const __nv_bfloat162*>(&uraw);
@@ -89,8 +104,8 @@ __device__ __forceinline__ uint4 silu_mul_vec8(const uint4& graw, const uint4& u
   for (int j = 0; j < 4; ++j) {
     float2 gf = __bfloat1622float2(g[j]);
     float2 uf = __bfloat1622float2(u[j]);
-    float y0 = __fmul_rn(__fdiv_rn(gf.x, __fadd_rn(1.0f, expf(-gf.x))), uf.x);
-    float y1 = __fmul_rn(__fdiv_rn(gf.y, __fadd_rn(1.0f, expf(-gf.y))), uf.y);
+    float y0 = __fmul_rn(__fdividef(gf.x, __fadd_rn(1.0f, expf(-gf.x))), uf.x);
+    float y1 = __fmul_rn(__fdividef(gf.y, __fadd_rn(1.0f, expf(-gf.y))), uf.y);
     o[j] = __floats2bfloat162_rn(y0, y1);
   }
   return out;
@@ -106,11 +121,18 @@ struct RowSrc {
     a = reinterpret_cast<const uint4*>(base + row * ld);
     b = reinterpret_cast<const uint4*>(base + row * ld + width);
   }
-  __device__ __forceinline__ uint4 load(int vi) const {
+  // Issue the HBM load(s) of vector vi; combine() turns them into the value.
+  // Kept apart so a thread can have all of its loads in flight before it
+  // consumes the first one.
+  __device__ __forceinline__ void fetch(int vi, uint4& x, uint4& y) const {
+    x = __ldcs(a + vi);
+    if constexpr (SILU) y = __ldcs(b + vi);
+  }
+  __device__ __forceinline__ uint4 combine(const uint4& x, const uint4& y) const {
     if constexpr (SILU) {
-      return silu_mul_vec8(__ldcs(a + vi), __ldcs(b + vi));
+      return silu_mul_vec8(x, y);
     } else {
-      return __ldcs(a + vi);
+      return x;
     }
   }
 };
@@ -121,28 +143,36 @@ __global__ void __launch_bounds__(kRegThreads) rows_reg_kernel(const __nv_bfloat
                                                                int8_t* __restrict__ q, float* __restrict__ scale,
                                                                __nv_bfloat16* __restrict__ y_out, int width) {
   __shared__ float red[32];
+  w8a8::dev::griddep_wait();  // the row is the previous kernel's output
+  w8a8::dev::griddep_launch();
   const int64_t row = blockIdx.x;
   const int nvec = width >> 3;
   const RowSrc<SILU> src(in, row, ld, width);
-  uint4 buf[VPT];
+  uint4 buf[VPT], aux[VPT];
   float amax = 0.0f;
 #pragma unroll
   for (int i = 0; i < VPT; ++i) {
     const int vi = threadIdx.x + i * blockDim.x;
+    if (vi < nvec) src.fetch(vi, buf[i], aux[i]);
+  }
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    const int vi = threadIdx.x + i * blockDim.x;
     if (vi < nvec) {
-      buf[i] = src.load(vi);
+      buf[i] = src.combine(buf[i], aux[i]);
       amax = fmaxf(amax, vec8_absmax(buf[i]));
     }
   }
   amax = block_max(amax, red);
   const float s = __fdiv_rn(amax, 127.0f);
+  const float inv = s > 0.0f ? __frcp_rn(s) : 0.0f;
   uint2* qr = reinterpret_cast<uint2*>(q + row * static_cast<int64_t>(width));
   uint4* yr = y_out ? reinterpret_cast<uint4*>(y_out + row * static_cast<int64_t>(width)) : nullptr;
 #pragma unroll
   for (int i = 0; i < VPT; ++i) {
     const int vi = threadIdx.x + i * blockDim.x;
     if (vi < nvec) {
-      qr[vi] = quant_vec8(buf[i], s);
+      qr[vi] = quant_vec8(buf[i], s, inv);
       if (SILU && yr) yr[vi] = buf[i];
     }
   }
@@ -156,6 +186,8 @@ __global__ void __launch_bounds__(kSmemThreads) rows_smem_kernel(const __nv_bflo
                                                                  __nv_bfloat16* __restrict__ y_out, int width) {
   extern __shared__ uint4 stage[];
   __shared__ float red[32];
+  w8a8::dev::griddep_wait();  // the row is the previous kernel's output
+  w8a8::dev::griddep_launch();
   const int64_t row = blockIdx.x;
   const int nvec = width >> 3;
   const RowSrc<SILU> src(in, row, ld, width);
@@ -163,8 +195,13 @@ __global__ void __launch_bounds__(kSmemThreads) rows_smem_kernel(const __nv_bflo
   int vi = threadIdx.x;
   // four independent loads in flight per thread
   for (; vi + 3 * kSmemThreads < nvec; vi += 4 * kSmemThreads) {
-    uint4 v0 = src.load(vi), v1 = src.load(vi + kSmemThreads);
-    uint4 v2 = src.load(vi + 2 * kSmemThreads), v3 = src.load(vi + 3 * kSmemThreads);
+    uint4 x0, y0, x1, y1, x2, y2, x3, y3;
+    src.fetch(vi, x0, y0);
+    src.fetch(vi + kSmemThreads, x1, y1);
+    src.fetch(vi + 2 * kSmemThreads, x2, y2);
+    src.fetch(vi + 3 * kSmemThreads, x3, y3);
+    const uint4 v0 = src.combine(x0, y0), v1 = src.combine(x1, y1);
+    const uint4 v2 = src.combine(x2, y2), v3 = src.combine(x3, y3);
     stage[vi] = v0;
     stage[vi + kSmemThreads] = v1;
     stage[vi + 2 * kSmemThreads] = v2;
@@ -172,17 +209,20 @@ __global__ void __launch_bounds__(kSmemThreads) rows_smem_kernel(const __nv_bflo
     amax = fmaxf(fmaxf(amax, vec8_absmax(v0)), fmaxf(vec8_absmax(v1), fmaxf(vec8_absmax(v2), vec8_absmax(v3))));
   }
   for (; vi < nvec; vi += kSmemThreads) {
-    const uint4 v = src.load(vi);
+    uint4 x, y;
+    src.fetch(vi, x, y);
+    const uint4 v = src.combine(x, y);
     stage[vi] = v;
     amax = fmaxf(amax, vec8_absmax(v));
   }
   amax = block_max(amax, red);  // its __syncthreads also publishes `stage`
   const float s = __fdiv_rn(amax, 127.0f);
+  const float inv = s > 0.0f ? __frcp_rn(s) : 0.0f;
   uint2* qr = reinterpret_cast<uint2*>(q + row * static_cast<int64_t>(width));
   uint4* yr = y_out ? reinterpret_cast<uint4*>(y_out + row * static_cast<int64_t>(width)) : nullptr;
   for (int i = threadIdx.x; i < nvec; i += kSmemThreads) {
     const uint4 v = stage[i];
-    qr[i] = quant_vec8(v, s);
+    qr[i] = quant_vec8(v, s, inv);
     if (SILU && yr) yr[i] = v;
   }
   if (threadIdx.x == 0) scale[row] = s;
@@ -198,9 +238,12 @@ int launch_rows(const __nv_bfloat16* in, int64_t ld, int8_t* q, float* scale, __
     const int need = (nvec + vpt - 1) / vpt;
     const int threads = need < 32 ? 32 : ((need + 31) / 32) * 32;
     switch (vpt) {
-      case 1: rows_reg_kernel<1, SILU><<<grid, threads, 0, s>>>(in, ld, q, scale, y, width); break;
-      case 2: rows_reg_kernel<2, SILU><<<grid, threads, 0, s>>>(in, ld, q, scale, y, width); break;
-      default: rows_reg_kernel<4, SILU><<<grid, threads, 0, s>>>(in, ld, q, scale, y, width); break;
+      case 1: W8A8_CUDA_TRY(w8a8::launch_pdl(rows_reg_kernel<1, SILU>, grid, dim3(threads), 0, s, in, ld, q, scale, y,
+                                             width)); break;
+      case 2: W8A8_CUDA_TRY(w8a8::launch_pdl(rows_reg_kernel<2, SILU>, grid, dim3(threads), 0, s, in, ld, q, scale, y,
+                                             width)); break;
+      default: W8A8_CUDA_TRY(w8a8::launch_pdl(rows_reg_kernel<4, SILU>, grid, dim3(threads), 0, s, in, ld, q, scale,
+                                              y, width)); break;
     }
   } else {
     static std::mutex mu;
@@ -215,7 +258,8 @@ int launch_rows(const __nv_bfloat16* in, int64_t ld, int8_t* q, float* scale, __
         configured[dev] = true;
       }
     }
-    rows_smem_kernel<SILU><<<grid, kSmemThreads, nvec * 16, s>>>(in, ld, q, scale, y, width);
+    W8A8_CUDA_TRY(w8a8::launch_pdl(rows_smem_kernel<SILU>, grid, dim3(kSmemThreads), static_cast<size_t>(nvec) * 16, s,
+                                   in, ld, q, scale, y, width));
   }
   W8A8_CUDA_TRY(cudaGetLastError());
   return W8A8_OK;

@@ -19,6 +19,19 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
   return t;
 }
 
+// ------------------------------------------- programmatic dependent launch
+// Kernels are launched with programmatic stream serialisation: a kernel may
+// start while the previous one in the stream is finishing.  Everything before
+// griddep_wait() must touch only data the previous kernel cannot write or read
+// (shared memory, TMEM, weights); griddep_wait() returns once the previous
+// kernel has completed and its memory operations are visible.
+// griddep_launch() lets the next kernel start its own prologue.
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+__device__ __forceinline__ void griddep_launch() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // ------------------------------------------------------------------ mbarrier
 __device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");

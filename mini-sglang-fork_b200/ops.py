@@ -126,24 +126,25 @@ def silu_and_mul(x: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.T
     return y
 
 
-def gemm_plan(m: int, n: int, k: int, variant: int = 0, splits: int = 0,
+def gemm_plan(m: int, n: int, k: int, variant: int = 0, ctas: int = 0,
               workspace_bytes: int = WORKSPACE_BYTES, num_sms: int = 148) -> Dict[str, int]:
     """Host-only query of the tile configuration the GEMM would use."""
     out = (ctypes.c_int64 * 8)()
-    _lib.check(_lib.load().w8a8_gemm_plan(m, n, k, variant, splits, workspace_bytes, num_sms, out),
+    _lib.check(_lib.load().w8a8_gemm_plan(m, n, k, variant, ctas, workspace_bytes, num_sms, out),
                "gemm_plan")
-    keys = ("variant", "bn", "swap", "tiles", "splits", "kb_per_split", "grid", "workspace_bytes")
+    keys = ("variant", "bn", "swap", "tiles", "grid", "kblocks", "gran", "workspace_bytes")
     return dict(zip(keys, (int(v) for v in out)))
 
 
 def w8a8_gemm(aq: torch.Tensor, wq: torch.Tensor, sa: torch.Tensor, sw: torch.Tensor,
               bias: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None,
-              out_i32: Optional[torch.Tensor] = None, variant: int = 0, splits: int = 0) -> torch.Tensor:
+              out_i32: Optional[torch.Tensor] = None, variant: int = 0, ctas: int = 0) -> torch.Tensor:
     """``bf16((f32(aq @ wq.T) * sa[:, None]) * sw[None, :] + bias)`` on tcgen05.
 
     ``aq [M, K]`` int8, ``wq [N, K]`` int8, ``sa [M]`` / ``sw [N]`` fp32,
     ``bias [N]`` bf16 or None.  ``out_i32`` (optional ``[M, N]`` int32)
-    receives the exact accumulator.
+    receives the exact accumulator.  ``variant`` / ``ctas`` override the
+    planner (0 = automatic).
     """
     _require_cuda("w8a8_gemm", aq, wq, sa, sw, bias, out, out_i32)
     if aq.dtype != torch.int8 or wq.dtype != torch.int8:
@@ -168,7 +169,7 @@ def w8a8_gemm(aq: torch.Tensor, wq: torch.Tensor, sa: torch.Tensor, sw: torch.Te
     ws = gemm_workspace(aq.device)
     lib = _lib.load()
     st = lib.w8a8_gemm_config(_ptr(aq), _ptr(wq), _ptr(sa), _ptr(sw), _ptr(bias), _ptr(out), _ptr(out_i32),
-                              m, n, k, variant, splits, _ptr(ws), ws.numel(), _stream(aq))
+                              m, n, k, variant, ctas, _ptr(ws), ws.numel(), _stream(aq))
     _lib.check(st, "w8a8_gemm")
     return out
 

@@ -68,27 +68,78 @@ def test_planner_variant_choice(pkg, m, n, k, variant, bn, swap):
     p = pkg.ops.gemm_plan(m, n, k)
     assert (p["variant"], p["bn"], p["swap"]) == (variant, bn, swap)
     assert 1 <= p["grid"] <= 148
-    assert p["splits"] >= 1 and p["kb_per_split"] * p["splits"] >= (k + 127) // 128
-    assert (p["splits"] - 1) * p["kb_per_split"] < (k + 127) // 128  # no empty split
-    if p["splits"] > 1:
-        assert p["workspace_bytes"] >= p["tiles"] * 128 * p["bn"] * 4
+    assert p["kblocks"] == (k + 127) // 128
+    assert p["gran"] in (1, p["kblocks"])
+    if p["workspace_bytes"]:
+        assert p["workspace_bytes"] >= 2 * p["grid"] * 128 * p["bn"] * 4
 
 
-def test_planner_splits_small_m_to_fill_the_gpu(pkg):
-    # decode: down_proj of the Qwen3-8B MLP has only 32 weight tiles
+def _schedule(tiles, kblocks, grid, gran=1):
+    """Host model of the kernel's hybrid schedule (FragmentWalk, sk_begin,
+    sk_owner): whole tiles dealt in grid-stride order, then stream-K ranges
+    over the remaining tiles' k blocks.  Returns per-CTA fragment lists."""
+    dp = (tiles // grid) * grid
+    units = (tiles - dp) * kblocks // gran
+    begin = [dp * kblocks + (c * units // grid) * gran for c in range(grid + 1)]
+    owner = lambda x: (((x - dp * kblocks) // gran + 1) * grid - 1) // units  # noqa: E731
+    frags = []
+    for c in range(grid):
+        f = [(t, 0, kblocks) for t in range(c, dp, grid)]
+        it, end = begin[c], begin[c + 1]
+        while it < end:
+            t, k0 = divmod(it, kblocks)
+            k1 = min(kblocks, k0 + (end - it))
+            f.append((t, k0, k1))
+            it += k1 - k0
+        frags.append(f)
+    return frags, begin, owner
+
+
+@pytest.mark.parametrize("tiles,kblocks,grid", [(400, 40, 148), (32, 96, 148), (7, 3, 5), (6400, 40, 148),
+                                                (80, 40, 148), (3, 1, 3), (1, 1, 1), (200, 7, 64),
+                                                (119, 9, 148), (296, 40, 148)])
+def test_hybrid_schedule_covers_every_iteration_once(tiles, kblocks, grid):
+    grid = min(grid, tiles * kblocks)
+    frags, begin, owner = _schedule(tiles, kblocks, grid)
+    seen = {}
+    for c, f in enumerate(frags):
+        for (t, k0, k1) in f:
+            for k in range(k0, k1):
+                assert (t, k) not in seen
+                seen[(t, k)] = c
+    assert len(seen) == tiles * kblocks
+    # per cut tile: the owners of its first and last iteration bound its
+    # fragments, and the workspace slots (2c + started-before-tile) are distinct
+    for t in range(tiles):
+        owners = sorted({seen[(t, k)] for k in range(kblocks)})
+        if len(owners) == 1:
+            continue
+        c0, c1 = owner(t * kblocks), owner(t * kblocks + kblocks - 1)
+        assert owners == list(range(c0, c1 + 1))
+        slots = {2 * c + (1 if begin[c] < t * kblocks else 0) for c in owners}
+        assert len(slots) == len(owners)
+    # balance: k blocks per CTA differ by at most one tile's worth plus one
+    work = [sum(k1 - k0 for _, k0, k1 in f) for f in frags]
+    assert max(work) - min(work) <= 1
+
+
+def test_planner_stream_k_balances_few_tiles(pkg):
+    # decode: down_proj of the Qwen3-8B MLP has only 32 weight tiles; stream-K
+    # still spreads its 3072 k-block iterations over every SM
     p = pkg.ops.gemm_plan(1, 4096, 12288)
-    assert p["tiles"] == 32 and p["splits"] > 4 and p["tiles"] * p["splits"] >= 148
-    # large prefill keeps one split
-    assert pkg.ops.gemm_plan(8192, 24576, 4096)["splits"] == 1
+    assert p["tiles"] == 32 and p["grid"] == 148 and p["gran"] == 1 and p["workspace_bytes"] > 0
+    # a prefill shape whose iterations split evenly into whole tiles needs no workspace
+    p = pkg.ops.gemm_plan(8192, 24576, 4096, ctas=128)
+    assert p["grid"] == 128 and p["workspace_bytes"] == 0
 
 
 def test_planner_respects_workspace_limit(pkg):
     p = pkg.ops.gemm_plan(1, 4096, 12288, workspace_bytes=0)
-    assert p["splits"] == 1 and p["workspace_bytes"] == 0
+    assert p["gran"] == p["kblocks"] and p["workspace_bytes"] == 0 and p["grid"] == 32
+    p = pkg.ops.gemm_plan(1, 4096, 12288, ctas=7)
+    assert p["grid"] == 7 and p["gran"] == 1
     with pytest.raises(pkg.W8A8Error):
-        pkg.ops.gemm_plan(1, 4096, 12288, splits=4, workspace_bytes=1024)
-    p = pkg.ops.gemm_plan(1, 4096, 12288, splits=4)
-    assert p["splits"] == 4
+        pkg.ops.gemm_plan(1, 4096, 12288, ctas=-1)
 
 
 def test_ops_refuse_cpu_tensors(pkg):

@@ -28,19 +28,19 @@ def _operands(m, n, k, seed, bias=False):
     return aq, wq, sa, sw, b
 
 
-def _check(pkg, oracle, dev, m, n, k, variant=0, splits=0, bias=False, seed=0):
+def _check(pkg, oracle, dev, m, n, k, variant=0, ctas=0, bias=False, seed=0):
     aq, wq, sa, sw, b = _operands(m, n, k, seed, bias)
     acc_ref = oracle.int_gemm(aq, wq)
     y_ref = oracle.dequant(acc_ref, sa, sw, b)
     acc = torch.empty(m, n, dtype=torch.int32, device=dev)
     y = pkg.ops.w8a8_gemm(aq.to(dev), wq.to(dev), sa.to(dev), sw.to(dev), None if b is None else b.to(dev),
-                          out_i32=acc, variant=variant, splits=splits)
+                          out_i32=acc, variant=variant, ctas=ctas)
     torch.cuda.synchronize()
     assert pkg.ops.device_error() == 0
-    assert torch.equal(acc.cpu(), acc_ref), f"int32 mismatch m={m} n={n} k={k} v={variant} s={splits}"
+    assert torch.equal(acc.cpu(), acc_ref), f"int32 mismatch m={m} n={n} k={k} v={variant} ctas={ctas}"
     yc = y.cpu()
     torch.testing.assert_close(yc.float(), y_ref.float(), rtol=RTOL, atol=ATOL)
-    assert torch.equal(yc, y_ref), f"bf16 mismatch m={m} n={n} k={k} v={variant} s={splits}"
+    assert torch.equal(yc, y_ref), f"bf16 mismatch m={m} n={n} k={k} v={variant} ctas={ctas}"
 
 
 # (m, n, k) spanning every variant's edge cases: partial tiles, K not a
@@ -54,13 +54,16 @@ CASES = [
 @pytest.mark.parametrize("variant", [1, 2, 3, 4, 5, 6])
 @pytest.mark.parametrize("m,n,k", CASES)
 def test_gemm_variants_bit_exact(pkg, oracle, cuda_dev, variant, m, n, k):
-    _check(pkg, oracle, cuda_dev, m, n, k, variant=variant, splits=1, seed=m + n + k + variant)
+    _check(pkg, oracle, cuda_dev, m, n, k, variant=variant, seed=m + n + k + variant)
 
 
 @pytest.mark.parametrize("variant", [1, 2, 3, 5, 6])
-@pytest.mark.parametrize("splits", [2, 3, 7])
-def test_gemm_split_k_bit_exact(pkg, oracle, cuda_dev, variant, splits):
-    _check(pkg, oracle, cuda_dev, 40, 400, 1024, variant=variant, splits=splits, seed=splits * 10 + variant)
+@pytest.mark.parametrize("ctas", [1, 2, 3, 7, 64])
+def test_gemm_stream_k_bit_exact(pkg, oracle, cuda_dev, variant, ctas):
+    """Few CTAs over many tiles: ranges cut tiles at arbitrary k blocks, and a
+    tile can be shared by several CTAs (workspace fix-up path)."""
+    _check(pkg, oracle, cuda_dev, 40, 400, 1024, variant=variant, ctas=ctas, seed=ctas * 10 + variant)
+    _check(pkg, oracle, cuda_dev, 130, 272, 1664, variant=variant, ctas=ctas, seed=ctas * 10 + variant + 1)
 
 
 @pytest.mark.parametrize("m,n,k", [(1, 24576, 4096), (16, 4096, 12288), (64, 6144, 1024), (256, 5120, 8192),
@@ -69,12 +72,16 @@ def test_gemm_auto_plan(pkg, oracle, cuda_dev, m, n, k):
     _check(pkg, oracle, cuda_dev, m, n, k, bias=(m % 2 == 0), seed=m * 3 + n)
 
 
-def test_split_k_workspace_stays_zero(pkg, oracle, cuda_dev):
-    """Back-to-back split-K calls: every call leaves the workspace zeroed."""
-    for rep in range(3):
-        _check(pkg, oracle, cuda_dev, 5, 4096, 12288, seed=rep)
+def test_stream_k_counters_return_to_zero(pkg, oracle, cuda_dev):
+    """Back-to-back stream-K calls of different shapes sharing the workspace:
+    every call leaves the tile counters at the workspace head zeroed, and no
+    call's partial tiles land on another call's counters."""
+    for rep, (m, n, k) in enumerate([(5, 4096, 12288), (300, 8192, 1024), (7, 2048, 3072), (5, 4096, 12288)]):
+        _check(pkg, oracle, cuda_dev, m, n, k, seed=rep)
+    p = pkg.ops.gemm_plan(5, 4096, 12288, num_sms=torch.cuda.get_device_properties(0).multi_processor_count)
+    assert p["workspace_bytes"] > 0
     ws = pkg.ops.gemm_workspace(cuda_dev)
-    assert int(ws.count_nonzero()) == 0
+    assert int(ws[: 65536 * 4].count_nonzero()) == 0   # the whole fixed counter region
 
 
 def test_gemm_golden_small(pkg, oracle, cuda_dev):

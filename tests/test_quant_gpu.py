@@ -46,6 +46,26 @@ def test_quant_edge_rows(pkg, oracle, cuda_dev):
     assert int(q[4, 0]) == 0
 
 
+def test_quant_half_integer_ties(pkg, oracle, cuda_dev):
+    """x / s at or next to a half-integer: the kernel's reciprocal fast path
+    must fall back to the exact quotient there and round half to even."""
+    rows = []
+    ties = torch.arange(0, 127).float() + 0.5                        # s == 1: exact ties
+    rows.append(torch.cat([torch.tensor([127.0]), ties, -ties, torch.zeros(1)]).bfloat16())  # 256 wide
+    g = torch.Generator().manual_seed(1)
+    for _ in range(63):
+        amax = float(torch.rand(1, generator=g)) * 10 + 0.01
+        s = torch.tensor(amax, dtype=torch.float32) / 127.0
+        k = torch.randint(-127, 127, (255,), generator=g).float() + 0.5
+        near = (k * s).bfloat16()                                       # bf16 values close to ties
+        rows.append(torch.cat([torch.tensor([amax]).bfloat16(), near]))
+    x = torch.stack(rows)
+    q, s = pkg.ops.quant_per_token(x.to(cuda_dev))
+    qr, sr = oracle.quant_per_token(x)
+    assert torch.equal(s.cpu(), sr) and torch.equal(q.cpu(), qr)
+    assert q[0, 1:5].tolist() == [0, 2, 2, 4]
+
+
 def test_quant_strided_rows(pkg, oracle, cuda_dev):
     """A row-strided view (e.g. a slice of a wider buffer) quantises like its copy."""
     big = _x(9, 512, seed=11).to(cuda_dev)
