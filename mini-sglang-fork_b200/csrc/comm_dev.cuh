@@ -100,10 +100,13 @@ __device__ __forceinline__ bool wait_peer(const CommView& v, int phase, int slot
   }
 }
 
-// 16-byte load that bypasses this SM's L1 (peer data changes between calls).
+// 16-byte load of data another rank (or another call) wrote: cached at L2
+// only (.cg), never in this SM's L1, so no stale line can be hit.  Ordering
+// comes from the flag protocol: the polling thread's acquire load of the flag,
+// then a barrier of the reading threads, precede every such load.
 __device__ __forceinline__ uint4 ld_volatile_v4(const void* p) {
   uint4 r;
-  asm volatile("ld.volatile.global.v4.u32 {%0, %1, %2, %3}, [%4];"
+  asm volatile("ld.global.cg.v4.u32 {%0, %1, %2, %3}, [%4];"
                : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
                : "l"(p)
                : "memory");

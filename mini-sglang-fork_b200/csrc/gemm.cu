@@ -162,6 +162,7 @@ int run_gemm(const int8_t* A, const int8_t* B, const float* sa, const float* sb,
   args.tiles_n = p.tiles_n;
   args.num_tiles = p.num_tiles;
   args.dp_tiles = p.dp_tiles;
+  args.sk_ctas = p.sk_ctas;
   args.gran = p.gran;
   args.kblocks = p.kblocks;
   args.units = p.units;

@@ -25,6 +25,7 @@ struct GemmPlan {
   int dp_tiles;             // leading whole tiles in grid-stride order
   int gran;                 // stream-K granularity in k blocks: 1 or kblocks
   long long units;          // (num_tiles - dp_tiles) * kblocks / gran
+  int sk_ctas;              // CTAs sharing the stream-K part: min(grid, units), >= 1
   int grid;                 // persistent CTAs
   int wide_fast;
   bool cut_tiles;           // some tile is shared by two or more CTAs
@@ -89,9 +90,11 @@ inline int plan_gemm(int64_t M, int64_t N, int64_t K, int variant, int ctas_req,
   p->dp_tiles = static_cast<int>((p->num_tiles / g) * g);
   const long long iters = static_cast<long long>(p->num_tiles - p->dp_tiles) * p->kblocks;
 
-  // Does an even split of the remaining iterations cut any tile?
+  // Does an even split of the remaining iterations over min(g, iters) CTAs
+  // cut any tile?
+  const long long gs = iters < g ? iters : g;
   bool cut = false;
-  for (long long c = 1; c < g && iters > 0 && !cut; ++c) cut = ((c * iters / g) % p->kblocks) != 0;
+  for (long long c = 1; c < gs && !cut; ++c) cut = ((c * iters / gs) % p->kblocks) != 0;
   const size_t need = kCounterBytes + 2 * static_cast<size_t>(g) * 128 * p->bn * 4;
   if (cut && (need > ws_avail || p->num_tiles > kMaxCounterTiles)) {
     // no room to finish cut tiles: whole-tile ranges
@@ -106,6 +109,7 @@ inline int plan_gemm(int64_t M, int64_t N, int64_t K, int variant, int ctas_req,
   }
   p->grid = static_cast<int>(g);
   p->units = (static_cast<long long>(p->num_tiles - p->dp_tiles) * p->kblocks) / p->gran;
+  p->sk_ctas = static_cast<int>(p->units < g ? (p->units > 0 ? p->units : 1) : g);
   p->cut_tiles = cut;
   p->ws_counter_bytes = cut ? kCounterBytes : 0;
   p->ws_bytes = cut ? need : 0;

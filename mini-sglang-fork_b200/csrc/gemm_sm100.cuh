@@ -81,6 +81,7 @@ struct GemmArgs {
   int dp_tiles;               // leading tiles done whole, in grid-stride order
   int gran;                   // stream-K granularity in k blocks (1, or kblocks = whole tiles)
   long long units;            // (num_tiles - dp_tiles) * kblocks / gran
+  int sk_ctas;                // CTAs sharing the stream-K part: min(G, units), >= 1
   int wide_fast;              // raster: 1 = consecutive tiles walk the 128-row side
 };
 
@@ -120,15 +121,17 @@ __device__ __forceinline__ void tile_coords(const GemmArgs& a, int tile, int& tw
 // together adjacent for L2 reuse; the k-block iterations of the remaining
 // tiles are split evenly (stream-K).  sk_begin(c) is the first stream-K
 // iteration of CTA c (global iteration index).
+// Only the first sk_ctas = min(G, units) CTAs take stream-K work, so every one
+// of them has a non-empty range.
 __device__ __forceinline__ long long sk_begin(const GemmArgs& a, int c) {
-  return static_cast<long long>(a.dp_tiles) * a.kblocks +
-         (static_cast<long long>(c) * a.units / gridDim.x) * a.gran;
+  const int cc = c < a.sk_ctas ? c : a.sk_ctas;
+  return static_cast<long long>(a.dp_tiles) * a.kblocks + (static_cast<long long>(cc) * a.units / a.sk_ctas) * a.gran;
 }
 
 // The CTA whose stream-K range holds iteration x: max{c : sk_begin(c) <= x}.
 __device__ __forceinline__ int sk_owner(const GemmArgs& a, long long x) {
   const long long rel = x - static_cast<long long>(a.dp_tiles) * a.kblocks;
-  return static_cast<int>(((rel / a.gran + 1) * gridDim.x - 1) / a.units);
+  return static_cast<int>(((rel / a.gran + 1) * a.sk_ctas - 1) / a.units);
 }
 
 // Iterates the fragments (tile, [kb0, kb1)) of this CTA: its whole tiles of
@@ -234,35 +237,106 @@ __device__ __forceinline__ void tile_rect(const GemmArgs& a, int tile, int& m0, 
   }
 }
 
+// Threads of a CTA that take part in the fused reduction (all six warps, once
+// the GEMM work of the CTA is done) and the named barrier they use.
+constexpr int kReduceThreads = 192;
+constexpr int kReduceBar = 2;
+
+// Reduce-scatter of one tile share: rank-order fp32 sum of vectors [lo, hi)
+// of the tile rectangle from every rank, written in place into this rank's
+// buffer.  W = world (compile-time), so each thread keeps 8 / W vectors x W
+// ranks = 8 independent 16-byte loads in flight before it adds anything.
+template <int W>
+__device__ __forceinline__ void reduce_share(const CommView& cv, uint32_t epoch, const GemmArgs& a, int m0, int n0,
+                                             int vpr, int lo, int hi, int tid) {
+  constexpr int V = 8 / W;
+  const char* src[W];
+#pragma unroll
+  for (int r = 0; r < W; ++r) src[r] = dev::half_ptr(cv, r, epoch);
+  char* mine = dev::half_ptr(cv, cv.rank, epoch);
+  for (int base = lo + tid; base < hi; base += kReduceThreads * V) {
+    uint4 buf[V][W];
+    size_t off[V];
+#pragma unroll
+    for (int j = 0; j < V; ++j) {
+      const int i = base + j * kReduceThreads;
+      const int r = i / vpr, c = i - r * vpr;
+      off[j] = (static_cast<size_t>(m0 + r) * a.N + n0 + c * 8) * 2;
+      if (i < hi) {
+#pragma unroll
+        for (int q = 0; q < W; ++q) buf[j][q] = dev::ld_volatile_v4(src[q] + off[j]);
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < V; ++j) {
+      if (base + j * kReduceThreads < hi) {
+        float acc[8];
+        const __nv_bfloat162* h0 = reinterpret_cast<const __nv_bfloat162*>(&buf[j][0]);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 f = __bfloat1622float2(h0[e]);
+          acc[2 * e] = f.x;
+          acc[2 * e + 1] = f.y;
+        }
+#pragma unroll
+        for (int q = 1; q < W; ++q) {
+          const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&buf[j][q]);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float2 f = __bfloat1622float2(h[e]);
+            acc[2 * e] = __fadd_rn(acc[2 * e], f.x);
+            acc[2 * e + 1] = __fadd_rn(acc[2 * e + 1], f.y);
+          }
+        }
+        uint4 o;
+        __nv_bfloat162* ho = reinterpret_cast<__nv_bfloat162*>(&o);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) ho[e] = __floats2bfloat162_rn(acc[2 * e], acc[2 * e + 1]);
+        *reinterpret_cast<uint4*>(mine + off[j]) = o;
+      }
+    }
+  }
+}
+
+// Any world size: one vector at a time, ranks summed in order.
+__device__ __forceinline__ void reduce_share_any(const CommView& cv, uint32_t epoch, const GemmArgs& a, int m0,
+                                                 int n0, int vpr, int lo, int hi, int tid) {
+  char* mine = dev::half_ptr(cv, cv.rank, epoch);
+  for (int i = lo + tid; i < hi; i += kReduceThreads) {
+    const int r = i / vpr, c = i - r * vpr;
+    const size_t off = (static_cast<size_t>(m0 + r) * a.N + n0 + c * 8) * 2;
+    *reinterpret_cast<uint4*>(mine + off) = dev::sum_ranks_vec8(cv, epoch, off);
+  }
+}
+
 // Two-shot reduction of the tiles this CTA owns (t % gridDim.x == blockIdx.x)
-// across the ranks, by the 128 epilogue threads (index et).  Returns false if a
-// flag wait timed out.
+// across the ranks, by all kReduceThreads threads of the CTA (index tid).
+// Returns false if a flag wait timed out (uniformly across the threads).
 template <int BN, bool SWAP>
-__device__ bool fused_reduce_tiles(const GemmArgs& a, const CommView& cv, uint32_t epoch, int et) {
-  __nv_bfloat16* mine = reinterpret_cast<__nv_bfloat16*>(dev::half_ptr(cv, cv.rank, epoch));
+__device__ bool fused_reduce_tiles(const GemmArgs& a, const CommView& cv, uint32_t epoch, int tid) {
   // shot 1: reduce-scatter of every owned tile
   for (int t = blockIdx.x; t < a.num_tiles; t += gridDim.x) {
-    const bool ok = dev::wait_peer(cv, 0, t, epoch, et);
-    if (dev::named_bar_or(1, 128, !ok)) return false;
+    const bool ok = dev::wait_peer(cv, 0, t, epoch, tid);
+    if (dev::named_bar_or(kReduceBar, kReduceThreads, !ok)) return false;
     int m0, hm, n0, wn;
     tile_rect<BN, SWAP>(a, t, m0, hm, n0, wn);
     const int vpr = wn >> 3;
     const int nv = hm * vpr;
     const int lo = static_cast<int>((static_cast<long long>(nv) * cv.rank) / cv.world);
     const int hi = static_cast<int>((static_cast<long long>(nv) * (cv.rank + 1)) / cv.world);
-    for (int i = lo + et; i < hi; i += 128) {
-      const int r = i / vpr, c = i - r * vpr;
-      const size_t off = (static_cast<size_t>(m0 + r) * a.N + n0 + c * 8) * 2;
-      const uint4 s = dev::sum_ranks_vec8(cv, epoch, off);
-      *reinterpret_cast<uint4*>(reinterpret_cast<char*>(mine) + off) = s;
+    switch (cv.world) {
+      case 2: reduce_share<2>(cv, epoch, a, m0, n0, vpr, lo, hi, tid); break;
+      case 4: reduce_share<4>(cv, epoch, a, m0, n0, vpr, lo, hi, tid); break;
+      case 8: reduce_share<8>(cv, epoch, a, m0, n0, vpr, lo, hi, tid); break;
+      default: reduce_share_any(cv, epoch, a, m0, n0, vpr, lo, hi, tid); break;
     }
-    dev::named_bar_sync(1, 128);
-    dev::signal_peers(cv, 1, t, epoch, et);
+    dev::named_bar_sync(kReduceBar, kReduceThreads);
+    dev::signal_peers(cv, 1, t, epoch, tid);
   }
-  // shot 2: all-gather of every owned tile into C
+  // shot 2: all-gather of every owned tile into C, 8 loads in flight per thread
   for (int t = blockIdx.x; t < a.num_tiles; t += gridDim.x) {
-    const bool ok = dev::wait_peer(cv, 1, t, epoch, et);
-    if (dev::named_bar_or(1, 128, !ok)) return false;
+    const bool ok = dev::wait_peer(cv, 1, t, epoch, tid);
+    if (dev::named_bar_or(kReduceBar, kReduceThreads, !ok)) return false;
     int m0, hm, n0, wn;
     tile_rect<BN, SWAP>(a, t, m0, hm, n0, wn);
     const int vpr = wn >> 3;
@@ -271,11 +345,24 @@ __device__ bool fused_reduce_tiles(const GemmArgs& a, const CommView& cv, uint32
       const int lo = static_cast<int>((static_cast<long long>(nv) * src) / cv.world);
       const int hi = static_cast<int>((static_cast<long long>(nv) * (src + 1)) / cv.world);
       const char* from = dev::half_ptr(cv, src, epoch);
-      for (int i = lo + et; i < hi; i += 128) {
-        const int r = i / vpr, c = i - r * vpr;
-        const size_t idx = static_cast<size_t>(m0 + r) * a.N + n0 + c * 8;
-        *reinterpret_cast<uint4*>(a.C + static_cast<size_t>(m0 + r) * a.ldc + n0 + c * 8) =
-            dev::ld_volatile_v4(from + idx * 2);
+      for (int base = lo + tid; base < hi; base += kReduceThreads * 8) {
+        uint4 v[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const int i = base + j * kReduceThreads;
+          if (i < hi) {
+            const int r = i / vpr, c = i - r * vpr;
+            v[j] = dev::ld_volatile_v4(from + (static_cast<size_t>(m0 + r) * a.N + n0 + c * 8) * 2);
+          }
+        }
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const int i = base + j * kReduceThreads;
+          if (i < hi) {
+            const int r = i / vpr, c = i - r * vpr;
+            *reinterpret_cast<uint4*>(a.C + static_cast<size_t>(m0 + r) * a.ldc + n0 + c * 8) = v[j];
+          }
+        }
       }
     }
   }
@@ -300,6 +387,7 @@ __global__ void __launch_bounds__(192, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   volatile int* last_flag = abort_flag + 1;
+  volatile uint32_t* epoch_slot = reinterpret_cast<volatile uint32_t*>(last_flag + 1);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -580,7 +668,8 @@ __global__ void __launch_bounds__(192, 1)
     }
     dev::tc_fence_before();
     if constexpr (FUSED) {
-      if (!aborted) fused_reduce_tiles<BN, SWAP>(args, cv, epoch, et);
+      if (aborted) *abort_flag = 1;
+      if (et == 0) *epoch_slot = epoch;
     }
   }
 
@@ -590,9 +679,16 @@ __global__ void __launch_bounds__(192, 1)
     dev::tmem_dealloc(tmem_base, T::kTmemCols);
   }
   if constexpr (FUSED) {
-    // The last CTA of the call publishes the epoch for the next call (thread
-    // 64 is an epilogue thread, which read the epoch after griddep_wait).
-    if (threadIdx.x == 64) {
+    // All six warps reduce the CTA's tiles across the ranks (abort_flag and the
+    // epoch are read after the barrier, so the decision is uniform).
+    epoch = *epoch_slot;
+    if (*abort_flag == 0) {
+      dev::griddep_wait();
+      fused_reduce_tiles<BN, SWAP>(args, cv, epoch, threadIdx.x);
+    }
+    __syncthreads();
+    // The last CTA of the call publishes the epoch for the next call.
+    if (threadIdx.x == 0) {
       uint32_t* c = dev::ctrl_ptr(cv.base[cv.rank]);
       __threadfence();
       const uint32_t done = atomicAdd(c + 1, 1u);

@@ -80,8 +80,9 @@ def _schedule(tiles, kblocks, grid, gran=1):
     over the remaining tiles' k blocks.  Returns per-CTA fragment lists."""
     dp = (tiles // grid) * grid
     units = (tiles - dp) * kblocks // gran
-    begin = [dp * kblocks + (c * units // grid) * gran for c in range(grid + 1)]
-    owner = lambda x: (((x - dp * kblocks) // gran + 1) * grid - 1) // units  # noqa: E731
+    sk = max(1, min(grid, units))            # CTAs sharing the stream-K part
+    begin = [dp * kblocks + (min(c, sk) * units // sk) * gran for c in range(grid + 1)]
+    owner = lambda x: (((x - dp * kblocks) // gran + 1) * sk - 1) // units  # noqa: E731
     frags = []
     for c in range(grid):
         f = [(t, 0, kblocks) for t in range(c, dp, grid)]
@@ -97,7 +98,8 @@ def _schedule(tiles, kblocks, grid, gran=1):
 
 @pytest.mark.parametrize("tiles,kblocks,grid", [(400, 40, 148), (32, 96, 148), (7, 3, 5), (6400, 40, 148),
                                                 (80, 40, 148), (3, 1, 3), (1, 1, 1), (200, 7, 64),
-                                                (119, 9, 148), (296, 40, 148)])
+                                                (119, 9, 148), (296, 40, 148), (160, 4, 148),
+                                                (150, 2, 148), (149, 1, 148), (300, 3, 148)])
 def test_hybrid_schedule_covers_every_iteration_once(tiles, kblocks, grid):
     grid = min(grid, tiles * kblocks)
     frags, begin, owner = _schedule(tiles, kblocks, grid)
@@ -118,9 +120,10 @@ def test_hybrid_schedule_covers_every_iteration_once(tiles, kblocks, grid):
         assert owners == list(range(c0, c1 + 1))
         slots = {2 * c + (1 if begin[c] < t * kblocks else 0) for c in owners}
         assert len(slots) == len(owners)
-    # balance: k blocks per CTA differ by at most one tile's worth plus one
+    # every stream-K CTA has work, and k blocks per CTA differ by at most one
+    # tile when the remainder is smaller than the grid, else by at most one
     work = [sum(k1 - k0 for _, k0, k1 in f) for f in frags]
-    assert max(work) - min(work) <= 1
+    assert max(work) - min(work) <= max(1, kblocks if (tiles % grid) * kblocks < grid else 1)
 
 
 def test_planner_stream_k_balances_few_tiles(pkg):

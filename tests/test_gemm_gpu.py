@@ -67,7 +67,9 @@ def test_gemm_stream_k_bit_exact(pkg, oracle, cuda_dev, variant, ctas):
 
 
 @pytest.mark.parametrize("m,n,k", [(1, 24576, 4096), (16, 4096, 12288), (64, 6144, 1024), (256, 5120, 8192),
-                                   (2048, 2048, 4096), (33, 1280, 8192)])
+                                   (2048, 2048, 4096), (33, 1280, 8192),
+                                   # stream-K remainder smaller than the grid (160 tiles, 148 CTAs, 4 k blocks)
+                                   (1024, 5120, 512), (1100, 5120, 256)])
 def test_gemm_auto_plan(pkg, oracle, cuda_dev, m, n, k):
     _check(pkg, oracle, cuda_dev, m, n, k, bias=(m % 2 == 0), seed=m * 3 + n)
 
