@@ -45,7 +45,8 @@ struct w8a8_comm {
   int rank = 0;
   int world = 1;
   int device = 0;
-  size_t half_bytes = 0;
+  size_t slot_bytes = 0;   // max_bytes rounded up
+  size_t half_bytes = 0;   // (world + 1) * slot_bytes
   size_t total_bytes = 0;
   char* local = nullptr;
   char* peers[w8a8::kMaxWorld] = {nullptr};
@@ -147,6 +148,8 @@ CommView make_view(const w8a8_comm* c, unsigned int* err) {
   v.rank = c->rank;
   v.world = c->world;
   v.half_bytes = c->half_bytes;
+  v.slot_bytes = c->slot_bytes;
+  v.two_shot = 0;
   v.err = err;
   v.timeout_ns = c->timeout_ns;
   return v;
@@ -187,7 +190,8 @@ int w8a8_comm_create(int rank, int world, int device, size_t max_bytes, w8a8_com
   c->rank = rank;
   c->world = world;
   c->device = device;
-  c->half_bytes = round_up(max_bytes, 4096);
+  c->slot_bytes = round_up(max_bytes, 4096);
+  c->half_bytes = static_cast<size_t>(world + 1) * c->slot_bytes;
   c->total_bytes = kHeaderBytes + 2 * c->half_bytes;
   cudaError_t e = cudaMalloc(&c->local, c->total_bytes);
   if (e == cudaSuccess) e = cudaMemset(c->local, 0, kHeaderBytes);
@@ -276,8 +280,8 @@ int w8a8_all_reduce(w8a8_comm* c, void* x, int64_t numel, void* stream) {
                (long long)numel);
   W8A8_REQUIRE(W8A8_ALIGNED16(x), W8A8_ERR_ALIGNMENT, "all_reduce: tensor must be 16-byte aligned");
   const size_t bytes = static_cast<size_t>(numel) * 2;
-  W8A8_REQUIRE(bytes <= c->half_bytes, W8A8_ERR_INVALID_ARG,
-               "all_reduce: %zu bytes exceed the communicator's max_bytes %zu", bytes, c->half_bytes);
+  W8A8_REQUIRE(bytes <= c->slot_bytes, W8A8_ERR_INVALID_ARG,
+               "all_reduce: %zu bytes exceed the communicator's max_bytes %zu", bytes, c->slot_bytes);
   unsigned int* err = device_error_word();
   if (!err) return W8A8_ERR_CUDA;
   const CommView v = make_view(c, err);
@@ -304,7 +308,14 @@ int w8a8_gemm_allreduce(w8a8_comm* c, const int8_t* A, const int8_t* B, const fl
                     static_cast<cudaStream_t>(stream), kDefaultGemmTimeoutNs, nullptr);
   unsigned int* err = device_error_word();
   if (!err) return W8A8_ERR_CUDA;
-  const CommView v = make_view(c, err);
+  CommView v = make_view(c, err);
+  // One-shot push (every rank receives every partial row and reduces the whole
+  // tile itself: one flag hop) unless the extra (world - 2) copies of the
+  // output would cost more NVLink time than a second hop: two-shot for large
+  // outputs at world >= 4 (tiles in the normal orientation, M > 64).
+  const size_t bytes = static_cast<size_t>(M) * N * 2;
+  const bool two = c->mode == 2 || (c->mode == 0 && c->world >= 4 && M > 64 && bytes * (c->world - 1) > (4u << 20));
+  v.two_shot = (two && M > 64) ? 1 : 0;
   return run_gemm(A, B, sa, sb, bias, C, nullptr, M, N, K, 0, 0, workspace, workspace_bytes,
                   static_cast<cudaStream_t>(stream), c->timeout_ns, &v);
 }

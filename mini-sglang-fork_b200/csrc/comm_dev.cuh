@@ -35,8 +35,10 @@ struct CommView {
   char* base[kMaxWorld];  // every rank's buffer, as mapped in this process
   int rank;
   int world;
-  unsigned long long half_bytes;
-  unsigned int* err;      // device error word
+  unsigned long long half_bytes;  // (world + 1) * slot_bytes
+  unsigned long long slot_bytes;  // one [M, N] bf16 tensor of at most max_bytes
+  int two_shot;                   // fused GEMM reduce: 1 = two-shot, 0 = one-shot
+  unsigned int* err;              // device error word
   long long timeout_ns;
 };
 
@@ -52,6 +54,18 @@ __device__ __forceinline__ uint32_t* ctrl_ptr(char* base) {
 
 __device__ __forceinline__ char* half_ptr(const CommView& v, int r, uint32_t epoch) {
   return v.base[r] + kHeaderBytes + static_cast<size_t>(epoch & 1u) * v.half_bytes;
+}
+
+// Inside a data half, the fused GEMM reduce uses world receive slots (slot s
+// holds source rank s's partial rows, same [M, N] layout as C) followed by
+// one all-gather slot (reduced rows pushed by their owners, two-shot only).
+// The standalone all-reduce uses the start of the half (slot 0).
+__device__ __forceinline__ char* recv_slot(const CommView& v, int at_rank, int src, uint32_t epoch) {
+  return half_ptr(v, at_rank, epoch) + static_cast<size_t>(src) * v.slot_bytes;
+}
+
+__device__ __forceinline__ char* gather_slot(const CommView& v, int at_rank, uint32_t epoch) {
+  return half_ptr(v, at_rank, epoch) + static_cast<size_t>(v.world) * v.slot_bytes;
 }
 
 __device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {

@@ -118,10 +118,15 @@ int run_gemm(const int8_t* A, const int8_t* B, const float* sa, const float* sb,
   if (comm) {
     W8A8_REQUIRE(p.num_tiles <= kMaxSlots, W8A8_ERR_UNSUPPORTED,
                  "gemm_allreduce: %d output tiles exceed the %d flag slots", p.num_tiles, kMaxSlots);
-    W8A8_REQUIRE(static_cast<unsigned long long>(M) * N * 2 <= comm->half_bytes, W8A8_ERR_INVALID_ARG,
+    W8A8_REQUIRE(static_cast<unsigned long long>(M) * N * 2 <= comm->slot_bytes, W8A8_ERR_INVALID_ARG,
                  "gemm_allreduce: output of %lld x %lld bf16 exceeds the communicator's max_bytes %llu",
-                 (long long)M, (long long)N, comm->half_bytes);
+                 (long long)M, (long long)N, comm->slot_bytes);
     W8A8_REQUIRE(c_i32 == nullptr, W8A8_ERR_INVALID_ARG, "gemm_allreduce: no int32 output in fused mode");
+    // receive slots hold whole (padded) tiles
+    W8A8_REQUIRE(static_cast<unsigned long long>(p.num_tiles) * 128 * p.bn * 2 <= comm->slot_bytes,
+                 W8A8_ERR_INVALID_ARG,
+                 "gemm_allreduce: %d padded %dx%d output tiles exceed the communicator's max_bytes %llu", p.num_tiles,
+                 p.swap ? p.bn : 128, p.swap ? 128 : p.bn, comm->slot_bytes);
   }
   if (p.cut_tiles) {
     W8A8_REQUIRE(workspace != nullptr && workspace_bytes >= p.ws_bytes, W8A8_ERR_WORKSPACE,
@@ -168,7 +173,11 @@ int run_gemm(const int8_t* A, const int8_t* B, const float* sa, const float* sb,
   args.units = p.units;
   args.wide_fast = p.wide_fast;
 
-  if (comm) return dispatch_variant<true>(p, tw, tn, args, *comm, stream);
+  if (comm) {
+    CommView cv = *comm;
+    if (p.swap) cv.two_shot = 0;  // weight-stationary tiles push every partial to every rank
+    return dispatch_variant<true>(p, tw, tn, args, cv, stream);
+  }
   CommView none;
   std::memset(&none, 0, sizeof(none));
   return dispatch_variant<false>(p, tw, tn, args, none, stream);

@@ -99,7 +99,9 @@ struct GemmTraits {
   static constexpr int kTmemCols = (2 * BN) <= 32 ? 32 : (2 * BN) <= 64 ? 64 : (2 * BN) <= 128 ? 128
                                    : (2 * BN) <= 256 ? 256 : 512;
   static constexpr int kBarrierBytes = 256;
-  static constexpr int kSmemBytes = 1024 + STAGES * kStageBytes + kBarrierBytes;
+  static constexpr int kStagingBytes = 4 * 2048;  // fused epilogue: 2 KB transpose buffer per warp
+  static constexpr int kTileOutBytes = 128 * BN * 2;  // one tile's bf16 block in a receive slot
+  static constexpr int kSmemBytes = 1024 + STAGES * kStageBytes + kBarrierBytes + kStagingBytes;
   static constexpr int kThreads = 192;
   static constexpr uint32_t kIdesc = dev::idesc_i8(kBM, BN);
   static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "MMA N");
@@ -165,18 +167,17 @@ __device__ __forceinline__ float dequant1(int32_t acc, float sa, float sb) {
   return __fmul_rn(__fmul_rn(__int2float_rn(acc), sa), sb);
 }
 
-// Dequantise CH accumulators of one TMEM row and store them into `out`
-// ([M, N] bf16, row stride a.ldc).
+// Dequantise CH accumulators of one TMEM row and hand the bf16 values to the
+// emitters: emit16(m, n, 8 packed values) / emit2(m, n, 1 value).
 //   normal: row = token m, the values are channels col0..col0+CH-1.
 //   swap:   row = channel n, the values are tokens col0..col0+CH-1.
-template <bool SWAP, int CH>
-__device__ __forceinline__ void store_chunk(const GemmArgs& a, __nv_bfloat16* out, int row, int col0,
-                                            const uint32_t (&v)[32]) {
+template <bool SWAP, int CH, class Emit16, class Emit2>
+__device__ __forceinline__ void store_chunk(const GemmArgs& a, int row, int col0, const uint32_t (&v)[32],
+                                            Emit16&& emit16, Emit2&& emit2) {
   if (!SWAP) {
     const int m = row;
     if (m >= a.M) return;
     const float sam = __ldg(a.sa + m);
-    __nv_bfloat16* crow = out + static_cast<int64_t>(m) * a.ldc;
 #pragma unroll
     for (int g = 0; g < CH / 8; ++g) {
       const int n = col0 + g * 8;
@@ -194,7 +195,7 @@ __device__ __forceinline__ void store_chunk(const GemmArgs& a, __nv_bfloat16* ou
         }
         h[j] = __floats2bfloat162_rn(y0, y1);
       }
-      *reinterpret_cast<uint4*>(crow + n) = pk;
+      emit16(m, n, pk);
       if (a.c_i32) {
         int4* dst = reinterpret_cast<int4*>(a.c_i32 + static_cast<int64_t>(m) * a.N + n);
         dst[0] = make_int4(v[g * 8 + 0], v[g * 8 + 1], v[g * 8 + 2], v[g * 8 + 3]);
@@ -212,10 +213,16 @@ __device__ __forceinline__ void store_chunk(const GemmArgs& a, __nv_bfloat16* ou
       if (m >= a.M) break;
       float y = dequant1(static_cast<int32_t>(v[j]), __ldg(a.sa + m), sbn);
       if (a.bias) y = __fadd_rn(y, bn);
-      out[static_cast<int64_t>(m) * a.ldc + n] = __float2bfloat16_rn(y);
+      emit2(m, n, __float2bfloat16_rn(y));
       if (a.c_i32) a.c_i32[static_cast<int64_t>(m) * a.N + n] = static_cast<int32_t>(v[j]);
     }
   }
+}
+
+// Fused mode: rank of the owner of row (m - m0) of a tile of hm rows when the
+// rows are shared out evenly between the ranks (two-shot).
+__device__ __forceinline__ int row_owner(int m, int m0, int hm, int world) {
+  return ((m - m0 + 1) * world - 1) / hm;
 }
 
 // Output rectangle of a tile in C coordinates: rows [m0, m0+hm), columns
@@ -242,127 +249,169 @@ __device__ __forceinline__ void tile_rect(const GemmArgs& a, int tile, int& m0, 
 constexpr int kReduceThreads = 192;
 constexpr int kReduceBar = 2;
 
-// Reduce-scatter of one tile share: rank-order fp32 sum of vectors [lo, hi)
-// of the tile rectangle from every rank, written in place into this rank's
-// buffer.  W = world (compile-time), so each thread keeps 8 / W vectors x W
-// ranks = 8 independent 16-byte loads in flight before it adds anything.
-template <int W>
-__device__ __forceinline__ void reduce_share(const CommView& cv, uint32_t epoch, const GemmArgs& a, int m0, int n0,
-                                             int vpr, int lo, int hi, int tid) {
-  constexpr int V = 8 / W;
-  const char* src[W];
-#pragma unroll
-  for (int r = 0; r < W; ++r) src[r] = dev::half_ptr(cv, r, epoch);
-  char* mine = dev::half_ptr(cv, cv.rank, epoch);
-  for (int base = lo + tid; base < hi; base += kReduceThreads * V) {
-    uint4 buf[V][W];
-    size_t off[V];
+// Receive-slot layout of one tile (block of 128 x BN bf16 at t * kTileOutBytes):
+//   normal: [chunk c = 0..BN/32)[row 0..127][32 columns]  (64-byte row pieces,
+//           so the 128 rows of a chunk are 8 KB contiguous)
+//   swap:   [token 0..BN)[128 channels]
+// Vector (8 bf16) v of the block maps to tile row r / column col (in C).
+template <int BN, bool SWAP>
+__device__ __forceinline__ void block_vec_rc(int v, int& r, int& col) {
+  if constexpr (!SWAP) {
+    const int c = v >> 9;          // 512 vectors per chunk
+    const int rem = v & 511;
+    r = rem >> 2;
+    col = c * 32 + (rem & 3) * 8;
+  } else {
+    r = v >> 4;                    // 16 vectors per token
+    col = (v & 15) * 8;
+  }
+}
+
+// Sum vectors `vec` (a batch of up to 8 / W block vectors per thread) of a
+// tile block over the world receive slots of this rank (every rank's partial,
+// pushed here by the epilogues): fp32 in rank order, one bf16 rounding; the
+// result goes to C and, with push_gather, into every other rank's gather slot
+// at the same block offset.  All loads are local; W = world at compile time
+// keeps 8 independent 16-byte loads in flight per thread (W = 0: any world).
+template <int W, int BN, bool SWAP, class VecOf>
+__device__ __forceinline__ void reduce_block(const GemmArgs& a, const CommView& cv, uint32_t epoch, int t, int m0,
+                                             int n0, int nvec, VecOf vec_of, int tid, bool push_gather) {
+  constexpr int V = W > 0 ? 8 / W : 1;
+  constexpr int TILE = 128 * BN * 2;
+  const int world = W > 0 ? W : cv.world;
+  const char* slot0 = dev::recv_slot(cv, cv.rank, 0, epoch) + static_cast<size_t>(t) * TILE;
+  const size_t sstride = cv.slot_bytes;
+  for (int base = tid; base < nvec; base += kReduceThreads * V) {
+    uint4 buf[V][W > 0 ? W : 1];
 #pragma unroll
     for (int j = 0; j < V; ++j) {
       const int i = base + j * kReduceThreads;
-      const int r = i / vpr, c = i - r * vpr;
-      off[j] = (static_cast<size_t>(m0 + r) * a.N + n0 + c * 8) * 2;
-      if (i < hi) {
+      if (i < nvec) {
+        const size_t off = static_cast<size_t>(vec_of(i)) * 16;
+        if constexpr (W > 0) {
 #pragma unroll
-        for (int q = 0; q < W; ++q) buf[j][q] = dev::ld_volatile_v4(src[q] + off[j]);
+          for (int q = 0; q < W; ++q) buf[j][q] = dev::ld_volatile_v4(slot0 + q * sstride + off);
+        } else {
+          buf[j][0] = dev::ld_volatile_v4(slot0 + off);
+        }
       }
     }
 #pragma unroll
     for (int j = 0; j < V; ++j) {
-      if (base + j * kReduceThreads < hi) {
-        float acc[8];
-        const __nv_bfloat162* h0 = reinterpret_cast<const __nv_bfloat162*>(&buf[j][0]);
+      const int i = base + j * kReduceThreads;
+      if (i >= nvec) continue;
+      const int v = vec_of(i);
+      const size_t off = static_cast<size_t>(v) * 16;
+      float acc[8];
+      {
+        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&buf[j][0]);
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-          const float2 f = __bfloat1622float2(h0[e]);
+          const float2 f = __bfloat1622float2(h[e]);
           acc[2 * e] = f.x;
           acc[2 * e + 1] = f.y;
         }
-#pragma unroll
-        for (int q = 1; q < W; ++q) {
-          const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&buf[j][q]);
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const float2 f = __bfloat1622float2(h[e]);
-            acc[2 * e] = __fadd_rn(acc[2 * e], f.x);
-            acc[2 * e + 1] = __fadd_rn(acc[2 * e + 1], f.y);
-          }
+      }
+      for (int q = 1; q < world; ++q) {
+        uint4 raw;
+        if constexpr (W > 0) {
+          raw = buf[j][q];
+        } else {
+          raw = dev::ld_volatile_v4(slot0 + q * sstride + off);
         }
-        uint4 o;
-        __nv_bfloat162* ho = reinterpret_cast<__nv_bfloat162*>(&o);
+        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw);
 #pragma unroll
-        for (int e = 0; e < 4; ++e) ho[e] = __floats2bfloat162_rn(acc[2 * e], acc[2 * e + 1]);
-        *reinterpret_cast<uint4*>(mine + off[j]) = o;
+        for (int e = 0; e < 4; ++e) {
+          const float2 f = __bfloat1622float2(h[e]);
+          acc[2 * e] = __fadd_rn(acc[2 * e], f.x);
+          acc[2 * e + 1] = __fadd_rn(acc[2 * e + 1], f.y);
+        }
+      }
+      uint4 o;
+      __nv_bfloat162* ho = reinterpret_cast<__nv_bfloat162*>(&o);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) ho[e] = __floats2bfloat162_rn(acc[2 * e], acc[2 * e + 1]);
+      int r, col;
+      block_vec_rc<BN, SWAP>(v, r, col);
+      const int m = m0 + r, n = n0 + col;
+      if (m < a.M && n < a.N) *reinterpret_cast<uint4*>(a.C + static_cast<size_t>(m) * a.ldc + n) = o;
+      if (push_gather) {
+        for (int d = 0; d < world; ++d) {
+          if (d == cv.rank) continue;
+          *reinterpret_cast<uint4*>(dev::gather_slot(cv, d, epoch) + static_cast<size_t>(t) * TILE + off) = o;
+        }
       }
     }
   }
 }
 
-// Any world size: one vector at a time, ranks summed in order.
-__device__ __forceinline__ void reduce_share_any(const CommView& cv, uint32_t epoch, const GemmArgs& a, int m0,
-                                                 int n0, int vpr, int lo, int hi, int tid) {
-  char* mine = dev::half_ptr(cv, cv.rank, epoch);
-  for (int i = lo + tid; i < hi; i += kReduceThreads) {
-    const int r = i / vpr, c = i - r * vpr;
-    const size_t off = (static_cast<size_t>(m0 + r) * a.N + n0 + c * 8) * 2;
-    *reinterpret_cast<uint4*>(mine + off) = dev::sum_ranks_vec8(cv, epoch, off);
+template <int BN, bool SWAP, class VecOf>
+__device__ __forceinline__ void reduce_block_any_world(const GemmArgs& a, const CommView& cv, uint32_t epoch, int t,
+                                                       int m0, int n0, int nvec, VecOf vec_of, int tid,
+                                                       bool push_gather) {
+  switch (cv.world) {
+    case 2: reduce_block<2, BN, SWAP>(a, cv, epoch, t, m0, n0, nvec, vec_of, tid, push_gather); break;
+    case 4: reduce_block<4, BN, SWAP>(a, cv, epoch, t, m0, n0, nvec, vec_of, tid, push_gather); break;
+    case 8: reduce_block<8, BN, SWAP>(a, cv, epoch, t, m0, n0, nvec, vec_of, tid, push_gather); break;
+    default: reduce_block<0, BN, SWAP>(a, cv, epoch, t, m0, n0, nvec, vec_of, tid, push_gather); break;
   }
 }
 
-// Two-shot reduction of the tiles this CTA owns (t % gridDim.x == blockIdx.x)
-// across the ranks, by all kReduceThreads threads of the CTA (index tid).
+// Reduction of the tiles this CTA owns (t % gridDim.x == blockIdx.x) from the
+// partials the epilogues of every rank pushed into this rank's receive slots.
+//   one-shot: wait for every rank's ready(t), reduce the whole tile into C.
+//   two-shot: wait for ready(t), reduce this rank's row share into C and push
+//             it into every other rank's gather slot, raise gathered(t);
+//             then wait for every rank's gathered(t) and copy their shares
+//             from the local gather slot into C.
 // Returns false if a flag wait timed out (uniformly across the threads).
 template <int BN, bool SWAP>
 __device__ bool fused_reduce_tiles(const GemmArgs& a, const CommView& cv, uint32_t epoch, int tid) {
-  // shot 1: reduce-scatter of every owned tile
+  constexpr int TILE = 128 * BN * 2;
+  constexpr int NV = TILE / 16;  // vectors per tile block
   for (int t = blockIdx.x; t < a.num_tiles; t += gridDim.x) {
     const bool ok = dev::wait_peer(cv, 0, t, epoch, tid);
     if (dev::named_bar_or(kReduceBar, kReduceThreads, !ok)) return false;
     int m0, hm, n0, wn;
     tile_rect<BN, SWAP>(a, t, m0, hm, n0, wn);
-    const int vpr = wn >> 3;
-    const int nv = hm * vpr;
-    const int lo = static_cast<int>((static_cast<long long>(nv) * cv.rank) / cv.world);
-    const int hi = static_cast<int>((static_cast<long long>(nv) * (cv.rank + 1)) / cv.world);
-    switch (cv.world) {
-      case 2: reduce_share<2>(cv, epoch, a, m0, n0, vpr, lo, hi, tid); break;
-      case 4: reduce_share<4>(cv, epoch, a, m0, n0, vpr, lo, hi, tid); break;
-      case 8: reduce_share<8>(cv, epoch, a, m0, n0, vpr, lo, hi, tid); break;
-      default: reduce_share_any(cv, epoch, a, m0, n0, vpr, lo, hi, tid); break;
+    if (!cv.two_shot) {
+      reduce_block_any_world<BN, SWAP>(a, cv, epoch, t, m0, n0, NV, [](int i) { return i; }, tid, false);
+    } else {
+      // rows [r0, r1) of every chunk: (r1 - r0) * 4 vectors per chunk
+      const int r0 = (hm * cv.rank) / cv.world, r1 = (hm * (cv.rank + 1)) / cv.world;
+      const int per_chunk = (r1 - r0) * 4;
+      auto vec_of = [=](int i) { return (i / per_chunk) * 512 + r0 * 4 + (i % per_chunk); };
+      reduce_block_any_world<BN, SWAP>(a, cv, epoch, t, m0, n0, per_chunk * (BN / 32), vec_of, tid, true);
+      dev::named_bar_sync(kReduceBar, kReduceThreads);
+      dev::signal_peers(cv, 1, t, epoch, tid);
     }
-    dev::named_bar_sync(kReduceBar, kReduceThreads);
-    dev::signal_peers(cv, 1, t, epoch, tid);
   }
-  // shot 2: all-gather of every owned tile into C, 8 loads in flight per thread
+  if (!cv.two_shot) return true;
   for (int t = blockIdx.x; t < a.num_tiles; t += gridDim.x) {
     const bool ok = dev::wait_peer(cv, 1, t, epoch, tid);
     if (dev::named_bar_or(kReduceBar, kReduceThreads, !ok)) return false;
     int m0, hm, n0, wn;
     tile_rect<BN, SWAP>(a, t, m0, hm, n0, wn);
-    const int vpr = wn >> 3;
-    const int nv = hm * vpr;
-    for (int src = 0; src < cv.world; ++src) {
-      const int lo = static_cast<int>((static_cast<long long>(nv) * src) / cv.world);
-      const int hi = static_cast<int>((static_cast<long long>(nv) * (src + 1)) / cv.world);
-      const char* from = dev::half_ptr(cv, src, epoch);
-      for (int base = lo + tid; base < hi; base += kReduceThreads * 8) {
-        uint4 v[8];
+    const char* from = dev::gather_slot(cv, cv.rank, epoch) + static_cast<size_t>(t) * TILE;
+    // every vector outside this rank's own row share
+    const int r0 = (hm * cv.rank) / cv.world, r1 = (hm * (cv.rank + 1)) / cv.world;
+    for (int base = tid; base < NV; base += kReduceThreads * 8) {
+      uint4 v[8];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const int i = base + j * kReduceThreads;
-          if (i < hi) {
-            const int r = i / vpr, c = i - r * vpr;
-            v[j] = dev::ld_volatile_v4(from + (static_cast<size_t>(m0 + r) * a.N + n0 + c * 8) * 2);
-          }
-        }
+      for (int j = 0; j < 8; ++j) {
+        const int i = base + j * kReduceThreads;
+        int r, col;
+        block_vec_rc<BN, SWAP>(i, r, col);
+        if (i < NV && (r < r0 || r >= r1)) v[j] = dev::ld_volatile_v4(from + static_cast<size_t>(i) * 16);
+      }
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const int i = base + j * kReduceThreads;
-          if (i < hi) {
-            const int r = i / vpr, c = i - r * vpr;
-            *reinterpret_cast<uint4*>(a.C + static_cast<size_t>(m0 + r) * a.ldc + n0 + c * 8) = v[j];
-          }
-        }
+      for (int j = 0; j < 8; ++j) {
+        const int i = base + j * kReduceThreads;
+        int r, col;
+        block_vec_rc<BN, SWAP>(i, r, col);
+        const int m = m0 + r, n = n0 + col;
+        if (i < NV && (r < r0 || r >= r1) && m < a.M && n < a.N)
+          *reinterpret_cast<uint4*>(a.C + static_cast<size_t>(m) * a.ldc + n) = v[j];
       }
     }
   }
@@ -388,6 +437,7 @@ __global__ void __launch_bounds__(192, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   volatile int* last_flag = abort_flag + 1;
   volatile uint32_t* epoch_slot = reinterpret_cast<volatile uint32_t*>(last_flag + 1);
+  uint8_t* staging = reinterpret_cast<uint8_t*>(bars) + T::kBarrierBytes;  // 16-byte aligned
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -427,7 +477,6 @@ __global__ void __launch_bounds__(192, 1)
   // so read after griddep_wait) selects the data half; partial tiles go there
   // instead of C.
   uint32_t epoch = 0;
-  __nv_bfloat16* out = args.C;
 
   if (warp == 0) {
     if (lane == 0) {
@@ -564,10 +613,58 @@ __global__ void __launch_bounds__(192, 1)
   } else {
     // ------------------------------------------------------------ epilogue
     dev::griddep_wait();
-    if constexpr (FUSED) {
-      epoch = dev::ld_relaxed_gpu(dev::ctrl_ptr(cv.base[cv.rank])) + 1u;
-      out = reinterpret_cast<__nv_bfloat16*>(dev::half_ptr(cv, cv.rank, epoch));
-    }
+    if constexpr (FUSED) epoch = dev::ld_relaxed_gpu(dev::ctrl_ptr(cv.base[cv.rank])) + 1u;
+    // Where a finished tile's bf16 values go.  Plain: C.  Fused: this rank's
+    // receive slot (tile-blocked layout) on every rank (one-shot) or on the
+    // rank owning the row (two-shot) -- remote stores over NVLink that overlap
+    // the next tile's MMAs.  Normal-orientation values are transposed through
+    // a 2 KB per-warp staging buffer so that every store instruction of a warp
+    // writes 512 contiguous bytes; weight-stationary tiles (M <= 64, always
+    // one-shot) store token rows of 64 contiguous bytes per warp directly.
+    const size_t my_slot = kHeaderBytes + static_cast<size_t>(epoch & 1u) * cv.half_bytes +
+                           static_cast<size_t>(cv.rank) * cv.slot_bytes;
+    uint4* stg = reinterpret_cast<uint4*>(staging + (warp & 3) * 2048);
+    int cur_m0 = 0, cur_hm = 1, cur_n0 = 0, cur_tile = 0;
+    auto emit16 = [&](int m, int n, const uint4& val) {
+      if constexpr (!FUSED) {
+        *reinterpret_cast<uint4*>(args.C + static_cast<size_t>(m) * args.ldc + n) = val;
+      } else {
+        stg[lane * 4 + ((n - cur_n0) & 31) / 8] = val;  // [row in warp][16-byte piece of the 64-byte chunk]
+      }
+    };
+    auto emit2 = [&](int m, int n, __nv_bfloat16 val) {
+      if constexpr (!FUSED) {
+        args.C[static_cast<size_t>(m) * args.ldc + n] = val;
+      } else {
+        const size_t off = static_cast<size_t>(cur_tile) * T::kTileOutBytes +
+                           (static_cast<size_t>(m - cur_m0) * 128 + (n - cur_n0)) * 2;
+        for (int d = 0; d < cv.world; ++d) *reinterpret_cast<__nv_bfloat16*>(cv.base[d] + my_slot + off) = val;
+      }
+    };
+    // Fused normal orientation: after a chunk's values are staged, the warp
+    // pushes its 32 rows x 64 bytes (2 KB contiguous in the tile block).
+    auto push_chunk = [&](int c) {
+      if constexpr (FUSED && !SWAP) {
+        __syncwarp();
+        const size_t blk = static_cast<size_t>(cur_tile) * T::kTileOutBytes + static_cast<size_t>(c) * 8192 +
+                           static_cast<size_t>(warp & 3) * 2048;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int k = lane + 32 * j;  // 16-byte piece k of the warp's 2 KB
+          const int r = (warp & 3) * 32 + (k >> 2);
+          if (r >= cur_hm) continue;    // padding rows of a bottom tile are never read: not pushed
+          const uint4 val = stg[k];
+          const size_t off = blk + static_cast<size_t>(k) * 16;
+          if (cv.two_shot) {
+            const int owner = min(row_owner(cur_m0 + r, cur_m0, cur_hm, cv.world), cv.world - 1);
+            *reinterpret_cast<uint4*>(cv.base[owner] + my_slot + off) = val;
+          } else {
+            for (int d = 0; d < cv.world; ++d) *reinterpret_cast<uint4*>(cv.base[d] + my_slot + off) = val;
+          }
+        }
+        __syncwarp();
+      }
+    };
     const int quarter = warp & 3;
     const int row_in_tile = quarter * 32 + lane;
     const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
@@ -581,6 +678,11 @@ __global__ void __launch_bounds__(192, 1)
     while (walk.next(tile, kb0, kb1)) {
       int tw, tn;
       tile_coords(args, tile, tw, tn);
+      if constexpr (FUSED) {
+        int wn_;
+        tile_rect<BN, SWAP>(args, tile, cur_m0, cur_hm, cur_n0, wn_);
+        cur_tile = tile;
+      }
       const bool ok = dev::mbar_wait(dev::smem_u32(acc_full + acc), acc_phase, abort_flag, args.err,
                                      kErrGemmWait, tmo);
       if (dev::named_bar_or(1, 128, !ok)) {  // uniform exit of all epilogue threads
@@ -602,7 +704,8 @@ __global__ void __launch_bounds__(192, 1)
             dev::tc_fence_before();
             dev::mbar_arrive(dev::smem_u32(acc_empty + acc));
           }
-          store_chunk<SWAP, T::kChunk>(args, out, row, tn * BN + c * T::kChunk, v);
+          store_chunk<SWAP, T::kChunk>(args, row, tn * BN + c * T::kChunk, v, emit16, emit2);
+          push_chunk(c);
         }
       } else {
         // partial fragment: park the int32 tile in this CTA's slot
@@ -647,7 +750,8 @@ __global__ void __launch_bounds__(192, 1)
               for (int j = 0; j < T::kChunk; ++j)
                 v[j] = static_cast<uint32_t>(static_cast<int32_t>(v[j]) + __ldcg(p + j * T::kBM));
             }
-            store_chunk<SWAP, T::kChunk>(args, out, row, tn * BN + c * T::kChunk, v);
+            store_chunk<SWAP, T::kChunk>(args, row, tn * BN + c * T::kChunk, v, emit16, emit2);
+            push_chunk(c);
           }
           if (et == 0) args.counters[tile] = 0u;
         }

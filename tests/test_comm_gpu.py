@@ -124,9 +124,14 @@ def _scn_random_bit_exact(pkg, O, rank, world, dev, dist):
 def _scn_gemm_allreduce(pkg, O, rank, world, dev, dist):
     """Fused row-parallel GEMM + all-reduce == oracle tp_linear("row"), bit-exact."""
     comm = pkg.comm.PeerMemCommunicator(rank, world, 2048 * 5120 * 2, device=dev)
-    for (m, n, kfull, bias) in [(1, 5120, 1024 * world, False), (16, 4096, 512 * world, True),
-                                (64, 1024, 256 * world, False), (200, 2048, 384 * world, False),
-                                (1024, 5120, 512 * world, False), (2048, 1536, 128 * world, True)]:
+    cases = [(0, 1, 5120, 1024 * world, False), (0, 16, 4096, 512 * world, True),
+             (0, 64, 1024, 256 * world, False), (0, 200, 2048, 384 * world, False),
+             (0, 1024, 5120, 512 * world, False), (0, 2048, 1536, 128 * world, True),
+             # forced one-shot and two-shot reductions on normal-orientation tiles
+             (1, 333, 4096, 256 * world, False), (2, 333, 4096, 256 * world, True),
+             (2, 1024, 5120, 512 * world, False), (2, 65, 2048, 128 * world, False)]
+    for (mode, m, n, kfull, bias) in cases:
+        comm.set_mode(mode)
         g = torch.Generator().manual_seed(m * 7 + n)
         x = torch.randn(m, kfull, generator=g).bfloat16()
         w = (torch.randn(n, kfull, generator=g) * 0.02).bfloat16()
@@ -138,7 +143,7 @@ def _scn_gemm_allreduce(pkg, O, rank, world, dev, dist):
         q, s = pkg.ops.quant_per_token(xs)
         y = comm.gemm_allreduce(q, wshard, s, ws.to(dev), None if b is None else b.to(dev))
         torch.cuda.synchronize()
-        assert torch.equal(y.cpu(), want), f"m={m} n={n} k={kfull}"
+        assert torch.equal(y.cpu(), want), f"mode={mode} m={m} n={n} k={kfull}"
     assert comm.device_error() == 0
     comm.close()
     return True
