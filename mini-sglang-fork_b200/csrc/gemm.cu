@@ -8,7 +8,7 @@
 #include <mutex>
 
 #include "common.cuh"
-#include "gemm_sm100.cuh"
+#include "gemm2_sm100.cuh"
 #include "gemm_api.h"
 #include "gemm_plan.h"
 
@@ -87,6 +87,26 @@ int validate_gemm_args(const int8_t* A, const int8_t* B, const float* sa, const 
   return W8A8_OK;
 }
 
+template <int STAGES, bool FUSED>
+int launch_pair_variant(const GemmPlan& p, const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& args,
+                        const CommView& cv, cudaStream_t stream) {
+  using T = Gemm2Traits<STAGES>;
+  auto kern = w8a8_gemm2_kernel<STAGES, FUSED>;
+  static std::mutex mu;
+  static bool configured[64] = {false};
+  const int dev = current_device();
+  W8A8_REQUIRE(dev >= 0 && dev < 64, W8A8_ERR_CUDA, "no current device");
+  {
+    std::lock_guard<std::mutex> lk(mu);
+    if (!configured[dev]) {
+      W8A8_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, T::kSmemBytes));
+      configured[dev] = true;
+    }
+  }
+  W8A8_CUDA_TRY(launch_pdl(kern, dim3(p.grid), dim3(T::kThreads), T::kSmemBytes, stream, ta, tb, args, cv));
+  return W8A8_OK;
+}
+
 template <bool FUSED>
 int dispatch_variant(const GemmPlan& p, const CUtensorMap& tw, const CUtensorMap& tn, const GemmArgs& args,
                      const CommView& cv, cudaStream_t stream) {
@@ -97,6 +117,7 @@ int dispatch_variant(const GemmPlan& p, const CUtensorMap& tw, const CUtensorMap
     case 4: return launch_variant<32, 9, true, FUSED>(p, tw, tn, args, cv, stream);
     case 5: return launch_variant<64, 8, true, FUSED>(p, tw, tn, args, cv, stream);
     case 6: return launch_variant<128, 6, true, FUSED>(p, tw, tn, args, cv, stream);
+    case 7: return launch_pair_variant<6, FUSED>(p, tw, tn, args, cv, stream);
     default: return fail(W8A8_ERR_INVALID_ARG, "gemm: unknown variant %d", p.variant);
   }
 }
@@ -144,7 +165,7 @@ int run_gemm(const int8_t* A, const int8_t* B, const float* sa, const float* sb,
   CUtensorMap tw, tn;
   rc = encode_operand(&tw, wide, rows_w, K, 128);
   if (rc) return rc;
-  rc = encode_operand(&tn, narrow, rows_n, K, p.bn);
+  rc = encode_operand(&tn, narrow, rows_n, K, p.variant == 7 ? 128 : p.bn);
   if (rc) return rc;
 
   GemmArgs args;
@@ -224,7 +245,7 @@ int w8a8_gemm(const int8_t* A, const int8_t* B, const float* sa, const float* sb
 int w8a8_gemm_config(const int8_t* A, const int8_t* B, const float* sa, const float* sb, const void* bias,
                      void* C, int32_t* c_i32, int64_t M, int64_t N, int64_t K, int variant, int ctas,
                      void* workspace, size_t workspace_bytes, void* stream) {
-  W8A8_REQUIRE(variant >= 0 && variant <= 6, W8A8_ERR_INVALID_ARG, "gemm_config: variant %d out of range",
+  W8A8_REQUIRE(variant >= 0 && variant <= 7, W8A8_ERR_INVALID_ARG, "gemm_config: variant %d out of range",
                variant);
   W8A8_REQUIRE(ctas >= 0, W8A8_ERR_INVALID_ARG, "gemm_config: negative ctas");
   return w8a8::run_gemm(A, B, sa, sb, bias, C, c_i32, M, N, K, variant, ctas, workspace, workspace_bytes,

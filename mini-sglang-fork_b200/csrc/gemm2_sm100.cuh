@@ -1,0 +1,348 @@
+// Kernel 2, pair variant: W8A8 GEMM with the 2-SM MMA (tcgen05 cta_group::2)
+// for large (prefill) shapes, optionally fused with the row-parallel reduce.
+//
+// A cluster of two CTAs computes one 256 x 256 output block: CTA h of the
+// pair stages rows [128h, 128h + 128) of the A block and rows
+// [128h, 128h + 128) of the 256-row B (weight) block, 32 KB per 128-byte k
+// block; the even CTA issues tcgen05.mma.cta_group::2 (M = 256, N = 256,
+// K = 32), which reads both CTAs' shared memory and writes each CTA's own 128
+// TMEM lanes x 256 columns.  Per SM that is 128 MACs per staged byte against
+// 87 for the single-CTA 128 x 256 tile, which is what the single-CTA kernel is
+// bound by at prefill sizes.
+//
+// Synchronisation across the pair (no cluster multicast anywhere):
+//   * both producers load into their own shared memory and count the bytes
+//     on the leader's `full` barrier (cp.async.bulk.tensor ... cta_group::2);
+//     the leader arms it for both CTAs' bytes;
+//   * the leader's MMA thread frees a stage in both CTAs and announces a
+//     finished accumulator to both CTAs with one tcgen05.commit per CTA;
+//   * both epilogues release the accumulator on the leader's `acc_empty`
+//     barrier (the odd CTA with a remote arrive).
+// The schedule is whole 256 x 256 blocks in grid-stride order over the pairs
+// (the planner only picks this variant when that keeps every pair busy).  An
+// odd number of 128-row tiles leaves the last pair's second half outside C:
+// that CTA computes it (zero rows) and stores nothing.  Output tiles keep the
+// 128 x 256 numbering of the single-CTA BN = 256 variant, so the fused reduce,
+// its flags and receive-slot layout are shared with it.
+#pragma once
+
+#include "gemm_sm100.cuh"
+
+namespace w8a8 {
+
+template <int STAGES>
+struct Gemm2Traits {
+  static constexpr int kBK = 128;
+  static constexpr int kTileABytes = 128 * kBK;  // this CTA's 128 rows of A
+  static constexpr int kTileBBytes = 128 * kBK;  // this CTA's 128 rows of B
+  static constexpr int kStageBytes = kTileABytes + kTileBBytes;
+  static constexpr int kBN = 256;
+  static constexpr int kAccCols = 256;
+  static constexpr int kTmemCols = 512;
+  static constexpr int kBarrierBytes = 256;
+  static constexpr int kStagingBytes = 4 * 2048;
+  static constexpr int kTileOutBytes = 128 * kBN * 2;
+  static constexpr int kSmemBytes = 1024 + STAGES * kStageBytes + kBarrierBytes + kStagingBytes;
+  static constexpr int kThreads = 192;
+  static constexpr uint32_t kIdesc = dev::idesc_i8(256, 256);
+  static_assert(kSmemBytes <= 227 * 1024, "shared memory");
+};
+
+// Pair p -> (pw, tn): 256-row block index and 256-column block index.
+__device__ __forceinline__ void pair_coords(const GemmArgs& a, int pairs_w, int p, int& pw, int& tn) {
+  if (a.wide_fast) {
+    pw = p % pairs_w;
+    tn = p / pairs_w;
+  } else {
+    tn = p % a.tiles_n;
+    pw = p / a.tiles_n;
+  }
+}
+
+// Index of output tile (tw, tn) in tile_coords' numbering.
+__device__ __forceinline__ int tile_index(const GemmArgs& a, int tw, int tn) {
+  return a.wide_fast ? tn * a.tiles_w + tw : tw * a.tiles_n + tn;
+}
+
+template <int STAGES, bool FUSED>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
+    w8a8_gemm2_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
+                      const GemmArgs args, const CommView cv) {
+  using T = Gemm2Traits<STAGES>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* s_a = smem;
+  uint8_t* s_b = smem + STAGES * T::kTileABytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(s_b + STAGES * T::kTileBBytes);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + STAGES;
+  uint64_t* acc_full = bars + 2 * STAGES;
+  uint64_t* acc_empty = acc_full + 2;
+  uint64_t* drain = acc_empty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  volatile uint32_t* epoch_slot = reinterpret_cast<volatile uint32_t*>(abort_flag + 2);
+  uint8_t* staging = reinterpret_cast<uint8_t*>(bars) + T::kBarrierBytes;
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t half = dev::cluster_rank();  // 0 = leader
+  const int cluster = blockIdx.x >> 1;
+  const int nclusters = gridDim.x >> 1;
+  const int pairs_w = (args.tiles_w + 1) >> 1;
+  const int num_pairs = pairs_w * args.tiles_n;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      dev::mbar_init(dev::smem_u32(full + s), 1);
+      dev::mbar_init(dev::smem_u32(empty + s), 1);
+    }
+    for (int s = 0; s < 2; ++s) {
+      dev::mbar_init(dev::smem_u32(acc_full + s), 1);
+      dev::mbar_init(dev::smem_u32(acc_empty + s), 256);  // 128 epilogue threads of each CTA
+    }
+    dev::mbar_init(dev::smem_u32(drain), 1);
+    *abort_flag = 0;
+    dev::fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    dev::prefetch_tmap(&tm_a);
+    dev::prefetch_tmap(&tm_b);
+  }
+  if (warp == 1) {
+    dev::tmem_alloc2(dev::smem_u32(tmem_slot), T::kTmemCols);
+    dev::tmem_relinquish2();
+  }
+  dev::tc_fence_before();
+  dev::cluster_sync();  // barriers of both CTAs initialised before any cross-CTA use
+  dev::tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const long long tmo = args.timeout_ns;
+  dev::griddep_launch();
+  uint32_t epoch = 0;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------------------------------------------------- producer
+      dev::griddep_wait();
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t issued_mask = 0, issued_phase = 0;
+      bool ok = true;
+      for (int p = cluster; p < num_pairs && ok; p += nclusters) {
+        int pw, tn;
+        pair_coords(args, pairs_w, p, pw, tn);
+        const int tw = 2 * pw + static_cast<int>(half);
+        for (int kb = 0; kb < args.kblocks; ++kb) {
+          if (!dev::mbar_wait(dev::smem_u32(empty + stage), phase ^ 1u, abort_flag, args.err, kErrGemmWait,
+                              tmo)) {
+            ok = false;
+            break;
+          }
+          const uint32_t leader_full = dev::mapa(dev::smem_u32(full + stage), 0);
+          if (half == 0) dev::mbar_expect_tx(dev::smem_u32(full + stage), 2 * T::kStageBytes);
+          dev::tma_load_2d_pair(dev::smem_u32(s_a + stage * T::kTileABytes), &tm_a, leader_full, kb * T::kBK,
+                                tw * 128);
+          dev::tma_load_2d_pair(dev::smem_u32(s_b + stage * T::kTileBBytes), &tm_b, leader_full, kb * T::kBK,
+                                tn * 256 + static_cast<int>(half) * 128);
+          issued_mask |= 1u << stage;
+          issued_phase = (issued_phase & ~(1u << stage)) | (phase << stage);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      // The leader's full barriers count both CTAs' bytes: once they have
+      // landed, no copy of either CTA is in flight (the pair then meets at the
+      // closing cluster barrier).
+      if (half == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+          if (issued_mask & (1u << s)) {
+            if (!dev::mbar_wait_drain(dev::smem_u32(full + s), (issued_phase >> s) & 1u, tmo)) {
+              if (args.err) atomicOr(args.err, kErrGemmDrain);
+            }
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && half == 0) {
+      // --------------------------------------------- MMA issuer (leader only)
+      dev::griddep_wait();
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      for (int p = cluster; p < num_pairs && ok; p += nclusters) {
+        if (!dev::mbar_wait_cluster(dev::smem_u32(acc_empty + acc), acc_phase ^ 1u, abort_flag, args.err,
+                                    kErrGemmWait, tmo)) {
+          break;
+        }
+        dev::tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * T::kAccCols);
+        for (int kb = 0; kb < args.kblocks; ++kb) {
+          if (!dev::mbar_wait(dev::smem_u32(full + stage), phase, abort_flag, args.err, kErrGemmWait, tmo)) {
+            ok = false;
+            break;
+          }
+          dev::tc_fence_after();
+          const uint64_t da = dev::sdesc_k_sw128(dev::smem_u32(s_a + stage * T::kTileABytes));
+          const uint64_t db = dev::sdesc_k_sw128(dev::smem_u32(s_b + stage * T::kTileBBytes));
+#pragma unroll
+          for (int k = 0; k < T::kBK / 32; ++k) {
+            const uint64_t off = static_cast<uint64_t>((k * 32) >> 4);
+            dev::mma_i8_pair(d_tmem, da + off, db + off, T::kIdesc, (kb > 0 || k > 0) ? 1u : 0u);
+          }
+          dev::tc_commit_pair(dev::smem_u32(empty + stage));
+          dev::tc_commit_pair(dev::mapa(dev::smem_u32(empty + stage), 1));
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        dev::tc_commit_pair(dev::smem_u32(acc_full + acc));
+        dev::tc_commit_pair(dev::mapa(dev::smem_u32(acc_full + acc), 1));
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1u;
+        }
+      }
+      dev::tc_commit_pair(dev::smem_u32(drain));
+      if (!dev::mbar_wait_drain(dev::smem_u32(drain), 0, tmo)) {
+        if (args.err) atomicOr(args.err, kErrGemmDrain);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    dev::griddep_wait();
+    if constexpr (FUSED) epoch = dev::ld_relaxed_gpu(dev::ctrl_ptr(cv.base[cv.rank])) + 1u;
+    const size_t my_slot = kHeaderBytes + static_cast<size_t>(epoch & 1u) * cv.half_bytes +
+                           static_cast<size_t>(cv.rank) * cv.slot_bytes;
+    uint4* stg = reinterpret_cast<uint4*>(staging + (warp & 3) * 2048);
+    int cur_m0 = 0, cur_hm = 1, cur_n0 = 0, cur_tile = 0;
+    auto emit16 = [&](int m, int n, const uint4& val) {
+      if constexpr (!FUSED) {
+        *reinterpret_cast<uint4*>(args.C + static_cast<size_t>(m) * args.ldc + n) = val;
+      } else {
+        stg[lane * 4 + ((n - cur_n0) & 31) / 8] = val;
+      }
+    };
+    auto emit2 = [&](int, int, __nv_bfloat16) {};  // normal orientation only
+    auto push_chunk = [&](int c) {
+      if constexpr (FUSED) {
+        __syncwarp();
+        const size_t blk = static_cast<size_t>(cur_tile) * T::kTileOutBytes + static_cast<size_t>(c) * 8192 +
+                           static_cast<size_t>(warp & 3) * 2048;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int k = lane + 32 * j;
+          const int r = (warp & 3) * 32 + (k >> 2);
+          if (r >= cur_hm) continue;
+          const uint4 val = stg[k];
+          const size_t off = blk + static_cast<size_t>(k) * 16;
+          if (cv.two_shot) {
+            const int owner = min(row_owner(cur_m0 + r, cur_m0, cur_hm, cv.world), cv.world - 1);
+            *reinterpret_cast<uint4*>(cv.base[owner] + my_slot + off) = val;
+          } else {
+            for (int d = 0; d < cv.world; ++d) *reinterpret_cast<uint4*>(cv.base[d] + my_slot + off) = val;
+          }
+        }
+        __syncwarp();
+      }
+    };
+    const int quarter = warp & 3;
+    const int row_in_tile = quarter * 32 + lane;
+    const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
+    const int et = threadIdx.x - 64;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    bool aborted = false;
+    for (int p = cluster; p < num_pairs; p += nclusters) {
+      int pw, tn;
+      pair_coords(args, pairs_w, p, pw, tn);
+      const int tw = 2 * pw + static_cast<int>(half);
+      const bool real = tw < args.tiles_w;
+      const int tile = real ? tile_index(args, tw, tn) : 0;
+      if constexpr (FUSED) {
+        if (real) {
+          int wn_;
+          tile_rect<256, false>(args, tile, cur_m0, cur_hm, cur_n0, wn_);
+          cur_tile = tile;
+        }
+      }
+      const bool ok = dev::mbar_wait(dev::smem_u32(acc_full + acc), acc_phase, abort_flag, args.err, kErrGemmWait,
+                                     tmo);
+      if (dev::named_bar_or(1, 128, !ok)) {
+        aborted = true;
+        break;
+      }
+      dev::tc_fence_after();
+      const uint32_t t_acc = tmem_base + lane_base + static_cast<uint32_t>(acc * T::kAccCols);
+      const int row = tw * 128 + row_in_tile;
+#pragma unroll 1
+      for (int c = 0; c < 8; ++c) {
+        uint32_t v[32];
+        dev::tmem_ld32(t_acc + c * 32, v);
+        dev::tmem_wait_ld(v);
+        if (c == 7) {
+          dev::tc_fence_before();
+          const uint32_t bar = dev::smem_u32(acc_empty + acc);
+          if (half == 0) {
+            dev::mbar_arrive(bar);
+          } else {
+            dev::mbar_arrive_cluster(dev::mapa(bar, 0));
+          }
+        }
+        if (real) {
+          store_chunk<false, 32>(args, row, tn * 256 + c * 32, v, emit16, emit2);
+          push_chunk(c);
+        }
+      }
+      if constexpr (FUSED) {
+        if (real) {
+          dev::named_bar_sync(1, 128);
+          dev::signal_peers(cv, 0, tile, epoch, et);
+        }
+      }
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1u;
+      }
+    }
+    dev::tc_fence_before();
+    if constexpr (FUSED) {
+      if (aborted) *abort_flag = 1;
+      if (et == 0) *epoch_slot = epoch;
+    }
+  }
+
+  __syncthreads();
+  dev::cluster_sync();  // the pair is done with both CTAs' TMEM and shared memory
+  if (warp == 1) {
+    dev::tc_fence_after();
+    dev::tmem_dealloc2(tmem_base, T::kTmemCols);
+  }
+  if constexpr (FUSED) {
+    epoch = *epoch_slot;
+    if (*abort_flag == 0) {
+      dev::griddep_wait();
+      fused_reduce_tiles<256, false>(args, cv, epoch, threadIdx.x);
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      uint32_t* c = dev::ctrl_ptr(cv.base[cv.rank]);
+      __threadfence();
+      const uint32_t done = atomicAdd(c + 1, 1u);
+      if (done == gridDim.x - 1) {
+        c[1] = 0u;
+        __threadfence();
+        atomicExch(c, epoch);
+      }
+    }
+  }
+}
+
+}  // namespace w8a8

@@ -4,6 +4,8 @@
 // Variants (BM = 128 rows of the "wide" operand per tile, BK = 128):
 //   1: normal, BN = 256   2: normal, BN = 128
 //   3..6: weight-stationary (swap), BN = 16 / 32 / 64 / 128 token columns
+//   7: CTA pairs with the 2-SM MMA, 256 x 256 blocks (two 128 x 256 tiles),
+//      whole blocks in grid-stride order over SM pairs (prefill shapes)
 // Schedule: stream-K over G persistent CTAs (one per SM by default).  The
 // k-block iterations of all tiles are split evenly between the CTAs; tiles cut
 // by a CTA boundary are finished through the workspace (two int32 tile slots
@@ -34,11 +36,20 @@ struct GemmPlan {
 };
 
 inline int variant_bn(int v) {
-  static const int kBn[] = {0, 256, 128, 16, 32, 64, 128};
-  return (v >= 1 && v <= 6) ? kBn[v] : 0;
+  static const int kBn[] = {0, 256, 128, 16, 32, 64, 128, 256};
+  return (v >= 1 && v <= 7) ? kBn[v] : 0;
 }
 
-inline bool variant_swap(int v) { return v >= 3; }
+inline bool variant_swap(int v) { return v >= 3 && v <= 6; }
+
+// Share of SM pairs kept busy when 256 x 256 blocks are dealt whole.
+inline double pair_efficiency(int64_t M, int64_t N, int nsm) {
+  const int64_t pairs = ((M + 255) / 256) * ((N + 255) / 256);
+  const int64_t clusters = nsm / 2;
+  if (clusters <= 0 || pairs < clusters) return 0.0;
+  const int64_t rounds = (pairs + clusters - 1) / clusters;
+  return static_cast<double>(pairs) / static_cast<double>(rounds * clusters);
+}
 
 inline const char* plan_error(int rc) {
   switch (rc) {
@@ -68,12 +79,14 @@ inline int plan_gemm(int64_t M, int64_t N, int64_t K, int variant, int ctas_req,
       v = 4;
     } else if (M <= 64) {
       v = 5;
+    } else if (M > 256 && pair_efficiency(M, N, nsm) >= 0.85) {
+      v = 7;
     } else {
       const int64_t tiles256 = ((M + 127) / 128) * ((N + 255) / 256);
       v = tiles256 >= nsm ? 1 : 2;
     }
   }
-  if (v < 1 || v > 6) return 1;
+  if (v < 1 || v > 7) return 1;
   p->variant = v;
   p->bn = variant_bn(v);
   p->swap = variant_swap(v);
@@ -83,6 +96,24 @@ inline int plan_gemm(int64_t M, int64_t N, int64_t K, int variant, int ctas_req,
   p->tiles_n = static_cast<int>((rows_n + p->bn - 1) / p->bn);
   p->num_tiles = p->tiles_w * p->tiles_n;
   p->kblocks = static_cast<int>((K + 127) / 128);
+  if (v == 7) {
+    // whole 256 x 256 blocks over SM pairs; no stream-K, no workspace
+    const int64_t pairs = static_cast<int64_t>((p->tiles_w + 1) / 2) * p->tiles_n;
+    int64_t clusters = ctas_req > 0 ? ctas_req / 2 : nsm / 2;
+    if (clusters > nsm / 2) clusters = nsm / 2;
+    if (clusters < 1) clusters = 1;
+    if (clusters > pairs) clusters = pairs;
+    p->grid = static_cast<int>(2 * clusters);
+    p->dp_tiles = p->num_tiles;
+    p->gran = p->kblocks;
+    p->units = 0;
+    p->sk_ctas = 1;
+    p->cut_tiles = false;
+    p->ws_counter_bytes = 0;
+    p->ws_bytes = 0;
+    p->wide_fast = (rows_w <= rows_n) ? 1 : 0;
+    return 0;
+  }
   const long long total_iters = static_cast<long long>(p->num_tiles) * p->kblocks;
   long long g = ctas_req > 0 ? (ctas_req < nsm ? ctas_req : nsm) : nsm;
   if (g > total_iters) g = total_iters;

@@ -62,7 +62,8 @@ def test_host_validation_rejects_bad_arguments(pkg):
 @pytest.mark.parametrize("m,n,k,variant,bn,swap", [
     (1, 24576, 4096, 3, 16, 1), (16, 24576, 4096, 3, 16, 1), (17, 24576, 4096, 4, 32, 1),
     (64, 6144, 1024, 5, 64, 1), (65, 6144, 1024, 2, 128, 0), (256, 5120, 8192, 2, 128, 0),
-    (8192, 24576, 4096, 1, 256, 0), (8192, 4096, 12288, 1, 256, 0), (4096, 6400, 5120, 1, 256, 0),
+    (8192, 24576, 4096, 7, 256, 0), (8192, 4096, 12288, 7, 256, 0), (4096, 6400, 5120, 7, 256, 0),
+    (4096, 1280, 8192, 1, 256, 0), (512, 5120, 1024, 2, 128, 0), (8192, 1280, 8192, 1, 256, 0),
 ])
 def test_planner_variant_choice(pkg, m, n, k, variant, bn, swap):
     p = pkg.ops.gemm_plan(m, n, k)
@@ -132,8 +133,11 @@ def test_planner_stream_k_balances_few_tiles(pkg):
     p = pkg.ops.gemm_plan(1, 4096, 12288)
     assert p["tiles"] == 32 and p["grid"] == 148 and p["gran"] == 1 and p["workspace_bytes"] > 0
     # a prefill shape whose iterations split evenly into whole tiles needs no workspace
-    p = pkg.ops.gemm_plan(8192, 24576, 4096, ctas=128)
+    p = pkg.ops.gemm_plan(8192, 24576, 4096, variant=1, ctas=128)
     assert p["grid"] == 128 and p["workspace_bytes"] == 0
+    # the pair variant deals whole 256 x 256 blocks to an even number of CTAs
+    p = pkg.ops.gemm_plan(8192, 24576, 4096)
+    assert p["variant"] == 7 and p["grid"] == 148 and p["workspace_bytes"] == 0
 
 
 def test_planner_respects_workspace_limit(pkg):

@@ -51,7 +51,7 @@ CASES = [
 ]
 
 
-@pytest.mark.parametrize("variant", [1, 2, 3, 4, 5, 6])
+@pytest.mark.parametrize("variant", [1, 2, 3, 4, 5, 6, 7])
 @pytest.mark.parametrize("m,n,k", CASES)
 def test_gemm_variants_bit_exact(pkg, oracle, cuda_dev, variant, m, n, k):
     _check(pkg, oracle, cuda_dev, m, n, k, variant=variant, seed=m + n + k + variant)
@@ -72,6 +72,14 @@ def test_gemm_stream_k_bit_exact(pkg, oracle, cuda_dev, variant, ctas):
                                    (1024, 5120, 512), (1100, 5120, 256)])
 def test_gemm_auto_plan(pkg, oracle, cuda_dev, m, n, k):
     _check(pkg, oracle, cuda_dev, m, n, k, bias=(m % 2 == 0), seed=m * 3 + n)
+
+
+@pytest.mark.parametrize("ctas", [2, 6, 148])
+@pytest.mark.parametrize("m,n,k", [(384, 768, 640), (1000, 1040, 256), (256, 256, 128)])
+def test_gemm_pair_variant_bit_exact(pkg, oracle, cuda_dev, m, n, k, ctas):
+    """2-SM (CTA pair) variant: odd 128-row tile counts (a phantom half), N not
+    a multiple of 256, K tails, few or many pairs."""
+    _check(pkg, oracle, cuda_dev, m, n, k, variant=7, ctas=ctas, bias=(m % 2 == 0), seed=m + ctas)
 
 
 def test_stream_k_counters_return_to_zero(pkg, oracle, cuda_dev):
