@@ -123,13 +123,16 @@ def _scn_random_bit_exact(pkg, O, rank, world, dev, dist):
 
 def _scn_gemm_allreduce(pkg, O, rank, world, dev, dist):
     """Fused row-parallel GEMM + all-reduce == oracle tp_linear("row"), bit-exact."""
-    comm = pkg.comm.PeerMemCommunicator(rank, world, 2048 * 5120 * 2, device=dev)
+    comm = pkg.comm.PeerMemCommunicator(rank, world, 2560 * 5120 * 2, device=dev)
     cases = [(0, 1, 5120, 1024 * world, False), (0, 16, 4096, 512 * world, True),
              (0, 64, 1024, 256 * world, False), (0, 200, 2048, 384 * world, False),
              (0, 1024, 5120, 512 * world, False), (0, 2048, 1536, 128 * world, True),
              # forced one-shot and two-shot reductions on normal-orientation tiles
              (1, 333, 4096, 256 * world, False), (2, 333, 4096, 256 * world, True),
-             (2, 1024, 5120, 512 * world, False), (2, 65, 2048, 128 * world, False)]
+             (2, 1024, 5120, 512 * world, False), (2, 65, 2048, 128 * world, False),
+             # large M selects the 2-SM pair kernel (256x256 per CTA pair)
+             (0, 2560, 5120, 128 * world, True), (1, 2500, 5120, 128 * world, False),
+             (2, 2560, 5120, 128 * world, False)]
     for (mode, m, n, kfull, bias) in cases:
         comm.set_mode(mode)
         g = torch.Generator().manual_seed(m * 7 + n)
