@@ -89,8 +89,10 @@ int w8a8_gemm(const int8_t* A, const int8_t* B, const float* sa, const float* sb
 
 /* Same as w8a8_gemm with an explicit configuration (for tests and tuning):
  * variant 0 = auto, 1 = 128x256 tiles, 2 = 128x128 tiles, 3..6 =
- * weight-stationary (swap-AB) 128 x {16,32,64,128}; ctas = 0 for one CTA per
- * SM, else the number of persistent CTAs (at most one per SM). */
+ * weight-stationary (swap-AB) 128 x {16,32,64,128}, 7 = 256x256 blocks on
+ * SM pairs (2-CTA clusters sharing one tcgen05 MMA, whole blocks, no
+ * workspace); ctas = 0 for one CTA per SM, else the number of persistent
+ * CTAs (at most one per SM; rounded down to an even count for variant 7). */
 int w8a8_gemm_config(const int8_t* A, const int8_t* B, const float* sa, const float* sb,
                      const void* bias, void* C, int32_t* c_i32, int64_t M, int64_t N,
                      int64_t K, int variant, int ctas, void* workspace,
