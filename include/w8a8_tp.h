@@ -98,6 +98,22 @@ int w8a8_gemm_config(const int8_t* A, const int8_t* B, const float* sa, const fl
                      int64_t K, int variant, int ctas, void* workspace,
                      size_t workspace_bytes, void* stream);
 
+/* w8a8_gemm without a caller workspace and without any allocation: the
+ * stream-K scratch is a fixed 20 MiB device array in the library, one per
+ * device.  No counterpart in the reference (its F.linear path allocates
+ * through torch).  For callers that cannot allocate at call time: an engine
+ * whose KV-cache pool holds the HBM left after the weights, and FFI callers
+ * without a caching allocator, for which cudaMalloc/cudaFree mid-step would
+ * synchronise the device.  Same plan and results as w8a8_gemm; a shape whose
+ * plan needs more than 20 MiB of scratch returns W8A8_ERR_WORKSPACE before
+ * any launch.  The first accepted non-empty call on a device (device current)
+ * does the set-up (cudaGetSymbolAddress, counters cleared synchronously):
+ * make it before any stream capture.  Overlapping calls on one device share
+ * the scratch and race. */
+int w8a8_gemm_static_scratch(const int8_t* A, const int8_t* B, const float* sa, const float* sb,
+                             const void* bias, void* C, int32_t* c_i32, int64_t M, int64_t N,
+                             int64_t K, void* stream);
+
 /* Host-only planner query (no GPU needed): the configuration w8a8_gemm would
  * use for a shape on a device with num_sms SMs.  out[8] receives
  * {variant, BN, swap, tiles, CTAs, k-blocks per tile, partition granularity

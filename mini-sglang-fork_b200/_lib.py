@@ -54,6 +54,8 @@ SIGNATURES = {
                            _c_i64, _c_i64, _c_i64, _c_vp, _c_size, _c_vp]),
     "w8a8_gemm_config": (_c_int, [_c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp,
                                   _c_i64, _c_i64, _c_i64, _c_int, _c_int, _c_vp, _c_size, _c_vp]),
+    "w8a8_gemm_static_scratch": (_c_int, [_c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp,
+                                          _c_i64, _c_i64, _c_i64, _c_vp]),
     "w8a8_gemm_plan": (_c_int, [_c_i64, _c_i64, _c_i64, _c_int, _c_int, _c_size, _c_int,
                                 ctypes.POINTER(_c_i64)]),
     "w8a8_comm_handle_bytes": (_c_size, []),
