@@ -231,14 +231,20 @@ def max_over_ranks(v: float, world: int, dev) -> float:
     return float(t.item())
 
 
-def _read_traffic():
-    """Per-launch DRAM bytes of the dominant kernel from the committed ncu summary."""
+def _read_traffic(m: int, n: int, k: int):
+    """Per-launch DRAM bytes of the dominant kernel, from the committed ncu
+    summary of the gate_up GEMM at M=4096, N=51200, K=5120 (TP=1).  At TP=N
+    the launch has N/TP output columns; its traffic (weight rows read, output
+    columns written) scales with N, so the captured figure is scaled by
+    n / 51200.  None for another M or K."""
     p = os.path.join(ROOT, "profiles", "gemm_gate_up_m4096_tp1_ncu.txt")
+    if m != 4096 or k != HIDDEN:
+        return None
     try:
         with open(p) as f:
             for line in f:
                 if line.startswith("traffic_bytes_per_launch_full:"):
-                    return float(line.split(":", 1)[1])
+                    return round(float(line.split(":", 1)[1]) * n / (2 * INTER))
     except OSError:
         pass
     return None
@@ -388,7 +394,7 @@ def run_ours(args, rank, world, dev):
         v, desc, th = cpu_oracle_sample(world)
         cpu = {"value": round(v, 1), "unit": UNIT, "cores": th, "kind": "port", "sample": desc}
 
-    traffic = _read_traffic()
+    traffic = _read_traffic(args.m, n_gu, k_gu)
     line = {
         "metric": METRIC,
         "value": round(value, 1),
