@@ -43,13 +43,7 @@ inline int variant_bn(int v) {
 inline bool variant_swap(int v) { return v >= 3 && v <= 6; }
 
 // Share of SM pairs kept busy when 256 x 256 blocks are dealt whole.
-inline double pair_efficiency(int64_t M, int64_t N, int nsm) {
-  const int64_t pairs = ((M + 255) / 256) * ((N + 255) / 256);
-  const int64_t clusters = nsm / 2;
-  if (clusters <= 0 || pairs < clusters) return 0.0;
-  const int64_t rounds = (pairs + clusters - 1) / clusters;
-  return static_cast<double>(pairs) / static_cast<double>(rounds * clusters);
-}
+inline int64_t pair_blocks(int64_t M, int64_t N) { return ((M + 255) / 256) * ((N + 255) / 256); }
 
 inline const char* plan_error(int rc) {
   switch (rc) {
@@ -79,11 +73,15 @@ inline int plan_gemm(int64_t M, int64_t N, int64_t K, int variant, int ctas_req,
       v = 4;
     } else if (M <= 64) {
       v = 5;
-    } else if (M > 256 && pair_efficiency(M, N, nsm) >= 0.85) {
+    } else if (M > 128 && pair_blocks(M, N) * 2 >= nsm / 2) {
+      // 256 x 256 blocks on SM pairs whenever at least half of the pairs get
+      // a block: the pair kernel moves 128 int8 MACs per staged operand byte
+      // (128 x 256 tiles: 85), which outweighs its coarser tail.
       v = 7;
     } else {
-      const int64_t tiles256 = ((M + 127) / 128) * ((N + 255) / 256);
-      v = tiles256 >= nsm ? 1 : 2;
+      // 128 x 128 tiles + stream-K: measured faster than 128 x 256 tiles at
+      // every shape the pair kernel does not take
+      v = 2;
     }
   }
   if (v < 1 || v > 7) return 1;
@@ -117,8 +115,14 @@ inline int plan_gemm(int64_t M, int64_t N, int64_t K, int variant, int ctas_req,
   const long long total_iters = static_cast<long long>(p->num_tiles) * p->kblocks;
   long long g = ctas_req > 0 ? (ctas_req < nsm ? ctas_req : nsm) : nsm;
   if (g > total_iters) g = total_iters;
-  // whole tiles for every CTA first, stream-K over the remainder
-  p->dp_tiles = static_cast<int>((p->num_tiles / g) * g);
+  // Whole tiles for every CTA first, stream-K over the rest.  With a
+  // remainder and at least one full wave, the last full wave joins the
+  // stream-K region ("two-tile" stream-K): every CTA then takes between one
+  // and two tiles of iterations, so no tile is cut between more than two CTAs
+  // and a fix-up adds at most one other CTA's partial.
+  const long long full_waves = p->num_tiles / g;
+  const bool remainder = (p->num_tiles % g) != 0;
+  p->dp_tiles = static_cast<int>((remainder && full_waves >= 1 ? full_waves - 1 : full_waves) * g);
   const long long iters = static_cast<long long>(p->num_tiles - p->dp_tiles) * p->kblocks;
 
   // Does an even split of the remaining iterations over min(g, iters) CTAs
@@ -128,8 +132,9 @@ inline int plan_gemm(int64_t M, int64_t N, int64_t K, int variant, int ctas_req,
   for (long long c = 1; c < gs && !cut; ++c) cut = ((c * iters / gs) % p->kblocks) != 0;
   const size_t need = kCounterBytes + 2 * static_cast<size_t>(g) * 128 * p->bn * 4;
   if (cut && (need > ws_avail || p->num_tiles > kMaxCounterTiles)) {
-    // no room to finish cut tiles: whole-tile ranges
+    // no room to finish cut tiles: whole-tile ranges (plain data-parallel waves)
     p->gran = p->kblocks;
+    p->dp_tiles = static_cast<int>(full_waves * g);
     if (g > p->num_tiles) {
       g = p->num_tiles;
       p->dp_tiles = p->num_tiles;

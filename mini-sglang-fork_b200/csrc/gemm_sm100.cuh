@@ -27,27 +27,31 @@
 // handful of tokens; the math is unchanged (C^T = B . A^T) and the epilogue
 // writes C[m, n] with n along the 32 lanes of a warp.
 //
-// Schedule (hybrid data-parallel + stream-K).  With T tiles and G CTAs, the
-// first G*floor(T/G) tiles are dealt whole in grid-stride order; the k-block
-// iterations of the last T mod G tiles are laid end to end and CTA c takes the
-// contiguous range [c*L/G, (c+1)*L/G) of them (rounded to whole tiles in
-// tile-granular mode), so every CTA streams the same number of k blocks
-// whatever the tile count.  A range cut inside a tile leaves a partial
-// fragment: its int32 accumulator goes to a per-CTA workspace slot with plain
-// coalesced stores, the fragment's arrival is counted on the tile's counter,
-// and the last arriving fragment adds the other slots (int32, exact in any
-// order), dequantises, writes the tile and resets the counter, so the counters
-// stay zero between calls.
+// Schedule (hybrid data-parallel + stream-K).  With T tiles and G CTAs, whole
+// tiles are dealt in grid-stride order first; when T is not a multiple of G,
+// the last full wave is held back, and the k-block iterations of the held-back
+// wave plus the remainder are laid end to end, CTA c taking the contiguous
+// range [c*L/G, (c+1)*L/G) ("two-tile" stream-K: every CTA streams the same
+// number of k blocks, between one and two tiles' worth, and no tile is cut
+// between more than two CTAs).  A range cut inside a tile leaves a partial
+// fragment: its int32 accumulator goes to a per-CTA workspace slot with
+// coalesced 16-byte stores, the fragment's arrival is counted on the tile's
+// counter, and the last arriving fragment adds the other slot(s) to its own
+// accumulator, still in TMEM (int32, exact in any order), dequantises, writes
+// the tile and resets the counter, so the counters stay zero between calls.
 //
-// Fused all-reduce (row-parallel layers, FUSED = true).  The epilogue writes
-// each finished bf16 partial tile into this rank's IPC-shared buffer (same
-// [M, N] layout as C) and raises the tile's "ready" flag on every rank.  After
-// its GEMM work, CTA b reduces the tiles t with t % G == b in two shots: it
-// waits for every rank's ready(t), sums its 1/world share of the tile from all
-// ranks in rank order (fp32, one rounding), writes it back in place and raises
-// reduced(t) everywhere; then it waits for every rank's reduced(t) and gathers
-// the shares into C.  Waits happen only after all of the CTA's own signals, so
-// no wait can block a signal another rank needs.
+// Fused all-reduce (row-parallel layers, FUSED = true).  As each bf16 partial
+// tile leaves the epilogue it is pushed over NVLink into the peers' receive
+// slots (tile-blocked, 512-byte coalesced pieces through a per-warp shared
+// memory transpose): one-shot pushes the whole tile to every rank, two-shot
+// pushes each row share to the rank that owns it; then the tile's ready flag is
+// raised on every rank.  After its GEMM work, CTA b reduces the tiles t with
+// t % G == b from local memory only: it waits for every rank's ready(t), sums
+// the ranks' partials in rank order (fp32, one rounding) into C, and, two-shot,
+// pushes its reduced share into every peer's gather slot, raises gathered(t),
+// then copies the other ranks' shares from its own gather slot.  Waits happen
+// only after all of the CTA's own signals, so no wait can block a signal
+// another rank needs.
 //
 // Every mbarrier / flag wait is bounded (%globaltimer); on expiry the CTA
 // raises a shared abort flag and the device error word, drains its in-flight
@@ -708,22 +712,24 @@ __global__ void __launch_bounds__(192, 1)
           push_chunk(c);
         }
       } else {
-        // partial fragment: park the int32 tile in this CTA's slot
+        // Partial fragment: park the int32 values in this CTA's slot.  Slot
+        // layout [chunk][warp][column group j][lane][4 columns]: a thread
+        // moves its chunk as kChunk/4 16-byte stores / loads, and each warp
+        // instruction covers 512 contiguous bytes.
         const long long tile_begin = static_cast<long long>(tile) * args.kblocks;
         const int slot = 2 * blockIdx.x + (my_begin < tile_begin ? 1 : 0);
-        int32_t* wslot = args.ws + static_cast<int64_t>(slot) * (T::kBM * BN);
+        int4* wslot = reinterpret_cast<int4*>(args.ws + static_cast<int64_t>(slot) * (T::kBM * BN));
+        constexpr int kVec = T::kChunk / 4;
 #pragma unroll 1
         for (int c = 0; c < T::kChunks; ++c) {
           uint32_t v[32];
           dev::tmem_ld<T::kChunk>(t_acc + c * T::kChunk, v);
           dev::tmem_wait_ld(v);
-          if (c == T::kChunks - 1) {
-            dev::tc_fence_before();
-            dev::mbar_arrive(dev::smem_u32(acc_empty + acc));
-          }
+          int4* p = wslot + ((c * 4 + quarter) * kVec) * 32 + lane;
 #pragma unroll
-          for (int j = 0; j < T::kChunk; ++j)
-            __stcg(wslot + (c * T::kChunk + j) * T::kBM + row_in_tile, static_cast<int32_t>(v[j]));
+          for (int j = 0; j < kVec; ++j)
+            __stcg(p + j * 32, make_int4(static_cast<int>(v[4 * j]), static_cast<int>(v[4 * j + 1]),
+                                    static_cast<int>(v[4 * j + 2]), static_cast<int>(v[4 * j + 3])));
         }
         __threadfence();
         dev::named_bar_sync(1, 128);
@@ -735,20 +741,37 @@ __global__ void __launch_bounds__(192, 1)
         }
         dev::named_bar_sync(1, 128);
         wrote_tile = *last_flag != 0;
-        if (wrote_tile) {
+        if (!wrote_tile) {
+          dev::tc_fence_before();
+          dev::mbar_arrive(dev::smem_u32(acc_empty + acc));
+        } else {
+          // Last arriver: its own share is still in TMEM (the accumulator is
+          // released only after this fix-up); add the other CTAs' slots.
           __threadfence();
 #pragma unroll 1
           for (int c = 0; c < T::kChunks; ++c) {
             uint32_t v[32];
-#pragma unroll
-            for (int j = 0; j < 32; ++j) v[j] = 0u;
+            dev::tmem_ld<T::kChunk>(t_acc + c * T::kChunk, v);
+            dev::tmem_wait_ld(v);
             for (int cta = c_first; cta <= c_last; ++cta) {
+              if (cta == static_cast<int>(blockIdx.x)) continue;
               const int s = 2 * cta + (sk_begin(args, cta) < tile_begin ? 1 : 0);
-              const int32_t* p = args.ws + static_cast<int64_t>(s) * (T::kBM * BN) + (c * T::kChunk) * T::kBM +
-                                 row_in_tile;
+              const int4* p = reinterpret_cast<const int4*>(args.ws + static_cast<int64_t>(s) * (T::kBM * BN)) +
+                              ((c * 4 + quarter) * kVec) * 32 + lane;
+              int4 q[kVec];
 #pragma unroll
-              for (int j = 0; j < T::kChunk; ++j)
-                v[j] = static_cast<uint32_t>(static_cast<int32_t>(v[j]) + __ldcg(p + j * T::kBM));
+              for (int j = 0; j < kVec; ++j) q[j] = __ldcg(p + j * 32);
+#pragma unroll
+              for (int j = 0; j < kVec; ++j) {  // two's-complement sums, as int32
+                v[4 * j] += static_cast<uint32_t>(q[j].x);
+                v[4 * j + 1] += static_cast<uint32_t>(q[j].y);
+                v[4 * j + 2] += static_cast<uint32_t>(q[j].z);
+                v[4 * j + 3] += static_cast<uint32_t>(q[j].w);
+              }
+            }
+            if (c == T::kChunks - 1) {
+              dev::tc_fence_before();
+              dev::mbar_arrive(dev::smem_u32(acc_empty + acc));
             }
             store_chunk<SWAP, T::kChunk>(args, row, tn * BN + c * T::kChunk, v, emit16, emit2);
             push_chunk(c);

@@ -63,7 +63,9 @@ def test_host_validation_rejects_bad_arguments(pkg):
     (1, 24576, 4096, 3, 16, 1), (16, 24576, 4096, 3, 16, 1), (17, 24576, 4096, 4, 32, 1),
     (64, 6144, 1024, 5, 64, 1), (65, 6144, 1024, 2, 128, 0), (256, 5120, 8192, 2, 128, 0),
     (8192, 24576, 4096, 7, 256, 0), (8192, 4096, 12288, 7, 256, 0), (4096, 6400, 5120, 7, 256, 0),
-    (4096, 1280, 8192, 1, 256, 0), (512, 5120, 1024, 2, 128, 0), (8192, 1280, 8192, 1, 256, 0),
+    (4096, 1280, 8192, 7, 256, 0), (512, 5120, 1024, 7, 256, 0), (8192, 1280, 8192, 7, 256, 0),
+    # too few 256 x 256 blocks to occupy half of the SM pairs: 1-SM tiles + stream-K
+    (300, 1280, 5120, 2, 128, 0), (1024, 256, 4096, 2, 128, 0),
 ])
 def test_planner_variant_choice(pkg, m, n, k, variant, bn, swap):
     p = pkg.ops.gemm_plan(m, n, k)
@@ -78,8 +80,11 @@ def test_planner_variant_choice(pkg, m, n, k, variant, bn, swap):
 def _schedule(tiles, kblocks, grid, gran=1):
     """Host model of the kernel's hybrid schedule (FragmentWalk, sk_begin,
     sk_owner): whole tiles dealt in grid-stride order, then stream-K ranges
-    over the remaining tiles' k blocks.  Returns per-CTA fragment lists."""
-    dp = (tiles // grid) * grid
+    over the remaining tiles' k blocks.  With a remainder and a full wave, the
+    last full wave joins the stream-K part (two-tile stream-K).  Returns
+    per-CTA fragment lists."""
+    full, rem = divmod(tiles, grid)
+    dp = (full - 1 if rem and full >= 1 else full) * grid
     units = (tiles - dp) * kblocks // gran
     sk = max(1, min(grid, units))            # CTAs sharing the stream-K part
     begin = [dp * kblocks + (min(c, sk) * units // sk) * gran for c in range(grid + 1)]
@@ -119,6 +124,8 @@ def test_hybrid_schedule_covers_every_iteration_once(tiles, kblocks, grid):
             continue
         c0, c1 = owner(t * kblocks), owner(t * kblocks + kblocks - 1)
         assert owners == list(range(c0, c1 + 1))
+        if tiles >= grid:  # two-tile stream-K: a tile is cut between at most two CTAs
+            assert len(owners) <= 2
         slots = {2 * c + (1 if begin[c] < t * kblocks else 0) for c in owners}
         assert len(slots) == len(owners)
     # every stream-K CTA has work, and k blocks per CTA differ by at most one

@@ -66,7 +66,7 @@ def test_static_scratch_rejects_plans_above_its_size(pkg, cuda_dev):
     """A 128 x 256-tile plan with a cut remainder needs ~39 MB: refused before any launch."""
     lib = pkg.load_library()
     L = pkg._lib
-    m, n, k = 4096, 1280, 8192
+    m, n, k = 256, 51200, 5120
     plan = pkg.ops.gemm_plan(m, n, k)
     assert plan["workspace_bytes"] > 20 * 2 ** 20
     a, b, sa, sb, _ = _inputs(8, 16, 16, False, cuda_dev)  # never read: the call stops on the host
