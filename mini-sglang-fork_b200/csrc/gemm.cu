@@ -66,7 +66,8 @@ int launch_variant(const GemmPlan& p, const CUtensorMap& tw, const CUtensorMap& 
       configured[dev] = true;
     }
   }
-  W8A8_CUDA_TRY(launch_pdl(kern, dim3(p.grid), dim3(T::kThreads), T::kSmemBytes, stream, tw, tn, args, cv));
+  W8A8_CUDA_TRY(launch_pdl(kern, dim3(p.grid), dim3(gemm_block_threads<FUSED>()), T::kSmemBytes, stream, tw, tn,
+                           args, cv));
   return W8A8_OK;
 }
 
@@ -103,7 +104,8 @@ int launch_pair_variant(const GemmPlan& p, const CUtensorMap& ta, const CUtensor
       configured[dev] = true;
     }
   }
-  W8A8_CUDA_TRY(launch_pdl(kern, dim3(p.grid), dim3(T::kThreads), T::kSmemBytes, stream, ta, tb, args, cv));
+  W8A8_CUDA_TRY(launch_pdl(kern, dim3(p.grid), dim3(gemm_block_threads<FUSED>()), T::kSmemBytes, stream, ta, tb,
+                           args, cv));
   return W8A8_OK;
 }
 

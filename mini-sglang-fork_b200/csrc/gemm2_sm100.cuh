@@ -42,8 +42,7 @@ struct Gemm2Traits {
   static constexpr int kBarrierBytes = 256;
   static constexpr int kStagingBytes = 4 * 2048;
   static constexpr int kTileOutBytes = 128 * kBN * 2;
-  static constexpr int kSmemBytes = 1024 + STAGES * kStageBytes + kBarrierBytes + kStagingBytes;
-  static constexpr int kThreads = 192;
+  static constexpr int kSmemBytes = 1024 + STAGES * kStageBytes + kBarrierBytes + kStagingBytes + kSignalBytes;
   static constexpr uint32_t kIdesc = dev::idesc_i8(256, 256);
   static_assert(kSmemBytes <= 227 * 1024, "shared memory");
 };
@@ -65,7 +64,7 @@ __device__ __forceinline__ int tile_index(const GemmArgs& a, int tw, int tn) {
 }
 
 template <int STAGES, bool FUSED>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(gemm_block_threads<FUSED>(), 1)
     w8a8_gemm2_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
                       const GemmArgs args, const CommView cv) {
   using T = Gemm2Traits<STAGES>;
@@ -83,6 +82,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   volatile uint32_t* epoch_slot = reinterpret_cast<volatile uint32_t*>(abort_flag + 2);
   uint8_t* staging = reinterpret_cast<uint8_t*>(bars) + T::kBarrierBytes;
+  FusedState* sigq = reinterpret_cast<FusedState*>(staging + T::kStagingBytes);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -93,6 +93,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
   const int num_pairs = pairs_w * args.tiles_n;
 
   if (threadIdx.x == 0) {
+    init_fused_state(sigq);
     for (int s = 0; s < STAGES; ++s) {
       dev::mbar_init(dev::smem_u32(full + s), 1);
       dev::mbar_init(dev::smem_u32(empty + s), 1);
@@ -215,7 +216,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
         if (args.err) atomicOr(args.err, kErrGemmDrain);
       }
     }
-  } else {
+  } else if (warp < kGemmWarps) {
     // ------------------------------------------------------------ epilogue
     dev::griddep_wait();
     if constexpr (FUSED) epoch = dev::ld_relaxed_gpu(dev::ctrl_ptr(cv.base[cv.rank])) + 1u;
@@ -259,6 +260,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
     const int et = threadIdx.x - 64;
     int acc = 0;
     uint32_t acc_phase = 0;
+    uint32_t sig_n = 0;
     bool aborted = false;
     for (int p = cluster; p < num_pairs; p += nclusters) {
       int pw, tn;
@@ -303,8 +305,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
       }
       if constexpr (FUSED) {
         if (real) {
+          // every epilogue thread's pushes of the tile precede the hand-over
           dev::named_bar_sync(1, 128);
-          dev::signal_peers(cv, 0, tile, epoch, et);
+          if (et == 0 && !signal_handover(sigq, sig_n, tile, args.err, tmo)) *abort_flag = 1;
         }
       }
       if (++acc == 2) {
@@ -315,7 +318,33 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
     dev::tc_fence_before();
     if constexpr (FUSED) {
       if (aborted) *abort_flag = 1;
-      if (et == 0) *epoch_slot = epoch;
+      if (et == 0) {
+        *epoch_slot = epoch;
+        dev::st_release_cta(&sigq->closed, 1u);
+      }
+    }
+  } else {
+    if constexpr (FUSED) {
+      // ----------------------------------------------------------- reducers
+      // Each CTA of the pair reduces its own share of the call's 128 x 256
+      // tiles (t % gridDim.x == blockIdx.x) as the ranks' partials land, and
+      // raises its own ready flags meanwhile and afterwards.
+      dev::griddep_wait();
+      const uint32_t ep = dev::ld_relaxed_gpu(dev::ctrl_ptr(cv.base[cv.rank])) + 1u;
+      const ReduceGroup g{kReducerBar, kReduceThreads, static_cast<int>(threadIdx.x) - 32 * kGemmWarps, 0};
+      fused_reduce_group<256, false>(args, cv, ep, g, abort_flag, sigq);
+      if (g.tid == g.nthreads - 1) signal_drain(sigq, cv, ep, args.err, tmo);
+    }
+  }
+  if constexpr (FUSED) {
+    if (warp < kGemmWarps) {
+      // The six GEMM warps, done with the GEMM, join the reduction.
+      dev::named_bar_sync(kLateBar, 32 * kGemmWarps);
+      if (*abort_flag == 0) {
+        dev::griddep_wait();
+        const ReduceGroup g{kLateBar, 32 * kGemmWarps, static_cast<int>(threadIdx.x), 1};
+        fused_reduce_group<256, false>(args, cv, *epoch_slot, g, abort_flag, sigq);
+      }
     }
   }
 
@@ -327,11 +356,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
   }
   if constexpr (FUSED) {
     epoch = *epoch_slot;
-    if (*abort_flag == 0) {
-      dev::griddep_wait();
-      fused_reduce_tiles<256, false>(args, cv, epoch, threadIdx.x);
-    }
-    __syncthreads();
     if (threadIdx.x == 0) {
       uint32_t* c = dev::ctrl_ptr(cv.base[cv.rank]);
       __threadfence();

@@ -89,6 +89,9 @@ struct GemmArgs {
   int wide_fast;              // raster: 1 = consecutive tiles walk the 128-row side
 };
 
+// Shared memory of the fused epilogue and reduction state (FusedState, below).
+constexpr int kSignalBytes = 1088;
+
 template <int BN, int STAGES, bool SWAP>
 struct GemmTraits {
   static constexpr int kBM = 128;
@@ -105,8 +108,7 @@ struct GemmTraits {
   static constexpr int kBarrierBytes = 256;
   static constexpr int kStagingBytes = 4 * 2048;  // fused epilogue: 2 KB transpose buffer per warp
   static constexpr int kTileOutBytes = 128 * BN * 2;  // one tile's bf16 block in a receive slot
-  static constexpr int kSmemBytes = 1024 + STAGES * kStageBytes + kBarrierBytes + kStagingBytes;
-  static constexpr int kThreads = 192;
+  static constexpr int kSmemBytes = 1024 + STAGES * kStageBytes + kBarrierBytes + kStagingBytes + kSignalBytes;
   static constexpr uint32_t kIdesc = dev::idesc_i8(kBM, BN);
   static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "MMA N");
   static_assert(kSmemBytes <= 227 * 1024, "shared memory");
@@ -248,10 +250,151 @@ __device__ __forceinline__ void tile_rect(const GemmArgs& a, int tile, int& m0, 
   }
 }
 
-// Threads of a CTA that take part in the fused reduction (all six warps, once
-// the GEMM work of the CTA is done) and the named barrier they use.
-constexpr int kReduceThreads = 192;
-constexpr int kReduceBar = 2;
+// Fused mode adds two reducer warps (warps 6-7) to the six GEMM warps.  They
+// reduce the CTA's tiles across the ranks while the GEMM warps are still
+// producing later tiles; once the GEMM warps are done they join in as a second
+// group, and the two groups claim the CTA's tiles from shared counters.  The
+// last thread of each group also raises the ready flags of the tiles the
+// epilogue has pushed (FusedState).
+constexpr int kGemmWarps = 6;
+constexpr int kReduceThreads = 64;
+template <bool FUSED>
+constexpr int gemm_block_threads() { return 32 * kGemmWarps + (FUSED ? kReduceThreads : 0); }
+
+// Threads of the CTA doing reduction work together.
+struct ReduceGroup {
+  int bar;       // named barrier of the group
+  int nthreads;  // multiple of 32
+  int tid;       // 0 .. nthreads-1
+  int slot;      // the group's claim broadcast word
+};
+constexpr int kReducerBar = 2;  // warps 6-7
+constexpr int kLateBar = 3;     // warps 0-5 once the GEMM work is done
+
+// Shared state of the fused epilogue and the reduction.
+//
+// Hand-over of pushed tiles from the epilogue to the flag-raising threads.
+// Raising a ready flag needs a system-scope fence that waits until the CTA's
+// earlier peer stores have drained over NVLink (many microseconds when every
+// SM is pushing), so the epilogue does not do it: it moves straight on to the
+// next tile.  Epilogue thread 0 appends the tile id and publishes the count
+// with a CTA-scope release after the epilogue's barrier; a reduce thread
+// acquires the count, fences at system scope and stores the flags, which
+// orders the whole epilogue's pushes before them (causality is transitive
+// through the barrier and the CTA-scope release / acquire).  Raising a flag
+// twice stores the same epoch again, so concurrent raisers are harmless.
+constexpr int kSignalRing = 256;
+struct FusedState {
+  int tiles[kSignalRing];
+  uint32_t count;     // tiles handed over
+  uint32_t closed;    // 1 once the epilogue has handed over its last tile
+  uint32_t taken;     // tiles whose flags are raised (monotonic)
+  uint32_t claim[2];  // next tile index of this CTA to reduce, per phase
+  int bcast[2];       // claimed index, broadcast within each group
+};
+static_assert(sizeof(FusedState) <= kSignalBytes, "fused state");
+
+__device__ __forceinline__ void init_fused_state(FusedState* q) {
+  q->count = 0u;
+  q->closed = 0u;
+  q->taken = 0u;
+  q->claim[0] = q->claim[1] = 0u;
+}
+
+// Epilogue thread 0: append `tile` (n = tiles appended so far).  Bounded wait
+// while the ring is full; false on timeout.
+__device__ __forceinline__ bool signal_handover(FusedState* q, uint32_t& n, int tile, unsigned int* err,
+                                                long long tmo) {
+  if (n - dev::ld_acquire_cta(&q->taken) >= static_cast<uint32_t>(kSignalRing)) {
+    const uint64_t t0 = dev::globaltimer_ns();
+    while (n - dev::ld_acquire_cta(&q->taken) >= static_cast<uint32_t>(kSignalRing)) {
+      if (dev::globaltimer_ns() - t0 > static_cast<uint64_t>(tmo)) {
+        if (err) atomicOr(err, kErrGemmWait);
+        return false;
+      }
+      __nanosleep(64);
+    }
+  }
+  reinterpret_cast<volatile int*>(q->tiles)[n % kSignalRing] = tile;
+  dev::st_release_cta(&q->count, ++n);
+  return true;
+}
+
+// Raise ready(t) on every rank for each handed-over tile not yet raised.
+// Returns true once the epilogue has closed the queue and every tile is raised.
+__device__ __forceinline__ bool signal_pump(FusedState* q, const CommView& cv, uint32_t epoch) {
+  const uint32_t closed = dev::ld_acquire_cta(&q->closed);  // before count: a closed queue's count is final
+  const uint32_t n = dev::ld_acquire_cta(&q->count);
+  const uint32_t d = dev::ld_acquire_cta(&q->taken);
+  if (n != d) {
+    asm volatile("fence.acq_rel.sys;" ::: "memory");
+    for (uint32_t i = d; i < n; ++i) {
+      const int tile = reinterpret_cast<volatile int*>(q->tiles)[i % kSignalRing];
+      for (int r = 0; r < cv.world; ++r) {
+        uint32_t* f = dev::flag_ptr(cv.base[r], 0, tile, cv.rank);
+        asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(f), "r"(epoch) : "memory");
+      }
+    }
+    uint32_t old;
+    asm volatile("atom.release.cta.shared::cta.max.u32 %0, [%1], %2;"
+                 : "=r"(old)
+                 : "r"(dev::smem_u32(&q->taken)), "r"(n)
+                 : "memory");
+  }
+  return closed != 0;
+}
+
+// After its own work, a group's last thread keeps raising this CTA's ready
+// flags until the epilogue closes the queue (bounded by tmo).
+__device__ __forceinline__ void signal_drain(FusedState* q, const CommView& cv, uint32_t epoch, unsigned int* err,
+                                             long long tmo) {
+  const uint64_t t0 = dev::globaltimer_ns();
+  for (uint32_t it = 0; !signal_pump(q, cv, epoch); ++it) {
+    if ((it & 63u) == 63u && dev::globaltimer_ns() - t0 > static_cast<uint64_t>(tmo)) {
+      if (err) atomicOr(err, kErrGemmWait);
+      return;
+    }
+    __nanosleep(64);
+  }
+}
+
+// The group waits (bounded) until every rank has raised flag (phase, slot) of
+// call `epoch`; threads t < world poll rank t's flag and the group's last
+// thread keeps this CTA's own ready flags moving meanwhile.  False on timeout
+// or when the CTA's GEMM gave up.
+__device__ __forceinline__ bool group_wait(const CommView& cv, int phase, int slot, uint32_t epoch,
+                                           const ReduceGroup& g, FusedState* q, const volatile int* abort_flag) {
+  const uint32_t* f = g.tid < cv.world ? dev::flag_ptr(cv.base[cv.rank], phase, slot, g.tid) : nullptr;
+  const uint64_t t0 = dev::globaltimer_ns();
+  for (uint32_t it = 0;; ++it) {
+    const bool mine = f == nullptr || dev::ld_acquire_sys(f) == epoch;
+    if (g.tid == g.nthreads - 1) signal_pump(q, cv, epoch);
+    bool fail = false;
+    if (!mine && (it & 15u) == 15u) {
+      if (*abort_flag != 0) {
+        fail = true;
+      } else if (dev::globaltimer_ns() - t0 > static_cast<uint64_t>(cv.timeout_ns)) {
+        if (cv.err) atomicOr(cv.err, kErrCommWait);
+        uint32_t* c = dev::ctrl_ptr(cv.base[cv.rank]);
+        c[2] = (static_cast<uint32_t>(phase) << 24) | static_cast<uint32_t>(slot);
+        c[3] = static_cast<uint32_t>(g.tid);
+        fail = true;
+      }
+    }
+    if (dev::named_bar_or(g.bar, g.nthreads, fail)) return false;
+    if (!dev::named_bar_or(g.bar, g.nthreads, !mine)) return true;
+    if (it > 4) __nanosleep(32);
+  }
+}
+
+// The group claims the next index from `counter` (same value in every thread).
+__device__ __forceinline__ int group_claim(uint32_t* counter, const ReduceGroup& g, int* bcast) {
+  if (g.tid == 0) *bcast = static_cast<int>(atomicAdd(counter, 1u));
+  dev::named_bar_sync(g.bar, g.nthreads);
+  const int i = *reinterpret_cast<volatile int*>(bcast);
+  dev::named_bar_sync(g.bar, g.nthreads);  // every thread has read it before the next claim
+  return i;
+}
 
 // Receive-slot layout of one tile (block of 128 x BN bf16 at t * kTileOutBytes):
 //   normal: [chunk c = 0..BN/32)[row 0..127][32 columns]  (64-byte row pieces,
@@ -279,17 +422,17 @@ __device__ __forceinline__ void block_vec_rc(int v, int& r, int& col) {
 // keeps 8 independent 16-byte loads in flight per thread (W = 0: any world).
 template <int W, int BN, bool SWAP, class VecOf>
 __device__ __forceinline__ void reduce_block(const GemmArgs& a, const CommView& cv, uint32_t epoch, int t, int m0,
-                                             int n0, int nvec, VecOf vec_of, int tid, bool push_gather) {
+                                             int n0, int nvec, VecOf vec_of, int tid, int nt, bool push_gather) {
   constexpr int V = W > 0 ? 8 / W : 1;
   constexpr int TILE = 128 * BN * 2;
   const int world = W > 0 ? W : cv.world;
   const char* slot0 = dev::recv_slot(cv, cv.rank, 0, epoch) + static_cast<size_t>(t) * TILE;
   const size_t sstride = cv.slot_bytes;
-  for (int base = tid; base < nvec; base += kReduceThreads * V) {
+  for (int base = tid; base < nvec; base += nt * V) {
     uint4 buf[V][W > 0 ? W : 1];
 #pragma unroll
     for (int j = 0; j < V; ++j) {
-      const int i = base + j * kReduceThreads;
+      const int i = base + j * nt;
       if (i < nvec) {
         const size_t off = static_cast<size_t>(vec_of(i)) * 16;
         if constexpr (W > 0) {
@@ -302,7 +445,7 @@ __device__ __forceinline__ void reduce_block(const GemmArgs& a, const CommView& 
     }
 #pragma unroll
     for (int j = 0; j < V; ++j) {
-      const int i = base + j * kReduceThreads;
+      const int i = base + j * nt;
       if (i >= nvec) continue;
       const int v = vec_of(i);
       const size_t off = static_cast<size_t>(v) * 16;
@@ -351,70 +494,81 @@ __device__ __forceinline__ void reduce_block(const GemmArgs& a, const CommView& 
 
 template <int BN, bool SWAP, class VecOf>
 __device__ __forceinline__ void reduce_block_any_world(const GemmArgs& a, const CommView& cv, uint32_t epoch, int t,
-                                                       int m0, int n0, int nvec, VecOf vec_of, int tid,
+                                                       int m0, int n0, int nvec, VecOf vec_of, int tid, int nt,
                                                        bool push_gather) {
   switch (cv.world) {
-    case 2: reduce_block<2, BN, SWAP>(a, cv, epoch, t, m0, n0, nvec, vec_of, tid, push_gather); break;
-    case 4: reduce_block<4, BN, SWAP>(a, cv, epoch, t, m0, n0, nvec, vec_of, tid, push_gather); break;
-    case 8: reduce_block<8, BN, SWAP>(a, cv, epoch, t, m0, n0, nvec, vec_of, tid, push_gather); break;
-    default: reduce_block<0, BN, SWAP>(a, cv, epoch, t, m0, n0, nvec, vec_of, tid, push_gather); break;
+    case 2: reduce_block<2, BN, SWAP>(a, cv, epoch, t, m0, n0, nvec, vec_of, tid, nt, push_gather); break;
+    case 4: reduce_block<4, BN, SWAP>(a, cv, epoch, t, m0, n0, nvec, vec_of, tid, nt, push_gather); break;
+    case 8: reduce_block<8, BN, SWAP>(a, cv, epoch, t, m0, n0, nvec, vec_of, tid, nt, push_gather); break;
+    default: reduce_block<0, BN, SWAP>(a, cv, epoch, t, m0, n0, nvec, vec_of, tid, nt, push_gather); break;
   }
 }
 
 // Reduction of the tiles this CTA owns (t % gridDim.x == blockIdx.x) from the
-// partials the epilogues of every rank pushed into this rank's receive slots.
+// partials the epilogues of every rank pushed into this rank's receive slots,
+// by one group; groups claim the tiles one at a time.
 //   one-shot: wait for every rank's ready(t), reduce the whole tile into C.
 //   two-shot: wait for ready(t), reduce this rank's row share into C and push
 //             it into every other rank's gather slot, raise gathered(t);
-//             then wait for every rank's gathered(t) and copy their shares
-//             from the local gather slot into C.
-// Returns false if a flag wait timed out (uniformly across the threads).
+//             then (second claim pass) wait for every rank's gathered(t) and
+//             copy their shares from the local gather slot into C.
+// Returns false if a flag wait timed out or the CTA's GEMM gave up (uniformly
+// across the group).
 template <int BN, bool SWAP>
-__device__ bool fused_reduce_tiles(const GemmArgs& a, const CommView& cv, uint32_t epoch, int tid) {
+__device__ bool fused_reduce_group(const GemmArgs& a, const CommView& cv, uint32_t epoch, const ReduceGroup& g,
+                                   const volatile int* abort_flag, FusedState* q) {
   constexpr int TILE = 128 * BN * 2;
   constexpr int NV = TILE / 16;  // vectors per tile block
-  for (int t = blockIdx.x; t < a.num_tiles; t += gridDim.x) {
-    const bool ok = dev::wait_peer(cv, 0, t, epoch, tid);
-    if (dev::named_bar_or(kReduceBar, kReduceThreads, !ok)) return false;
+  const int G = static_cast<int>(gridDim.x), b = static_cast<int>(blockIdx.x);
+  const int owned = (a.num_tiles - b + G - 1) / G;  // tiles b, b + G, ...
+  for (;;) {
+    const int i = group_claim(&q->claim[0], g, &q->bcast[g.slot]);
+    if (i >= owned) break;
+    const int t = b + i * G;
+    if (!group_wait(cv, 0, t, epoch, g, q, abort_flag)) return false;
     int m0, hm, n0, wn;
     tile_rect<BN, SWAP>(a, t, m0, hm, n0, wn);
     if (!cv.two_shot) {
-      reduce_block_any_world<BN, SWAP>(a, cv, epoch, t, m0, n0, NV, [](int i) { return i; }, tid, false);
+      reduce_block_any_world<BN, SWAP>(a, cv, epoch, t, m0, n0, NV, [](int v) { return v; }, g.tid, g.nthreads,
+                                       false);
     } else {
       // rows [r0, r1) of every chunk: (r1 - r0) * 4 vectors per chunk
       const int r0 = (hm * cv.rank) / cv.world, r1 = (hm * (cv.rank + 1)) / cv.world;
       const int per_chunk = (r1 - r0) * 4;
-      auto vec_of = [=](int i) { return (i / per_chunk) * 512 + r0 * 4 + (i % per_chunk); };
-      reduce_block_any_world<BN, SWAP>(a, cv, epoch, t, m0, n0, per_chunk * (BN / 32), vec_of, tid, true);
-      dev::named_bar_sync(kReduceBar, kReduceThreads);
-      dev::signal_peers(cv, 1, t, epoch, tid);
+      auto vec_of = [=](int v) { return (v / per_chunk) * 512 + r0 * 4 + (v % per_chunk); };
+      reduce_block_any_world<BN, SWAP>(a, cv, epoch, t, m0, n0, per_chunk * (BN / 32), vec_of, g.tid, g.nthreads,
+                                       true);
+      dev::named_bar_sync(g.bar, g.nthreads);
+      dev::signal_peers(cv, 1, t, epoch, g.tid);
     }
   }
   if (!cv.two_shot) return true;
-  for (int t = blockIdx.x; t < a.num_tiles; t += gridDim.x) {
-    const bool ok = dev::wait_peer(cv, 1, t, epoch, tid);
-    if (dev::named_bar_or(kReduceBar, kReduceThreads, !ok)) return false;
+  for (;;) {
+    const int i = group_claim(&q->claim[1], g, &q->bcast[g.slot]);
+    if (i >= owned) break;
+    const int t = b + i * G;
+    if (!group_wait(cv, 1, t, epoch, g, q, abort_flag)) return false;
     int m0, hm, n0, wn;
     tile_rect<BN, SWAP>(a, t, m0, hm, n0, wn);
     const char* from = dev::gather_slot(cv, cv.rank, epoch) + static_cast<size_t>(t) * TILE;
     // every vector outside this rank's own row share
     const int r0 = (hm * cv.rank) / cv.world, r1 = (hm * (cv.rank + 1)) / cv.world;
-    for (int base = tid; base < NV; base += kReduceThreads * 8) {
+    for (int base = g.tid; base < NV; base += g.nthreads * 8) {
       uint4 v[8];
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
-        const int i = base + j * kReduceThreads;
+        const int k = base + j * g.nthreads;
         int r, col;
-        block_vec_rc<BN, SWAP>(i, r, col);
-        if (i < NV && (r < r0 || r >= r1)) v[j] = dev::ld_volatile_v4(from + static_cast<size_t>(i) * 16);
+        block_vec_rc<BN, SWAP>(k, r, col);
+        if (k < NV && (r < r0 || r >= r1)) v[j] = dev::ld_volatile_v4(from + static_cast<size_t>(k) * 16);
       }
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
-        const int i = base + j * kReduceThreads;
+        const int k = base + j * g.nthreads;
         int r, col;
-        block_vec_rc<BN, SWAP>(i, r, col);
+        block_vec_rc<BN, SWAP>(k, r, col);
         const int m = m0 + r, n = n0 + col;
-        if (i < NV && (r < r0 || r >= r1) && m < a.M && n < a.N)
+        if (k < NV && (r < r0 || r >= r1) && m < a.M && n < a.N)
           *reinterpret_cast<uint4*>(a.C + static_cast<size_t>(m) * a.ldc + n) = v[j];
       }
     }
@@ -423,7 +577,7 @@ __device__ bool fused_reduce_tiles(const GemmArgs& a, const CommView& cv, uint32
 }
 
 template <int BN, int STAGES, bool SWAP, bool FUSED>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(gemm_block_threads<FUSED>(), 1)
     w8a8_gemm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_n,
                      const GemmArgs args, const CommView cv) {
   using T = GemmTraits<BN, STAGES, SWAP>;
@@ -442,11 +596,13 @@ __global__ void __launch_bounds__(192, 1)
   volatile int* last_flag = abort_flag + 1;
   volatile uint32_t* epoch_slot = reinterpret_cast<volatile uint32_t*>(last_flag + 1);
   uint8_t* staging = reinterpret_cast<uint8_t*>(bars) + T::kBarrierBytes;  // 16-byte aligned
+  FusedState* sigq = reinterpret_cast<FusedState*>(staging + T::kStagingBytes);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
 
   if (threadIdx.x == 0) {
+    init_fused_state(sigq);
     for (int s = 0; s < STAGES; ++s) {
       dev::mbar_init(dev::smem_u32(full + s), 1);
       dev::mbar_init(dev::smem_u32(empty + s), 1);
@@ -614,7 +770,7 @@ __global__ void __launch_bounds__(192, 1)
         if (args.err) atomicOr(args.err, kErrGemmDrain);
       }
     }
-  } else {
+  } else if (warp < kGemmWarps) {
     // ------------------------------------------------------------ epilogue
     dev::griddep_wait();
     if constexpr (FUSED) epoch = dev::ld_relaxed_gpu(dev::ctrl_ptr(cv.base[cv.rank])) + 1u;
@@ -676,6 +832,7 @@ __global__ void __launch_bounds__(192, 1)
     const long long my_begin = sk_begin(args, blockIdx.x);
     int acc = 0;
     uint32_t acc_phase = 0;
+    uint32_t sig_n = 0;
     bool aborted = false;
     FragmentWalk walk(args);
     int tile, kb0, kb1;
@@ -783,9 +940,9 @@ __global__ void __launch_bounds__(192, 1)
       }
       if constexpr (FUSED) {
         if (wrote_tile) {
-          // all 128 threads' partial stores precede the ready flag
+          // every epilogue thread's pushes of the tile precede the hand-over
           dev::named_bar_sync(1, 128);
-          dev::signal_peers(cv, 0, tile, epoch, et);
+          if (et == 0 && !signal_handover(sigq, sig_n, tile, args.err, tmo)) *abort_flag = 1;
         }
       }
       if (++acc == 2) {
@@ -796,7 +953,33 @@ __global__ void __launch_bounds__(192, 1)
     dev::tc_fence_before();
     if constexpr (FUSED) {
       if (aborted) *abort_flag = 1;
-      if (et == 0) *epoch_slot = epoch;
+      if (et == 0) {
+        *epoch_slot = epoch;
+        dev::st_release_cta(&sigq->closed, 1u);
+      }
+    }
+  } else {
+    if constexpr (FUSED) {
+      // ----------------------------------------------------------- reducers
+      // Reduce this CTA's tiles across the ranks as every rank's partial of
+      // each lands, overlapping the GEMM of the later tiles; raise this CTA's
+      // own ready flags meanwhile and afterwards.
+      dev::griddep_wait();
+      const uint32_t ep = dev::ld_relaxed_gpu(dev::ctrl_ptr(cv.base[cv.rank])) + 1u;
+      const ReduceGroup g{kReducerBar, kReduceThreads, static_cast<int>(threadIdx.x) - 32 * kGemmWarps, 0};
+      fused_reduce_group<BN, SWAP>(args, cv, ep, g, abort_flag, sigq);
+      if (g.tid == g.nthreads - 1) signal_drain(sigq, cv, ep, args.err, tmo);
+    }
+  }
+  if constexpr (FUSED) {
+    if (warp < kGemmWarps) {
+      // The six GEMM warps, done with the GEMM, join the reduction.
+      dev::named_bar_sync(kLateBar, 32 * kGemmWarps);
+      if (*abort_flag == 0) {
+        dev::griddep_wait();
+        const ReduceGroup g{kLateBar, 32 * kGemmWarps, static_cast<int>(threadIdx.x), 1};
+        fused_reduce_group<BN, SWAP>(args, cv, *epoch_slot, g, abort_flag, sigq);
+      }
     }
   }
 
@@ -806,14 +989,7 @@ __global__ void __launch_bounds__(192, 1)
     dev::tmem_dealloc(tmem_base, T::kTmemCols);
   }
   if constexpr (FUSED) {
-    // All six warps reduce the CTA's tiles across the ranks (abort_flag and the
-    // epoch are read after the barrier, so the decision is uniform).
     epoch = *epoch_slot;
-    if (*abort_flag == 0) {
-      dev::griddep_wait();
-      fused_reduce_tiles<BN, SWAP>(args, cv, epoch, threadIdx.x);
-    }
-    __syncthreads();
     // The last CTA of the call publishes the epoch for the next call.
     if (threadIdx.x == 0) {
       uint32_t* c = dev::ctrl_ptr(cv.base[cv.rank]);
