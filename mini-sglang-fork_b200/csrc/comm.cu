@@ -86,9 +86,93 @@ __device__ __forceinline__ bool cta_barrier(const CommView& v, int phase, int sl
   return __syncthreads_and(ok) != 0;
 }
 
+// Copy vectors [lo, hi) of `src` to `dst`, four per thread in flight.
+template <class Load>
+__device__ __forceinline__ void copy_vectors(uint4* dst, Load load, long long lo, long long hi) {
+  const long long s = blockDim.x;
+  for (long long i = lo + threadIdx.x; i < hi; i += 4 * s) {
+    uint4 t[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u)
+      if (i + u * s < hi) t[u] = load(i + u * s);
+#pragma unroll
+    for (int u = 0; u < 4; ++u)
+      if (i + u * s < hi) dst[i + u * s] = t[u];
+  }
+}
+
+// fp32 rank-order sum (rank 0's value, then ranks 1..W-1 added in order, one
+// bf16 rounding) of vectors i and i + s (those below hi) over every rank's
+// staged copy.  All 2 * W loads are issued before the first add.
+template <int W>
+__device__ __forceinline__ void sum_ranks_pair(const CommView& v, uint32_t epoch, long long i, long long s,
+                                               long long hi, uint4 (&out)[2]) {
+  uint4 raw[2][W];
+#pragma unroll
+  for (int u = 0; u < 2; ++u) {
+    const long long k = i + u * s;
+    if (k < hi) {
+#pragma unroll
+      for (int r = 0; r < W; ++r) raw[u][r] = dev::ld_volatile_v4(dev::half_ptr(v, r, epoch) + static_cast<size_t>(k) * 16);
+    }
+  }
+#pragma unroll
+  for (int u = 0; u < 2; ++u) {
+    if (i + u * s >= hi) continue;
+    float acc[8];
+    const __nv_bfloat162* h0 = reinterpret_cast<const __nv_bfloat162*>(&raw[u][0]);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 f = __bfloat1622float2(h0[j]);
+      acc[2 * j] = f.x;
+      acc[2 * j + 1] = f.y;
+    }
+#pragma unroll
+    for (int r = 1; r < W; ++r) {
+      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw[u][r]);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 f = __bfloat1622float2(h[j]);
+        acc[2 * j] = __fadd_rn(acc[2 * j], f.x);
+        acc[2 * j + 1] = __fadd_rn(acc[2 * j + 1], f.y);
+      }
+    }
+    __nv_bfloat162* o = reinterpret_cast<__nv_bfloat162*>(&out[u]);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) o[j] = __floats2bfloat162_rn(acc[2 * j], acc[2 * j + 1]);
+  }
+}
+
+// Reduce vectors [lo, hi) into x (and into this rank's staged copy when
+// `mine` is set).  W = world at compile time (0: any world, one vector at a
+// time).
+template <int W>
+__device__ __forceinline__ void reduce_range(const CommView& v, uint32_t epoch, uint4* x, uint4* mine, long long lo,
+                                             long long hi) {
+  const long long s = blockDim.x;
+  if constexpr (W > 0) {
+    for (long long i = lo + threadIdx.x; i < hi; i += 2 * s) {
+      uint4 out[2];
+      sum_ranks_pair<W>(v, epoch, i, s, hi, out);
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        if (i + u * s >= hi) continue;
+        if (mine) mine[i + u * s] = out[u];
+        x[i + u * s] = out[u];
+      }
+    }
+  } else {
+    for (long long i = lo + threadIdx.x; i < hi; i += s) {
+      const uint4 o = dev::sum_ranks_vec8(v, epoch, static_cast<size_t>(i) * 16);
+      if (mine) mine[i] = o;
+      x[i] = o;
+    }
+  }
+}
+
 // x: nvec 16-byte vectors (8 bf16 each), in place.
-__global__ void __launch_bounds__(kArThreads) allreduce_kernel(CommView v, uint4* x, long long nvec,
-                                                               int two_shot) {
+template <int W>
+__global__ void __launch_bounds__(kArThreads) allreduce_kernel(CommView v, uint4* x, long long nvec, int two_shot) {
   dev::griddep_wait();  // x and the epoch word come from earlier kernels
   dev::griddep_launch();
   const uint32_t epoch = dev::ld_relaxed_gpu(dev::ctrl_ptr(v.base[v.rank])) + 1u;
@@ -107,31 +191,24 @@ __global__ void __launch_bounds__(kArThreads) allreduce_kernel(CommView v, uint4
   for (long long c = 0; c < chunks; ++c) {
     long long lo, hi;
     range(c, lo, hi);
-    for (long long i = lo + threadIdx.x; i < hi; i += blockDim.x) mine[i] = x[i];
+    copy_vectors(mine, [&](long long i) { return x[i]; }, lo, hi);
   }
   bool ok = cta_barrier(v, 0, slot, epoch);
   if (ok) {
+    long long lo, hi;
     if (!two_shot) {
-      long long lo, hi;
       range(0, lo, hi);
-      for (long long i = lo + threadIdx.x; i < hi; i += blockDim.x)
-        x[i] = dev::sum_ranks_vec8(v, epoch, static_cast<size_t>(i) * 16);
+      reduce_range<W>(v, epoch, x, nullptr, lo, hi);
     } else {
-      long long lo, hi;
       range(v.rank, lo, hi);
-      for (long long i = lo + threadIdx.x; i < hi; i += blockDim.x) {
-        const uint4 s = dev::sum_ranks_vec8(v, epoch, static_cast<size_t>(i) * 16);
-        mine[i] = s;
-        x[i] = s;
-      }
+      reduce_range<W>(v, epoch, x, mine, lo, hi);
       ok = cta_barrier(v, 1, slot, epoch);
       if (ok) {
         for (int c = 0; c < v.world; ++c) {
           if (c == v.rank) continue;
           range(c, lo, hi);
           const char* src = dev::half_ptr(v, c, epoch);
-          for (long long i = lo + threadIdx.x; i < hi; i += blockDim.x)
-            x[i] = dev::ld_volatile_v4(src + static_cast<size_t>(i) * 16);
+          copy_vectors(x, [&](long long i) { return dev::ld_volatile_v4(src + static_cast<size_t>(i) * 16); }, lo, hi);
         }
       }
     }
@@ -292,8 +369,16 @@ int w8a8_all_reduce(w8a8_comm* c, void* x, int64_t numel, void* stream) {
   if (nsm <= 0) nsm = 148;
   long long grid = (per_chunk + kArThreads * 2 - 1) / (kArThreads * 2);
   grid = grid < 1 ? 1 : (grid > 2 * nsm ? 2 * nsm : grid);
-  W8A8_CUDA_TRY(launch_pdl(allreduce_kernel, dim3(static_cast<unsigned>(grid)), dim3(kArThreads), 0,
-                           static_cast<cudaStream_t>(stream), v, static_cast<uint4*>(x), nvec, one ? 0 : 1));
+  const dim3 g(static_cast<unsigned>(grid)), b(kArThreads);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  uint4* xv = static_cast<uint4*>(x);
+  const int two = one ? 0 : 1;
+  switch (c->world) {
+    case 2: W8A8_CUDA_TRY(launch_pdl(allreduce_kernel<2>, g, b, 0, st, v, xv, nvec, two)); break;
+    case 4: W8A8_CUDA_TRY(launch_pdl(allreduce_kernel<4>, g, b, 0, st, v, xv, nvec, two)); break;
+    case 8: W8A8_CUDA_TRY(launch_pdl(allreduce_kernel<8>, g, b, 0, st, v, xv, nvec, two)); break;
+    default: W8A8_CUDA_TRY(launch_pdl(allreduce_kernel<0>, g, b, 0, st, v, xv, nvec, two)); break;
+  }
   return W8A8_OK;
 }
 

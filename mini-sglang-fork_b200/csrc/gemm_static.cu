@@ -16,9 +16,9 @@
 // Limits:
 //  * kStaticScratchBytes (20 MiB) per device: the 256 KiB counter region plus
 //    two partial-tile slots per CTA.  On a 148-SM device that covers every
-//    stream-K plan with tiles at most 128 wide; a plan that needs more (the
-//    128 x 256 tiles with a cut remainder) is rejected with
-//    W8A8_ERR_WORKSPACE before any launch.
+//    stream-K plan the planner makes (the largest, 128 x 128 tiles with a cut
+//    remainder, needs 19.7 MB); a plan that needs more (possible on a device
+//    with more SMs) is rejected with W8A8_ERR_WORKSPACE before any launch.
 //  * Set-up: the first accepted non-empty call on a device (with that device
 //    current) resolves the array's address with cudaGetSymbolAddress and clears
 //    the counter region, synchronously.  Make that first call before any

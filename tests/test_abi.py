@@ -147,6 +147,19 @@ def test_planner_stream_k_balances_few_tiles(pkg):
     assert p["variant"] == 7 and p["grid"] == 148 and p["workspace_bytes"] == 0
 
 
+def test_every_plan_fits_the_static_scratch(pkg):
+    """The no-allocation entry point's 20 MiB scratch covers every stream-K plan
+    the planner makes on a 148-SM device (the largest, 128 x 128 tiles with a
+    cut remainder, needs 256 KiB of counters + 2 x 148 x 64 KiB)."""
+    worst = 0
+    for m in (1, 16, 17, 32, 33, 64, 65, 100, 128, 129, 200, 256, 300, 512, 1024, 4096, 8192):
+        for n in (256, 1280, 2560, 5120, 6400, 10240, 25600, 51200):
+            for k in (512, 1024, 5120, 8192, 25600):
+                worst = max(worst, pkg.ops.gemm_plan(m, n, k, num_sms=148)["workspace_bytes"])
+    assert worst == 256 * 1024 + 2 * 148 * 128 * 128 * 4
+    assert worst <= 20 * 2 ** 20
+
+
 def test_planner_respects_workspace_limit(pkg):
     p = pkg.ops.gemm_plan(1, 4096, 12288, workspace_bytes=0)
     assert p["gran"] == p["kblocks"] and p["workspace_bytes"] == 0 and p["grid"] == 32
