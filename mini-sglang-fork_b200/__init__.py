@@ -10,7 +10,7 @@ The directory name is not a Python identifier; import it with
 """
 from __future__ import annotations
 
-from . import _lib, comm, distributed, layers, ops
+from . import _lib, comm, distributed, layers, ops, weights
 from ._lib import W8A8Error
 from .distributed import (DistributedCommunicator, DistributedInfo, destroy_distributed,
                           enable_peer_mem_distributed, get_tp_info, reset_tp_info, set_tp_info,
@@ -18,6 +18,7 @@ from .distributed import (DistributedCommunicator, DistributedInfo, destroy_dist
 from .layers import (BaseOP, GatedMLP, LinearColParallelMerged, LinearOProj, LinearQKVMerged,
                      LinearReplicated, LinearRowParallel, silu_and_mul, silu_and_mul_quant)
 from .ops import QuantizedActivation, quant_per_token, w8a8_gemm
+from .weights import load_w8a8_state_dict, w8a8_weight_stream
 
 __all__ = [
     "W8A8Error",
@@ -33,6 +34,8 @@ __all__ = [
     "silu_and_mul",
     "silu_and_mul_quant",
     "w8a8_gemm",
+    "load_w8a8_state_dict",
+    "w8a8_weight_stream",
     "DistributedCommunicator",
     "DistributedInfo",
     "set_tp_info",
