@@ -14,6 +14,7 @@
  *   - _LinearTPImpl.forward = F.linear(x, W, b)          M/layers/linear.py:31-32
  *   - LinearOProj / LinearRowParallel forward + all_reduce M/layers/linear.py:102-106,123-127
  *   - silu_and_mul(x, out)                                 M/layers/activation.py:9-12
+ *   - RMSNorm / RMSNormFused forward (+ the quantiser)     M/layers/norm.py:8-38
  *   - NCCLWrapper(rank, world, max_bytes, uid)             M/kernel/csrc/src/pynccl.cu:74-91
  *   - NCCLWrapper::all_reduce(t, "sum")                    M/kernel/csrc/src/pynccl.cu:93-134
  *   - init_pynccl (UID broadcast over the CPU group)       M/kernel/pynccl.py:45-78
@@ -68,6 +69,19 @@ int w8a8_quant_per_token(const void* x, int64_t ldx, int8_t* q, float* scale,
  * (nullable) receives the bf16 y.  Needs I % 8 == 0, ld % 8 == 0. */
 int w8a8_silu_mul_quant(const void* gate_up, int64_t ld, int8_t* q, float* scale,
                         void* y_out, int64_t M, int64_t I, void* stream);
+
+/* RMSNorm fused with the per-token quantiser: the input side of qkv and
+ * gate_up.  Replaces RMSNorm.forward / RMSNormFused.forward
+ * (M/layers/norm.py:8-38) followed by the quantiser.  x[M, K] bf16 (row stride
+ * ldx), weight[K] bf16.  With residual[M, K] (row stride ldr, nullable):
+ * v = x + residual (fp32), residual_out = bf16(v) (required; may be the
+ * residual itself); without: v = x and residual_out must be null.  Then
+ * y = bf16((v * r) * weight) with r = 1 / sqrt(sum(v*v)/K + eps) (correctly
+ * rounded), and q/scale are y's per-token quantisation.  y_out[M, K]
+ * (nullable) receives y.  Needs K % 8 == 0, K <= 8192, 16-byte alignment. */
+int w8a8_rmsnorm_quant(const void* x, int64_t ldx, const void* residual, int64_t ldr,
+                       const void* weight, float eps, int8_t* q, float* scale, void* residual_out,
+                       void* y_out, int64_t M, int64_t K, void* stream);
 
 /* ---------------------------------------------------------------- kernel 2
  * W8A8 GEMM on tcgen05 tensor cores: C[M, N] bf16 =

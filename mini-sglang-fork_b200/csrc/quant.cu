@@ -228,6 +228,137 @@ __global__ void __launch_bounds__(kSmemThreads) rows_smem_kernel(const __nv_bflo
   if (threadIdx.x == 0) scale[row] = s;
 }
 
+// ------------------------------------------------------------------ RMSNorm
+// RMSNorm (optionally after a residual add) fused with the per-token quantiser:
+// the input side of qkv and gate_up (RMSNorm / RMSNormFused,
+// M/layers/norm.py:8-38, whose flashinfer kernels compute in fp32):
+//   v = x (+ residual, fp32 add);  residual_out = bf16(v) when a residual is given
+//   r = 1 / sqrt(sum(v*v) / K + eps)   (correctly rounded sqrt and divide)
+//   y = bf16((v * r) * w)              (the normalised row, never written unless y_out)
+//   q, s = per-token quantisation of y (the rule above)
+// One CTA per row, the row in registers (K <= 8192), two block reductions.
+constexpr int kNormThreads = 256;
+constexpr int kNormMaxVec = 4 * kNormThreads;  // K <= 8192
+
+__device__ __forceinline__ float block_sum(float v, float* red) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  const int nw = (blockDim.x + 31) >> 5;
+  float r = (lane < nw) ? red[lane] : 0.0f;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) r += __shfl_xor_sync(0xffffffffu, r, o);
+  __syncthreads();  // `red` is reused by the next reduction
+  return r;
+}
+
+template <int VPT, bool ADD>
+__global__ void __launch_bounds__(kNormThreads) rmsnorm_quant_kernel(
+    const __nv_bfloat16* __restrict__ x, int64_t ldx, const __nv_bfloat16* residual, int64_t ldr,
+    const __nv_bfloat16* __restrict__ w, float eps, int8_t* __restrict__ q, float* __restrict__ scale,
+    __nv_bfloat16* residual_out, __nv_bfloat16* __restrict__ y_out, int width) {
+  __shared__ float red[32];
+  w8a8::dev::griddep_wait();  // x / residual are the previous kernel's output
+  w8a8::dev::griddep_launch();
+  const int64_t row = blockIdx.x;
+  const int nvec = width >> 3;
+  const uint4* xr = reinterpret_cast<const uint4*>(x + row * ldx);
+  const uint4* rr = ADD ? reinterpret_cast<const uint4*>(residual + row * ldr) : nullptr;
+  uint4 xa[VPT], ra[VPT];
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    const int vi = threadIdx.x + i * blockDim.x;
+    if (vi < nvec) {
+      xa[i] = __ldcs(xr + vi);
+      if constexpr (ADD) ra[i] = __ldcs(rr + vi);
+    }
+  }
+  float v[VPT][8];
+  float ss = 0.0f;
+  uint4* ro = ADD && residual_out ? reinterpret_cast<uint4*>(residual_out + row * ldr) : nullptr;
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    const int vi = threadIdx.x + i * blockDim.x;
+    if (vi >= nvec) continue;
+    const __nv_bfloat162* hx = reinterpret_cast<const __nv_bfloat162*>(&xa[i]);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      float2 f = __bfloat1622float2(hx[j]);
+      if constexpr (ADD) {
+        const float2 g = __bfloat1622float2(reinterpret_cast<const __nv_bfloat162*>(&ra[i])[j]);
+        f.x = __fadd_rn(f.x, g.x);
+        f.y = __fadd_rn(f.y, g.y);
+      }
+      v[i][2 * j] = f.x;
+      v[i][2 * j + 1] = f.y;
+      ss = __fmaf_rn(f.x, f.x, ss);
+      ss = __fmaf_rn(f.y, f.y, ss);
+    }
+    if (ro) {
+      uint4 o;
+      __nv_bfloat162* ho = reinterpret_cast<__nv_bfloat162*>(&o);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) ho[j] = __floats2bfloat162_rn(v[i][2 * j], v[i][2 * j + 1]);
+      ro[vi] = o;
+    }
+  }
+  ss = block_sum(ss, red);
+  const float r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, static_cast<float>(width)), eps)));
+  const uint4* wr = reinterpret_cast<const uint4*>(w);
+  uint4 ya[VPT];
+  float amax = 0.0f;
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    const int vi = threadIdx.x + i * blockDim.x;
+    if (vi >= nvec) continue;
+    const uint4 wv = __ldg(wr + vi);
+    const __nv_bfloat162* hw = reinterpret_cast<const __nv_bfloat162*>(&wv);
+    __nv_bfloat162* hy = reinterpret_cast<__nv_bfloat162*>(&ya[i]);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 wf = __bfloat1622float2(hw[j]);
+      hy[j] = __floats2bfloat162_rn(__fmul_rn(__fmul_rn(v[i][2 * j], r), wf.x),
+                                    __fmul_rn(__fmul_rn(v[i][2 * j + 1], r), wf.y));
+    }
+    amax = fmaxf(amax, vec8_absmax(ya[i]));
+  }
+  amax = block_max(amax, red);
+  const float s = __fdiv_rn(amax, 127.0f);
+  const float inv = s > 0.0f ? __frcp_rn(s) : 0.0f;
+  uint2* qr = reinterpret_cast<uint2*>(q + row * static_cast<int64_t>(width));
+  uint4* yr = y_out ? reinterpret_cast<uint4*>(y_out + row * static_cast<int64_t>(width)) : nullptr;
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    const int vi = threadIdx.x + i * blockDim.x;
+    if (vi >= nvec) continue;
+    qr[vi] = quant_vec8(ya[i], s, inv);
+    if (yr) yr[vi] = ya[i];
+  }
+  if (threadIdx.x == 0) scale[row] = s;
+}
+
+template <bool ADD>
+int launch_rmsnorm(const __nv_bfloat16* x, int64_t ldx, const __nv_bfloat16* res, int64_t ldr,
+                   const __nv_bfloat16* w, float eps, int8_t* q, float* scale, __nv_bfloat16* res_out,
+                   __nv_bfloat16* y, int64_t M, int width, cudaStream_t s) {
+  const int nvec = width / 8;
+  const int vpt = nvec <= kNormThreads ? 1 : (nvec <= 2 * kNormThreads ? 2 : 4);
+  const int need = (nvec + vpt - 1) / vpt;
+  const int threads = need < 32 ? 32 : ((need + 31) / 32) * 32;
+  const dim3 grid(static_cast<unsigned>(M)), block(threads);
+  switch (vpt) {
+    case 1: W8A8_CUDA_TRY(w8a8::launch_pdl(rmsnorm_quant_kernel<1, ADD>, grid, block, 0, s, x, ldx, res, ldr, w, eps,
+                                           q, scale, res_out, y, width)); break;
+    case 2: W8A8_CUDA_TRY(w8a8::launch_pdl(rmsnorm_quant_kernel<2, ADD>, grid, block, 0, s, x, ldx, res, ldr, w, eps,
+                                           q, scale, res_out, y, width)); break;
+    default: W8A8_CUDA_TRY(w8a8::launch_pdl(rmsnorm_quant_kernel<4, ADD>, grid, block, 0, s, x, ldx, res, ldr, w,
+                                            eps, q, scale, res_out, y, width)); break;
+  }
+  return W8A8_OK;
+}
+
 template <bool SILU>
 int launch_rows(const __nv_bfloat16* in, int64_t ld, int8_t* q, float* scale, __nv_bfloat16* y, int64_t M,
                 int width, cudaStream_t s) {
@@ -305,6 +436,41 @@ int w8a8_silu_mul_quant(const void* gate_up, int64_t ld, int8_t* q, float* scale
   return launch_rows<true>(static_cast<const __nv_bfloat16*>(gate_up), ld, q, scale,
                            static_cast<__nv_bfloat16*>(y_out), M, static_cast<int>(I),
                            static_cast<cudaStream_t>(stream));
+}
+
+int w8a8_rmsnorm_quant(const void* x, int64_t ldx, const void* residual, int64_t ldr, const void* weight,
+                       float eps, int8_t* q, float* scale, void* residual_out, void* y_out, int64_t M, int64_t K,
+                       void* stream) {
+  W8A8_REQUIRE(M >= 0 && K >= 0, W8A8_ERR_INVALID_ARG, "rmsnorm_quant: negative shape");
+  if (M == 0) return W8A8_OK;
+  W8A8_REQUIRE(x && weight && q && scale, W8A8_ERR_INVALID_ARG, "rmsnorm_quant: null pointer (x, weight, q, scale)");
+  W8A8_REQUIRE(K > 0 && K % 8 == 0, W8A8_ERR_INVALID_ARG, "rmsnorm_quant: K=%lld must be a positive multiple of 8",
+               (long long)K);
+  W8A8_REQUIRE(K / 8 <= kNormMaxVec, W8A8_ERR_UNSUPPORTED, "rmsnorm_quant: K=%lld exceeds the 8192 limit",
+               (long long)K);
+  W8A8_REQUIRE(ldx >= K && ldx % 8 == 0, W8A8_ERR_INVALID_ARG,
+               "rmsnorm_quant: row stride %lld must be >= K and a multiple of 8", (long long)ldx);
+  W8A8_REQUIRE(!(eps < 0.0f) && eps == eps, W8A8_ERR_INVALID_ARG, "rmsnorm_quant: eps must be >= 0");
+  W8A8_REQUIRE(M <= 0x7fffffff, W8A8_ERR_UNSUPPORTED, "rmsnorm_quant: M too large");
+  W8A8_REQUIRE(W8A8_ALIGNED16(x) && W8A8_ALIGNED16(weight) && W8A8_ALIGNED16(q) && W8A8_ALIGNED16(y_out),
+               W8A8_ERR_ALIGNMENT, "rmsnorm_quant: x, weight, q and y_out must be 16-byte aligned");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const auto* xb = static_cast<const __nv_bfloat16*>(x);
+  const auto* wb = static_cast<const __nv_bfloat16*>(weight);
+  auto* yb = static_cast<__nv_bfloat16*>(y_out);
+  if (residual == nullptr) {
+    W8A8_REQUIRE(residual_out == nullptr, W8A8_ERR_INVALID_ARG,
+                 "rmsnorm_quant: residual_out needs a residual (without one the residual is x itself)");
+    return launch_rmsnorm<false>(xb, ldx, nullptr, K, wb, eps, q, scale, nullptr, yb, M, static_cast<int>(K), s);
+  }
+  W8A8_REQUIRE(residual_out != nullptr, W8A8_ERR_INVALID_ARG,
+               "rmsnorm_quant: with a residual, residual_out (may be the residual itself) is required");
+  W8A8_REQUIRE(ldr >= K && ldr % 8 == 0, W8A8_ERR_INVALID_ARG,
+               "rmsnorm_quant: residual row stride %lld must be >= K and a multiple of 8", (long long)ldr);
+  W8A8_REQUIRE(W8A8_ALIGNED16(residual) && W8A8_ALIGNED16(residual_out), W8A8_ERR_ALIGNMENT,
+               "rmsnorm_quant: residual and residual_out must be 16-byte aligned");
+  return launch_rmsnorm<true>(xb, ldx, static_cast<const __nv_bfloat16*>(residual), ldr, wb, eps, q, scale,
+                              static_cast<__nv_bfloat16*>(residual_out), yb, M, static_cast<int>(K), s);
 }
 
 }  // extern "C"

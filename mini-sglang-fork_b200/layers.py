@@ -175,6 +175,23 @@ class LinearRowParallel(_RowParallel):
         super().__init__(input_size, output_size, div_even(input_size, tp_info.size), output_size, has_bias)
 
 
+class RMSNormFusedQuant(BaseOP):
+    """``RMSNormFused`` (M/layers/norm.py:23-38) with the following W8A8
+    layer's input quantisation fused in: ``forward(x, residual)`` returns
+    ``(QuantizedActivation, residual)`` -- the residual updated in place to
+    ``x + residual`` as ``fused_add_rmsnorm`` does, or ``x`` itself without
+    one -- and the bf16 normalised rows never reach HBM.  qkv / gate_up accept
+    the QuantizedActivation directly.  ``weight`` is the bf16 [size] norm
+    weight (state dict key ``weight``)."""
+
+    def __init__(self, size: int, eps: float) -> None:
+        self.eps = eps
+        self.weight = torch.empty(size, dtype=torch.bfloat16)
+
+    def forward(self, x: torch.Tensor, residual: Optional[torch.Tensor] = None):
+        return ops.rmsnorm_quant(x, self.weight, self.eps, residual)
+
+
 class GatedMLP(BaseOP):
     """W8A8 ``GatedMLP`` (M/models/utils.py:25-50): gate_up (column-parallel)
     -> fused SiLU*mul + per-token quant -> down (row-parallel + all-reduce).

@@ -116,6 +116,35 @@ def silu_and_mul_quant(gate_up: torch.Tensor, with_bf16: bool = False):
     return (qa, y) if with_bf16 else qa
 
 
+def rmsnorm_quant(x: torch.Tensor, weight: torch.Tensor, eps: float, residual: Optional[torch.Tensor] = None,
+                  with_bf16: bool = False):
+    """RMSNorm (after ``x + residual`` when a residual is given, updating the
+    residual in place, as ``fused_add_rmsnorm`` does) fused with the per-token
+    quantiser.  Returns ``(QuantizedActivation, residual)`` -- the residual is
+    ``x`` itself without one (M/layers/norm.py:31-38) -- plus the bf16
+    normalised rows with ``with_bf16``."""
+    _require_cuda("rmsnorm_quant", x)
+    if x.dtype != torch.bfloat16 or x.dim() != 2 or x.stride(1) != 1:
+        raise _lib.W8A8Error(_lib.ERR_INVALID_ARG, "rmsnorm_quant: x must be 2-D bf16 with unit column stride")
+    m, k = x.shape
+    if weight.dtype != torch.bfloat16 or weight.shape != (k,) or not weight.is_contiguous():
+        raise _lib.W8A8Error(_lib.ERR_INVALID_ARG, "rmsnorm_quant: weight must be a contiguous bf16 [K] vector")
+    if residual is not None and (residual.dtype != torch.bfloat16 or residual.shape != x.shape
+                                 or residual.stride(1) != 1):
+        raise _lib.W8A8Error(_lib.ERR_INVALID_ARG, "rmsnorm_quant: residual must match x (bf16, unit column stride)")
+    q = torch.empty(m, k, dtype=torch.int8, device=x.device)
+    s = torch.empty(m, dtype=torch.float32, device=x.device)
+    y = torch.empty(m, k, dtype=torch.bfloat16, device=x.device) if with_bf16 else None
+    lib = _lib.load()
+    _lib.check(lib.w8a8_rmsnorm_quant(_ptr(x), x.stride(0), _ptr(residual),
+                                      residual.stride(0) if residual is not None else k, _ptr(weight), float(eps),
+                                      _ptr(q), _ptr(s), _ptr(residual), _ptr(y), m, k, _stream(x)),
+               "rmsnorm_quant")
+    qa = QuantizedActivation(q, s)
+    res = residual if residual is not None else x
+    return (qa, res, y) if with_bf16 else (qa, res)
+
+
 def silu_and_mul(x: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
     """bf16 ``silu(x[:, :I]) * x[:, I:]`` — the signature of ``silu_and_mul``
     (M/layers/activation.py:9-12), computed by the fused kernel."""

@@ -52,6 +52,20 @@ def test_host_validation_rejects_bad_arguments(pkg):
     assert st == L.ERR_ALIGNMENT
     st = lib.w8a8_silu_mul_quant(16, 10, 16, 16, None, 2, 12, None)
     assert st == L.ERR_INVALID_ARG
+    # fused RMSNorm + quant: null weight, K % 8, K above 8192, residual_out without a residual
+    st = lib.w8a8_rmsnorm_quant(16, 16, None, 16, None, 1e-6, 16, 16, None, None, 4, 16, None)
+    assert st == L.ERR_INVALID_ARG and b"null" in lib.w8a8_last_error()
+    st = lib.w8a8_rmsnorm_quant(16, 16, None, 16, 16, 1e-6, 16, 16, None, None, 4, 12, None)
+    assert st == L.ERR_INVALID_ARG and b"multiple of 8" in lib.w8a8_last_error()
+    st = lib.w8a8_rmsnorm_quant(16, 16384, None, 16, 16, 1e-6, 16, 16, None, None, 4, 16384, None)
+    assert st == L.ERR_UNSUPPORTED and b"8192" in lib.w8a8_last_error()
+    st = lib.w8a8_rmsnorm_quant(16, 16, None, 16, 16, 1e-6, 16, 16, 16, None, 4, 16, None)
+    assert st == L.ERR_INVALID_ARG and b"residual_out" in lib.w8a8_last_error()
+    st = lib.w8a8_rmsnorm_quant(16, 16, 16, 16, 16, 1e-6, 16, 16, None, None, 4, 16, None)
+    assert st == L.ERR_INVALID_ARG and b"residual_out" in lib.w8a8_last_error()
+    st = lib.w8a8_rmsnorm_quant(16, 16, None, 16, 16, -1.0, 16, 16, None, None, 4, 16, None)
+    assert st == L.ERR_INVALID_ARG and b"eps" in lib.w8a8_last_error()
+    assert lib.w8a8_rmsnorm_quant(None, 16, None, 16, None, 1e-6, None, None, None, None, 0, 16, None) == L.OK
     # empty batches are a no-op success, as F.linear on an empty input
     assert lib.w8a8_quant_per_token(None, 16, None, None, 0, 16, None) == L.OK
     assert lib.w8a8_silu_mul_quant(None, 32, None, None, None, 0, 16, None) == L.OK

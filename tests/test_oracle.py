@@ -161,3 +161,20 @@ def test_int_gemm_exact(oracle, m, k, n):
     a = torch.randint(-127, 128, (m, k), generator=g, dtype=torch.int8)
     b = torch.randint(-127, 128, (n, k), generator=g, dtype=torch.int8)
     assert torch.equal(oracle.int_gemm(a, b).to(torch.int64), oracle.int_gemm_int64(a, b))
+
+
+def test_rmsnorm_restatement_matches_torch_rms_norm(oracle):
+    """The oracle's RMSNorm (fp32, correctly rounded 1/sqrt) against torch's
+    own fp32 rms_norm, before the common bf16 rounding: same to fp32 noise."""
+    g = torch.Generator().manual_seed(4)
+    x = torch.randn(16, 512, generator=g).bfloat16()
+    r = torch.randn(16, 512, generator=g).bfloat16()
+    w = (1 + 0.1 * torch.randn(512, generator=g)).bfloat16()
+    y, res = oracle.rmsnorm(x, w, 1e-6, r)
+    v = x.float() + r.float()
+    ref = torch.nn.functional.rms_norm(v, (512,), w.float(), 1e-6)
+    assert torch.equal(res, v.bfloat16())
+    torch.testing.assert_close(y.float(), ref, atol=0, rtol=2 ** -7)
+    q, s, y2, res2 = oracle.rmsnorm_quant(x, w, 1e-6)
+    assert res2 is x and torch.equal(y2, oracle.rmsnorm(x, w, 1e-6)[0])
+    assert torch.equal((q, s)[0], oracle.quant_per_token(y2)[0])
