@@ -216,6 +216,39 @@ def _scn_timeout_status(pkg, O, rank, world, dev, dist):
     return err
 
 
+def _scn_fused_timeout_status(pkg, O, rank, world, dev, dist):
+    """Rank 0 issues fused GEMM + all-reduce calls that the other ranks skip:
+    its reduce groups' bounded flag waits run out (~0.3 s each) and the host
+    reads the error status; the GEMM warps never wait on a flag, so the kernel
+    ends by itself.  Both the pair kernel (M=2048) and a swap-AB tile (M=64)."""
+    comm = pkg.comm.PeerMemCommunicator(rank, world, 2048 * 5120 * 2, device=dev, timeout_ms=300)
+    g = torch.Generator().manual_seed(5)
+    shapes = [(64, 1024, 256), (2048, 5120, 256)]
+    ops = []
+    for m, n, k in shapes:
+        a = torch.randint(-127, 128, (m, k), generator=g, dtype=torch.int8).to(dev)
+        w = torch.randint(-127, 128, (n, k), generator=g, dtype=torch.int8).to(dev)
+        sa, sw = (torch.rand(m, generator=g) * 1e-3).to(dev), (torch.rand(n, generator=g) * 1e-3).to(dev)
+        ops.append((a, w, sa, sw))
+    for a, w, sa, sw in ops:  # normal calls first, on every rank
+        comm.gemm_allreduce(a, w, sa, sw)
+    torch.cuda.synchronize()
+    assert comm.device_error() == 0
+    dist.barrier()
+    errs = []
+    if rank == 0:
+        for a, w, sa, sw in ops:
+            comm.gemm_allreduce(a, w, sa, sw)
+            torch.cuda.synchronize()
+            errs.append(comm.device_error())
+            pkg.ops.device_error(clear=True)
+        assert all(e != 0 for e in errs), errs
+        assert float(torch.ones(8, device=dev).sum()) == 8.0  # the context is still usable
+    dist.barrier()
+    comm.close()
+    return errs
+
+
 # ---------------------------------------------------------------------- tests
 def test_allreduce_known_answers():
     _run("known_answers")
@@ -236,3 +269,8 @@ def test_row_parallel_layer_and_cuda_graph():
 def test_flag_wait_timeout_reported():
     res = _run("timeout_status")
     assert res[0] != 0
+
+
+def test_fused_flag_wait_timeout_reported():
+    res = _run("fused_timeout_status")
+    assert len(res[0]) == 2 and all(e != 0 for e in res[0])
