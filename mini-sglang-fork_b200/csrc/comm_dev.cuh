@@ -97,11 +97,8 @@ __device__ __forceinline__ void signal_peers(const CommView& v, int phase, int s
 
 // Thread `t` (< world) waits until rank t has signalled (phase, slot) of call
 // `epoch`.  Bounded by v.timeout_ns; on expiry records where and returns false.
-// A non-null `abort` (this CTA's GEMM gave up, its error already recorded)
-// also ends the wait with false.  Polls back off with a short sleep, since the
-// waiting warps share the SM with GEMM warps.
-__device__ __forceinline__ bool wait_peer(const CommView& v, int phase, int slot, uint32_t epoch, int t,
-                                          const volatile int* abort = nullptr) {
+// Polls back off with a short sleep after the first few.
+__device__ __forceinline__ bool wait_peer(const CommView& v, int phase, int slot, uint32_t epoch, int t) {
   if (t >= v.world) return true;
   const uint32_t* f = flag_ptr(v.base[v.rank], phase, slot, t);
   if (ld_acquire_sys(f) == epoch) return true;
@@ -109,7 +106,6 @@ __device__ __forceinline__ bool wait_peer(const CommView& v, int phase, int slot
   for (uint32_t it = 1;; ++it) {
     if (ld_acquire_sys(f) == epoch) return true;
     if ((it & 255u) == 0) {
-      if (abort != nullptr && *abort != 0) return false;
       if (globaltimer_ns() - t0 > static_cast<uint64_t>(v.timeout_ns)) {
         if (v.err) atomicOr(v.err, 2u /* kErrCommWait */);
         uint32_t* c = ctrl_ptr(v.base[v.rank]);
