@@ -57,9 +57,10 @@ __device__ __forceinline__ char* half_ptr(const CommView& v, int r, uint32_t epo
 }
 
 // Inside a data half, the fused GEMM reduce uses world receive slots (slot s
-// holds source rank s's partial rows, same [M, N] layout as C) followed by
-// one all-gather slot (reduced rows pushed by their owners, two-shot only).
-// The standalone all-reduce uses the start of the half (slot 0).
+// holds source rank s's bf16 partial tiles, in the tile-blocked layout the
+// fused epilogue pushes: tile t at t * 128 * BN * 2 bytes) followed by one
+// gather slot (reduced row shares pushed by their owners, two-shot only, same
+// layout).  The standalone all-reduce uses the start of the half (slot 0).
 __device__ __forceinline__ char* recv_slot(const CommView& v, int at_rank, int src, uint32_t epoch) {
   return half_ptr(v, at_rank, epoch) + static_cast<size_t>(src) * v.slot_bytes;
 }
