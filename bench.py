@@ -24,6 +24,7 @@ import os
 import statistics
 import subprocess
 import sys
+import tempfile
 import time
 from datetime import timedelta
 
@@ -79,9 +80,9 @@ class ClockSampler:
               "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
               "clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, device_index: int):
+    def __init__(self, device_index: int, out_dir: str):
         self.proc = None
-        self.path = os.path.join(ROOT, "gpurun_out", f"clocks_rank{device_index}.csv")
+        self.path = os.path.join(out_dir, f"clocks_rank{device_index}.csv")
         target = str(device_index)
         try:
             uuid = str(torch.cuda.get_device_properties(device_index).uuid)
@@ -326,7 +327,7 @@ def run_ours(args, rank, world, dev):
     if world > 1:
         torch.distributed.barrier()
     torch.cuda.synchronize()
-    with ClockSampler(dev.index) as clk:
+    with ClockSampler(dev.index, args.clocks_dir) as clk:
         total_ms, per_ms, _ = time_graph(lambda: stack.forward(x), args.steps, args.warmup, flush_buf, stream)
         total_ms = max_over_ranks(total_ms, world, dev)
         ms_per_step = total_ms / args.steps
@@ -494,6 +495,8 @@ def main():
     ap.add_argument("--sweep", type=lambda s: [int(v) for v in s.split(",") if v], default=[1, 32, 128, 256])
     ap.add_argument("--nccl-baseline", action="store_true", help="row-parallel reduce through NCCL instead of fused")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--clocks-dir", default=tempfile.gettempdir(),
+                    help="where the raw nvidia-smi samples of the timed region are written")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
 

@@ -145,6 +145,11 @@ int run_gemm(const int8_t* A, const int8_t* B, const float* sa, const float* sb,
                  "gemm_allreduce: output of %lld x %lld bf16 exceeds the communicator's max_bytes %llu",
                  (long long)M, (long long)N, comm->slot_bytes);
     W8A8_REQUIRE(c_i32 == nullptr, W8A8_ERR_INVALID_ARG, "gemm_allreduce: no int32 output in fused mode");
+    // a CTA hands over at most its share of whole tiles plus two stream-K
+    // fix-ups; the hand-over ring must hold them all without reuse
+    W8A8_REQUIRE((p.num_tiles + p.grid - 1) / p.grid + 2 <= kSignalRing, W8A8_ERR_UNSUPPORTED,
+                 "gemm_allreduce: %d tiles over %d CTAs exceed the %d-tile hand-over ring", p.num_tiles, p.grid,
+                 kSignalRing);
     // receive slots hold whole (padded) tiles
     W8A8_REQUIRE(static_cast<unsigned long long>(p.num_tiles) * 128 * p.bn * 2 <= comm->slot_bytes,
                  W8A8_ERR_INVALID_ARG,
