@@ -340,6 +340,7 @@ __device__ __forceinline__ bool signal_pump(FusedState* q, const CommView& cv, u
                  : "=r"(old)
                  : "r"(dev::smem_u32(&q->taken)), "r"(n)
                  : "memory");
+    (void)old;  // only the update matters
   }
   return closed != 0;
 }
