@@ -148,6 +148,38 @@ def test_hybrid_schedule_covers_every_iteration_once(tiles, kblocks, grid):
     assert max(work) - min(work) <= max(1, kblocks if (tiles % grid) * kblocks < grid else 1)
 
 
+def test_hybrid_schedule_randomized_sweep():
+    """The same invariants over a seeded sweep of (tiles, k blocks, grid):
+    every iteration once; a cut tile's CTAs are contiguous with distinct
+    workspace slots; at most two CTAs per tile once there is a full wave."""
+    import random
+
+    rng = random.Random(1234)
+    for _ in range(300):
+        grid = rng.choice([1, 2, 3, 7, 16, 64, 74, 128, 148])
+        tiles = rng.randint(1, 6 * grid + 5)
+        kblocks = rng.randint(1, 64)
+        grid = min(grid, tiles * kblocks)
+        frags, begin, owner = _schedule(tiles, kblocks, grid)
+        seen = {}
+        for c, f in enumerate(frags):
+            for (t, k0, k1) in f:
+                for k in range(k0, k1):
+                    assert (t, k) not in seen
+                    seen[(t, k)] = c
+        assert len(seen) == tiles * kblocks, (tiles, kblocks, grid)
+        for t in range(tiles):
+            owners = sorted({seen[(t, k)] for k in range(kblocks)})
+            if len(owners) == 1:
+                continue
+            assert owners == list(range(owners[0], owners[-1] + 1))
+            assert (owner(t * kblocks), owner(t * kblocks + kblocks - 1)) == (owners[0], owners[-1])
+            if tiles >= grid:
+                assert len(owners) <= 2, (tiles, kblocks, grid, t)
+            slots = {2 * c + (1 if begin[c] < t * kblocks else 0) for c in owners}
+            assert len(slots) == len(owners)
+
+
 def test_planner_stream_k_balances_few_tiles(pkg):
     # decode: down_proj of the Qwen3-8B MLP has only 32 weight tiles; stream-K
     # still spreads its 3072 k-block iterations over every SM
