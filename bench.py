@@ -464,7 +464,8 @@ def run_reference(args, rank, world):
 
 def run_kernel_only(args, dev):
     """Profiling entry: three rounds of [quantiser, gate_up GEMM, fused
-    SiLU*mul+quant] at the headline shape on one GPU, no graphs, no timing."""
+    SiLU*mul+quant], then three of the fused residual-add + RMSNorm +
+    quantiser, at the headline shape on one GPU, no graphs, no timing."""
     pkg = _pkg()
     D = pkg.distributed
     D.reset_tp_info()
@@ -479,6 +480,10 @@ def run_kernel_only(args, dev):
         q, s = pkg.ops.quant_per_token(x)
         y = pkg.ops.w8a8_gemm(q, wq, s, ws)
         pkg.ops.silu_and_mul_quant(y)
+    res = torch.randn(args.m, k, device=dev, generator=g).bfloat16()
+    wn = torch.ones(k, device=dev).bfloat16()
+    for _ in range(3):
+        pkg.ops.rmsnorm_quant(x, wn, 1e-6, res)
     torch.cuda.synchronize()
     assert pkg.ops.device_error() == 0
     print(json.dumps({"kernel_only": True, "m": args.m, "n": n, "k": k}))
