@@ -1,15 +1,26 @@
 """Benchmark of the W8A8 tensor-parallel linear path on B200.
 
 Workload: the four quantised linears of one Qwen3-32B
-decoder layer at TP = N — qkv (column-parallel) -> o_proj (row-parallel +
+decoder layer at TP = N -- qkv (column-parallel) -> o_proj (row-parallel +
 all-reduce) -> gate_up (column-parallel) -> fused SiLU*mul + per-token quant
 -> down (row-parallel + all-reduce).  Attention is not part of the path: the
 q slice of the qkv output stands in for the attention output that feeds
 o_proj.  hidden 5120, 64 q / 8 kv heads x 128, intermediate 25600.  A step is
 one pass of that stack over M tokens (headline M = 4096, the prefill chunk;
-the decode sizes M = 1, 32, 128, 256 are reported in ``sweep``).  Synthetic
-seeded data: activations ~N(0, 1) bf16, weights ~N(0, 0.02) bf16 quantised per
-output channel by the library's own quantiser.
+the decode sizes M = 1, 32, 128, 256 are reported in ``sweep``).
+
+Synthetic seeded data: activations ~N(0, 1) bf16; a synthetic bf16
+checkpoint (~N(0, 0.02) per projection, q/k/v/o/gate/up/down, the same on
+every rank) goes through the package's own loader, which quantises each
+UNSHARDED weight per output channel and shards and merges it exactly as the
+reference's loader shards bf16 weights -- so the benchmarked layers are the
+ones a real load builds.
+
+After timing, the same layers' outputs on a fixed sample of rows are checked
+against the CPU oracle at every N (``parity``), a per-op breakdown is timed
+(``breakdown_us``), and at N > 1 the row-parallel reduce is also run through
+the reference's own NCCL path -- ``ncclMemAlloc`` + symmetric window +
+``ncclAllReduce`` with the copies in and out (``nccl_baseline``).
 
 Usage:  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 For N > 1 launch one rank per GPU with torchrun (RANK / WORLD_SIZE from env).
@@ -18,6 +29,7 @@ Prints one JSON line on rank 0.
 from __future__ import annotations
 
 import argparse
+import ctypes
 import importlib
 import json
 import os
@@ -38,6 +50,19 @@ METRIC = "W8A8 TP-layer tokens/s (Qwen3-32B decoder-layer linears: qkv, o_proj+A
 UNIT = "tokens/s"
 L2_FLUSH_BYTES = 256 << 20
 INT8_NOMINAL_TOPS = 4500.0
+L2_NOTE = "flushed (256 MB write) before every timed step; per-step CUDA-event timing of a CUDA-graph replay"
+
+# The synthetic checkpoint of one decoder layer: projection -> (module, N, K).
+PROJ = {
+    "q_proj": ("self_attn", NQ * HEAD_DIM, HIDDEN),
+    "k_proj": ("self_attn", NKV * HEAD_DIM, HIDDEN),
+    "v_proj": ("self_attn", NKV * HEAD_DIM, HIDDEN),
+    "o_proj": ("self_attn", HIDDEN, NQ * HEAD_DIM),
+    "gate_proj": ("mlp", INTER, HIDDEN),
+    "up_proj": ("mlp", INTER, HIDDEN),
+    "down_proj": ("mlp", HIDDEN, INTER),
+}
+PREFIX = "model.layers.0."
 
 
 def _pkg():
@@ -70,6 +95,26 @@ def layer_ops(tp: int):
     ops_per_token = sum(2 * n * k for n, k in sh.values())
     wbytes = sum(n * k + 4 * n for n, k in sh.values())
     return ops_per_token, wbytes
+
+
+def workload_config(world: int, m: int):
+    """The workload keys both arms (GPU and the CPU reference) report."""
+    return {"workload": "cfg3 Qwen3-32B decoder-layer W8A8 linears, TP=N, headline M = prefill chunk",
+            "M": m, "hidden": HIDDEN, "heads": [NQ, NKV], "head_dim": HEAD_DIM, "intermediate": INTER,
+            "parallelism": f"tp{world}"}
+
+
+def full_weight(name: str, dev: torch.device) -> torch.Tensor:
+    """The synthetic bf16 checkpoint tensor of one projection (identical on every rank)."""
+    _, n, k = PROJ[name]
+    g = torch.Generator(device=dev).manual_seed(1000 + list(PROJ).index(name))
+    return (torch.randn(n, k, device=dev, generator=g) * 0.02).bfloat16()
+
+
+def checkpoint_items(dev: torch.device):
+    """(name, tensor) pairs as safetensors yields them, one projection at a time."""
+    for name, (module, _, _) in PROJ.items():
+        yield f"{PREFIX}{module}.{name}.weight", full_weight(name, dev)
 
 
 # --------------------------------------------------------------------------- clocks
@@ -140,10 +185,11 @@ class ClockSampler:
                 "power_w_max": max(r[2] for r in rows)}
 
 
-# --------------------------------------------------------------------------- our arm
+# --------------------------------------------------------------------------- the layer stack
 class Stack:
     """The four W8A8 layers of one decoder layer on this rank, built through
-    the package's public layer classes and loaded with load_state_dict."""
+    the package's public layer classes and loaded from the synthetic
+    checkpoint with the package's loader (quantise unsharded, then shard)."""
 
     def __init__(self, pkg, tp: int, rank: int, dev: torch.device):
         L = pkg.layers
@@ -153,13 +199,13 @@ class Stack:
         self.gate_up = L.LinearColParallelMerged(HIDDEN, [INTER, INTER], has_bias=False)
         self.down = L.LinearRowParallel(INTER, HIDDEN, has_bias=False)
         self.q_cols = (NQ // tp) * HEAD_DIM
-        g = torch.Generator(device=dev).manual_seed(1000 + 8 * rank)
-        for i, layer in enumerate((self.qkv, self.o_proj, self.gate_up, self.down)):
-            n, k = layer.weight.shape
-            w = (torch.randn(n, k, device=dev, generator=g) * 0.02).bfloat16()
-            wq, ws = pkg.ops.quant_per_token(w)  # per-output-channel = per-row rule
-            del w
-            layer.load_state_dict({"weight": wq, "weight_scale": ws})
+        state = pkg.load_w8a8_state_dict(checkpoint_items(dev), rank, tp, NKV, device=dev)
+        for layer, key in ((self.qkv, "self_attn.qkv_proj"), (self.o_proj, "self_attn.o_proj"),
+                           (self.gate_up, "mlp.gate_up_proj"), (self.down, "mlp.down_proj")):
+            layer.load_state_dict({"weight": state.pop(f"{PREFIX}{key}.weight"),
+                                   "weight_scale": state.pop(f"{PREFIX}{key}.weight_scale")})
+        assert not state, sorted(state)
+        torch.cuda.synchronize()
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         qkv = self.qkv.forward(x)
@@ -169,9 +215,109 @@ class Stack:
         y = self.pkg.ops.silu_and_mul_quant(gu)
         return self.down.forward(y)
 
+    def forward_traced(self, x: torch.Tensor):
+        """forward, keeping every layer's input and output (parity check)."""
+        t = {"x": x}
+        t["qkv"] = self.qkv.forward(x)
+        t["attn"] = t["qkv"][:, : self.q_cols]
+        t["h"] = self.o_proj.forward(t["attn"])
+        t["gu"] = self.gate_up.forward(t["h"])
+        qa = self.pkg.ops.silu_and_mul_quant(t["gu"])
+        t["q"], t["s"] = qa.q, qa.s
+        t["out"] = self.down.forward(qa)
+        return t
+
+    def forward_nccl(self, x: torch.Tensor, nccl) -> torch.Tensor:
+        """The same stack with the row-parallel reduce through ``nccl`` (the
+        reference's path: GEMM, then an all-reduce call) instead of fused."""
+        ops = self.pkg.ops
+        qkv = self.qkv.forward(x)
+        qa = self.o_proj._quantize_input(qkv[:, : self.q_cols])
+        h = nccl.all_reduce(ops.w8a8_gemm(qa.q, self.o_proj.weight, qa.s, self.o_proj.weight_scale))
+        gu = self.gate_up.forward(h)
+        y = ops.silu_and_mul_quant(gu)
+        return nccl.all_reduce(ops.w8a8_gemm(y.q, self.down.weight, y.s, self.down.weight_scale))
+
     launches_per_step = 8  # 3 quantisers + 1 fused silu*mul+quant + 4 GEMMs (reduce fused or NCCL)
 
 
+# --------------------------------------------------------------------------- the reference's NCCL path
+class NcclUniqueId(ctypes.Structure):
+    _fields_ = [("internal", ctypes.c_char * 128)]
+
+
+class SymmetricNcclAllReduce:
+    """The reference's PyNCCL all-reduce, for the measured NCCL bar:
+    ``ncclCommInitRank`` with a unique id broadcast from rank 0,
+    ``ncclMemAlloc`` + ``ncclCommWindowRegister(NCCL_WIN_COLL_SYMMETRIC)`` of
+    a max_bytes buffer, and per call a device copy into the window, an
+    in-place ``ncclAllReduce`` (bf16, sum) and a copy back
+    (M/kernel/csrc/src/pynccl.cu:74-134), driven through ctypes on the NCCL
+    library torch ships."""
+
+    NCCL_BF16, NCCL_SUM, WIN_SYMMETRIC, D2D = 9, 0, 0x01, 3
+
+    def __init__(self, rank: int, world: int, max_bytes: int):
+        import nvidia.cuda_runtime
+        import nvidia.nccl
+
+        self.nccl = ctypes.CDLL(os.path.join(list(nvidia.nccl.__path__)[0], "lib", "libnccl.so.2"))
+        self.cudart = ctypes.CDLL(os.path.join(list(nvidia.cuda_runtime.__path__)[0], "lib", "libcudart.so.12"))
+        vp = ctypes.c_void_p
+        self.nccl.ncclCommInitRank.argtypes = [ctypes.POINTER(vp), ctypes.c_int, NcclUniqueId, ctypes.c_int]
+        self.nccl.ncclMemAlloc.argtypes = [ctypes.POINTER(vp), ctypes.c_size_t]
+        self.nccl.ncclCommWindowRegister.argtypes = [vp, vp, ctypes.c_size_t, ctypes.POINTER(vp), ctypes.c_int]
+        self.nccl.ncclCommWindowDeregister.argtypes = [vp, vp]
+        self.nccl.ncclAllReduce.argtypes = [vp, vp, ctypes.c_size_t, ctypes.c_int, ctypes.c_int, vp, vp]
+        self.nccl.ncclMemFree.argtypes = [vp]
+        self.nccl.ncclCommDestroy.argtypes = [vp]
+        self.nccl.ncclGetErrorString.restype = ctypes.c_char_p
+        self.cudart.cudaMemcpyAsync.argtypes = [vp, vp, ctypes.c_size_t, ctypes.c_int, vp]
+        self.max_bytes = int(max_bytes)
+        uid = NcclUniqueId()
+        if rank == 0:
+            self._check(self.nccl.ncclGetUniqueId(ctypes.byref(uid)), "ncclGetUniqueId")
+        obj = [bytes(uid.internal) if rank == 0 else None]
+        torch.distributed.broadcast_object_list(obj, src=0)
+        ctypes.memmove(uid.internal, obj[0], 128)
+        self.comm, self.buf, self.win = vp(), vp(), vp()
+        self._check(self.nccl.ncclCommInitRank(ctypes.byref(self.comm), world, uid, rank), "ncclCommInitRank")
+        self._check(self.nccl.ncclMemAlloc(ctypes.byref(self.buf), self.max_bytes), "ncclMemAlloc")
+        self._check(self.nccl.ncclCommWindowRegister(self.comm, self.buf, self.max_bytes, ctypes.byref(self.win),
+                                                     self.WIN_SYMMETRIC), "ncclCommWindowRegister")
+
+    def version(self) -> int:
+        v = ctypes.c_int(0)
+        self.nccl.ncclGetVersion(ctypes.byref(v))
+        return v.value
+
+    def _check(self, rc: int, what: str) -> None:
+        if rc != 0:
+            raise RuntimeError(f"{what} failed: {self.nccl.ncclGetErrorString(rc).decode()}")
+
+    def all_reduce(self, x: torch.Tensor) -> torch.Tensor:
+        nbytes = x.numel() * x.element_size()
+        if nbytes > self.max_bytes:
+            raise RuntimeError("tensor larger than the symmetric window")
+        st = torch.cuda.current_stream(x.device).cuda_stream
+        if self.cudart.cudaMemcpyAsync(self.buf, x.data_ptr(), nbytes, self.D2D, st) != 0:
+            raise RuntimeError("cudaMemcpyAsync into the window failed")
+        self._check(self.nccl.ncclAllReduce(self.buf, self.buf, x.numel(), self.NCCL_BF16, self.NCCL_SUM,
+                                            self.comm, st), "ncclAllReduce")
+        if self.cudart.cudaMemcpyAsync(x.data_ptr(), self.buf, nbytes, self.D2D, st) != 0:
+            raise RuntimeError("cudaMemcpyAsync out of the window failed")
+        return x
+
+    def close(self) -> None:
+        if self.comm.value:
+            torch.cuda.synchronize()
+            self.nccl.ncclCommWindowDeregister(self.comm, self.win)
+            self.nccl.ncclMemFree(self.buf)
+            self.nccl.ncclCommDestroy(self.comm)
+            self.comm = ctypes.c_void_p()
+
+
+# --------------------------------------------------------------------------- timing helpers
 def _flush(buf):
     buf.add_(1)
 
@@ -251,75 +397,303 @@ def _read_traffic(m: int, n: int, k: int):
     return None
 
 
-def cpu_oracle_sample(tp: int, budget_s: float = 15.0):
-    """Time the CPU oracle (the restated reference path) on a bounded sample of
-    the same workload: all TP ranks' shards of the four linears, sequentially,
-    with every host thread.  Returns (tokens/s, description, threads)."""
+def int8_peak(pkg, stream, reps: int = 3):
+    """Measured int8 tensor-core ceiling: the library's MMA-only probe (1-SM
+    128x256 and 2-SM 256x256 shapes), best of `reps` launches of each."""
+    lib = pkg.load_library()
+    best = {}
+    for pair in (0, 1):
+        ops = ctypes.c_int64(0)
+        times = []
+        with torch.cuda.stream(stream):
+            for _ in range(reps + 1):
+                s = torch.cuda.Event(enable_timing=True)
+                e = torch.cuda.Event(enable_timing=True)
+                s.record(stream)
+                pkg._lib.check(lib.w8a8_mma_peak_probe(pair, 40000, ctypes.byref(ops), stream.cuda_stream),
+                               "mma_peak_probe")
+                e.record(stream)
+                times.append((s, e))
+        torch.cuda.synchronize()
+        ms = min(s.elapsed_time(e) for s, e in times[1:])
+        best["pair" if pair else "single"] = round(ops.value / (ms * 1e-3) / 1e12, 1)
+    return best
+
+
+# --------------------------------------------------------------------------- parity vs the oracle
+def sample_rows(m: int):
+    """A fixed sample of token rows: two per 128-row tile (one pseudo-random,
+    one at the tile's end), so every output tile of every GEMM is checked."""
+    rows = set()
+    for t in range((m + 127) // 128):
+        lo, hi = t * 128, min(m, t * 128 + 128)
+        rows.add(lo + (t * 53 + 17) % (hi - lo))
+        rows.add(hi - 1)
+    return sorted(rows)
+
+
+def collect_trace(pkg, stack, x, rows, world):
+    """Every rank's sampled rows of each layer's input and output, plus the
+    gate_up GEMM's int32 accumulator and the quantiser's outputs for the
+    sampled inputs; all ranks' traces on every rank (CPU tensors)."""
+    ops = pkg.ops
+    idx = torch.tensor(rows, device=x.device)
+    t = stack.forward_traced(x)
+    qh = ops.quant_per_token(t["h"])
+    acc = torch.empty(x.shape[0], stack.gate_up.weight.shape[0], dtype=torch.int32, device=x.device)
+    gu2 = ops.w8a8_gemm(qh[0], stack.gate_up.weight, qh[1], stack.gate_up.weight_scale, out_i32=acc)
+    xq = ops.quant_per_token(x.index_select(0, idx))
+    torch.cuda.synchronize()
+    mine = {k: v.index_select(0, idx).cpu() for k, v in t.items()}
+    mine["gu_i32"] = acc.index_select(0, idx).cpu()
+    mine["gu_again_equal"] = bool(torch.equal(gu2.index_select(0, idx), t["gu"].index_select(0, idx)))
+    mine["xq"], mine["xs"] = xq[0].cpu(), xq[1].cpu()
+    mine["wq_qkv_head"] = stack.qkv.weight[:4].cpu()
+    mine["ws_qkv"] = stack.qkv.weight_scale.cpu()
+    del acc, gu2, t
+    if world == 1:
+        return [mine]
+    everyone = [None] * world
+    torch.distributed.all_gather_object(everyone, mine)
+    return everyone
+
+
+def oracle_parity(traces, tp: int, dev: torch.device):
+    """Recompute every layer on the sampled rows with the CPU oracle from each
+    layer's actual input, and compare (int8 / int32 / bf16 bit for bit; the
+    SiLU*mul quantiser's int8 within one step on at most 0.1 % of elements,
+    since its bf16 product may differ from the CPU's by one ulp)."""
     from oracle import w8a8_oracle as O
 
-    threads = torch.get_num_threads()
-    sh = local_shapes(tp)
-    g = torch.Generator().manual_seed(0)
-    weights = {}
-    for name, (n, k) in sh.items():
-        weights[name] = [(torch.randint(-127, 128, (n, k), generator=g, dtype=torch.int8),
-                          torch.rand(n, generator=g) * 1e-3 + 1e-5) for _ in range(1)]
+    W = {}
+    for name in PROJ:
+        W[name] = O.quant_weight_per_channel(full_weight(name, dev).cpu())
 
-    def run(m):
-        x = torch.randn(m, HIDDEN, generator=g).bfloat16()
-        for _r in range(tp):  # every rank's shard is the same size; rank 0's weights stand in
-            wq, ws = weights["qkv"][0]
-            _, _, _, qkv = O.w8a8_linear(x, wq, ws)
-            attn = qkv[:, : (NQ // tp) * HEAD_DIM].contiguous()
-            wq, ws = weights["o_proj"][0]
-            h = O.w8a8_linear(attn, wq, ws)[3]
-        h = O.all_reduce_sum([h] * tp)
-        for _r in range(tp):
-            wq, ws = weights["gate_up"][0]
-            gu = O.w8a8_linear(h, wq, ws)[3]
-            q, s, _ = O.silu_mul_quant(gu)
-            wq, ws = weights["down"][0]
-            out = O.dequant(O.int_gemm(q, wq), s, ws)
-        return O.all_reduce_sum([out] * tp)
+    def shard(name, r):
+        key = "." + name
+        return O.shard_tensor(key, W[name][0], r, tp, NKV), O.shard_scale(key, W[name][1], r, tp, NKV)
 
-    m = 16
-    t0 = time.perf_counter()
-    run(m)
-    t1 = time.perf_counter()
-    per = max(t1 - t0, 1e-3)
-    m = int(max(16, min(4096, m * (budget_s / 4.0) / per)))
-    times = []
-    t_end = time.perf_counter() + budget_s
-    while time.perf_counter() < t_end or len(times) < 2:
-        t0 = time.perf_counter()
-        run(m)
-        times.append(time.perf_counter() - t0)
-        if len(times) >= 10:
-            break
-    med = statistics.median(times)
-    desc = (f"{m} tokens through all {tp} rank shard(s) of the 4 W8A8 linears + SiLU*mul quant "
-            f"(oracle: torch._int_mm on CPU), median of {len(times)} runs")
-    return m / med, desc, threads
+    bad = []
+    max_err = 0.0
+
+    def cmp(what, got, want):
+        nonlocal max_err
+        if not torch.equal(got, want):
+            err = float((got.float() - want.float()).abs().max())
+            max_err = max(max_err, err)
+            bad.append(f"{what}: max |diff| {err:.3g}")
+
+    t0 = traces[0]
+    q_ref, s_ref = O.quant_per_token(t0["x"])
+    cmp("quantiser x int8", t0["xq"], q_ref)
+    cmp("quantiser x scale", t0["xs"], s_ref)
+    i32_ok = True
+    silu_mismatch = 0.0
+    for r in range(tp):
+        parts = [shard(n, r) for n in ("q_proj", "k_proj", "v_proj")]
+        wq = torch.cat([p[0] for p in parts])
+        ws = torch.cat([p[1] for p in parts])
+        cmp(f"loader weight shard r{r}", traces[r]["wq_qkv_head"], wq[:4])
+        cmp(f"loader weight scales r{r}", traces[r]["ws_qkv"], ws)
+        cmp(f"qkv r{r}", traces[r]["qkv"], O.w8a8_linear(traces[r]["x"], wq, ws)[3])
+    attn_full = torch.cat([traces[r]["attn"] for r in range(tp)], dim=1)
+    h_ref = O.tp_linear("row", attn_full, W["o_proj"][0], W["o_proj"][1], tp, key=".o_proj")[0]
+    for r in range(tp):
+        cmp(f"o_proj+allreduce r{r}", traces[r]["h"], h_ref)
+        gate, up = shard("gate_proj", r), shard("up_proj", r)
+        wq, ws = torch.cat([gate[0], up[0]]), torch.cat([gate[1], up[1]])
+        _, _, acc, gu = O.w8a8_linear(traces[r]["h"], wq, ws)
+        cmp(f"gate_up r{r}", traces[r]["gu"], gu)
+        if not torch.equal(traces[r]["gu_i32"], acc):
+            i32_ok = False
+            bad.append(f"gate_up int32 r{r}")
+        if not traces[r]["gu_again_equal"]:
+            bad.append(f"gate_up repeat r{r}")
+        q, s, _ = O.silu_mul_quant(traces[r]["gu"])
+        dq = (traces[r]["q"].int() - q.int()).abs()
+        silu_mismatch = max(silu_mismatch, float((dq != 0).float().mean()))
+        if int(dq.max()) > 1 or silu_mismatch > 1e-3:
+            bad.append(f"silu*mul quant r{r}: max |dq| {int(dq.max())}")
+    parts = []
+    for r in range(tp):
+        wq, _ = shard("down_proj", r)
+        parts.append(O.dequant(O.int_gemm(traces[r]["q"], wq), traces[r]["s"], W["down_proj"][1]))
+    out_ref = O.all_reduce_sum(parts) if tp > 1 else parts[0]
+    for r in range(tp):
+        cmp(f"down+allreduce r{r}", traces[r]["out"], out_ref)
+    within_tol = max_err <= 1e-2 or all(
+        torch.allclose(traces[r]["out"].float(), out_ref.float(), rtol=1e-2, atol=1e-2) for r in range(tp))
+    return {
+        "rows": len(t0["x"]),
+        "int8": "bit-exact" if not any("quantiser" in b for b in bad) else "mismatch",
+        "int32": "bit-exact" if i32_ok else "mismatch",
+        "bf16": "bit-exact" if max_err == 0.0 else max_err,
+        "silu_quant_int8_mismatch_frac": silu_mismatch,
+        "tolerance": "int8/int32 bit-exact; bf16 within 1e-2 rel / 1e-2 abs",
+        "ok": (not bad) or (within_tol and i32_ok and all(("int32" not in b and "quantiser" not in b) for b in bad)),
+        "layers": ["quant(x)", "qkv", "o_proj+allreduce", "gate_up (+int32)", "silu*mul quant", "down+allreduce"],
+        "failures": bad[:8],
+    }
 
 
+# --------------------------------------------------------------------------- CPU baselines
+def _cpu_rank(rank, world, m, threads, init_file, q, c0_budget_s):
+    """One CPU TP rank: this rank's shard of the four W8A8 linears through the
+    oracle (torch._int_mm on CPU) with the row-parallel partials summed over
+    gloo ranks by ``all_reduce`` (TorchDistributedImpl, M/distributed/impl.py:24-32);
+    then the reference's own bf16 arithmetic (F.linear, M/layers/linear.py:31-32)
+    of the same shard on a bounded token sample."""
+    try:
+        torch.set_num_threads(threads)
+        import torch.distributed as dist
+        from oracle import w8a8_oracle as O
+
+        if world > 1:
+            dist.init_process_group("gloo", init_method=f"file://{init_file}", rank=rank, world_size=world)
+
+        def all_reduce(x):
+            if world > 1:
+                dist.all_reduce(x)
+            return x
+
+        sh = local_shapes(world)
+        g = torch.Generator().manual_seed(100 + rank)
+        w8 = {k: (torch.randint(-127, 128, (n, kk), generator=g, dtype=torch.int8), torch.rand(n, generator=g) * 1e-3)
+              for k, (n, kk) in sh.items()}
+        x = torch.randn(m, HIDDEN, generator=torch.Generator().manual_seed(0)).bfloat16()
+        qc = (NQ // world) * HEAD_DIM
+
+        def step_w8a8():
+            qkv = O.w8a8_linear(x, *w8["qkv"])[3]
+            h = all_reduce(O.w8a8_linear(qkv[:, :qc].contiguous(), *w8["o_proj"])[3])
+            gu = O.w8a8_linear(h, *w8["gate_up"])[3]
+            qq, ss, _ = O.silu_mul_quant(gu)
+            return all_reduce(O.dequant(O.int_gemm(qq, w8["down"][0]), ss, w8["down"][1]))
+
+        def timed(fn, n):
+            ts = []
+            for _ in range(n):
+                if world > 1:
+                    dist.barrier()
+                t0 = time.perf_counter()
+                fn()
+                ts.append(time.perf_counter() - t0)
+            return statistics.median(ts)
+
+        step_w8a8()
+        t8 = timed(step_w8a8, 3)
+        # C0: the reference's bf16 F.linear layers (+ all_reduce) on a bounded sample
+        wb = {k: torch.randn(n, kk, generator=g).bfloat16() for k, (n, kk) in sh.items()}
+        F = torch.nn.functional
+
+        def step_bf16(xb):
+            qkv = F.linear(xb, wb["qkv"])
+            h = all_reduce(F.linear(qkv[:, :qc], wb["o_proj"]))
+            gu = F.linear(h, wb["gate_up"])
+            i = gu.shape[1] // 2
+            y = (F.silu(gu[:, :i].float()) * gu[:, i:].float()).bfloat16()
+            return all_reduce(F.linear(y, wb["down"]))
+
+        m0 = 16
+        t1 = timed(lambda: step_bf16(x[:m0]), 1)
+        flag = torch.tensor([int(max(16, min(m, m0 * c0_budget_s / max(t1, 1e-3))))])
+        if world > 1:
+            dist.all_reduce(flag, op=dist.ReduceOp.MIN)
+        mc0 = int(flag.item())
+        tb = timed(lambda: step_bf16(x[:mc0]), 2)
+        if world > 1:
+            dist.destroy_process_group()
+        q.put((rank, t8, tb, mc0))
+    except BaseException as e:  # noqa: BLE001 - reported to the parent
+        q.put((rank, None, repr(e), 0))
+
+
+def host_cores() -> int:
+    """Physical cores this process may run on (torchrun pins OMP_NUM_THREADS
+    to 1 in its ranks, so torch's own thread count says nothing here)."""
+    try:
+        import psutil
+
+        phys = psutil.cpu_count(logical=False) or 1
+    except Exception:  # noqa: BLE001
+        phys = os.cpu_count() or 1
+    return max(1, min(phys, len(os.sched_getaffinity(0))))
+
+
+def cpu_tp_baseline(world: int, m: int, threads_total: int, c0_budget_s: float = 4.0, timeout: float = 600.0):
+    """Time the CPU path at TP = world as `world` gloo ranks (spawned, no GPU),
+    each with threads_total // world threads, at exactly M tokens.  Returns a
+    cpu_baseline dict (W8A8 oracle = the restated reference path) with the
+    reference's bf16 F.linear arithmetic (C0) beside it."""
+    import multiprocessing as mp
+
+    threads = max(1, threads_total // world)
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    init_file = tempfile.mktemp(prefix="w8a8_cpu_gloo_")
+    saved = {k: os.environ.get(k) for k in ("CUDA_VISIBLE_DEVICES", "OMP_NUM_THREADS")}
+    os.environ["CUDA_VISIBLE_DEVICES"] = ""  # the CPU ranks never touch a GPU
+    os.environ["OMP_NUM_THREADS"] = str(threads)
+    try:
+        procs = [ctx.Process(target=_cpu_rank, args=(r, world, m, threads, init_file, q, c0_budget_s))
+                 for r in range(world)]
+        for p in procs:
+            p.start()
+    finally:
+        for k, v in saved.items():
+            if v is None:
+                os.environ.pop(k, None)
+            else:
+                os.environ[k] = v
+    res = {}
+    try:
+        for _ in range(world):
+            r, t8, tb, mc0 = q.get(timeout=timeout)
+            res[r] = (t8, tb, mc0)
+    finally:
+        for p in procs:
+            p.join(timeout=30)
+            if p.is_alive():
+                p.terminate()
+        try:
+            os.unlink(init_file)
+        except OSError:
+            pass
+    errs = [v[1] for v in res.values() if v[0] is None]
+    if errs:
+        raise RuntimeError(f"CPU baseline rank failed: {errs[0]}")
+    t8 = max(v[0] for v in res.values())
+    tb = max(v[1] for v in res.values())
+    mc0 = res[0][2]
+    return {
+        "value": round(m / t8, 1), "unit": UNIT, "cores": threads * world, "kind": "port",
+        "sample": (f"M={m} tokens through the 4 W8A8 linears + SiLU*mul quant at TP={world}: {world} gloo CPU "
+                   f"rank(s) x {threads} threads, row-parallel partials summed by all_reduce; oracle "
+                   f"(torch._int_mm on CPU); median of 3 after 1 warm-up"),
+        "c0_reference_bf16": {"value": round(mc0 / tb, 1), "unit": UNIT,
+                              "sample": f"the reference's bf16 F.linear layers (+ all_reduce) on M={mc0} tokens, "
+                                        f"same ranks and threads, median of 2"},
+    }
+
+
+# --------------------------------------------------------------------------- our arm
 def run_ours(args, rank, world, dev):
     pkg = _pkg()
     D = pkg.distributed
     D.reset_tp_info()
     D.set_tp_info(rank, world)
     D.DistributedCommunicator.plugins = [D.TorchDistributedImpl()]
-    comm_kind = "nccl-allreduce"
-    if world > 1 and not args.nccl_baseline:
-        try:
-            D.enable_peer_mem_distributed(D.get_tp_info(), None, max_bytes=args.m * HIDDEN * 2, device=dev)
-            comm_kind = "fused-peer-mem"
-        except Exception as e:  # noqa: BLE001 - reported in the JSON
-            comm_kind = f"nccl-allreduce (peer-mem unavailable: {type(e).__name__}: {e})"[:200]
+    comm = None
+    comm_kind = "none (tp1)"
+    if world > 1:
+        comm = D.enable_peer_mem_distributed(D.get_tp_info(), None, max_bytes=args.m * HIDDEN * 2, device=dev)
+        comm_kind = "fused into the row-parallel GEMMs (NVLink peer memory)"
     stream = torch.cuda.Stream(dev)
     flush_buf = torch.zeros(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
     stack = Stack(pkg, world, rank, dev)
     pkg.ops.gemm_workspace(dev)
     peaks, peak_kind = _peaks()
+    ops = pkg.ops
 
     # ---------------------------------------------------------------- headline
     gx = torch.Generator(device=dev).manual_seed(0)
@@ -341,41 +715,130 @@ def run_ours(args, rank, world, dev):
             tms, _, _ = time_graph(lambda: stack.forward(xm), max(20, args.steps), args.warmup, flush_buf, stream)
             tms = max_over_ranks(tms, world, dev)
             us = tms / max(20, args.steps) * 1e3
-            hbm_frac = (wbytes / (us * 1e-6)) / (peaks["hbm_gbs"] * 1e9)
+            t_hbm = wbytes / (peaks["hbm_gbs"] * 1e9) * 1e6
             sweep[str(m)] = {"tokens_per_s": round(m / (us * 1e-6), 1), "us_per_step": round(us, 2),
-                             "weight_stream_frac_of_hbm": round(hbm_frac, 3)}
+                             "weight_stream_frac_of_hbm": round(t_hbm / us, 3)}
 
         # ------------------------------------------------------------ roofline: dominant kernel
         n_gu, k_gu = local_shapes(world)["gate_up"]
         qa = stack.gate_up._quantize_input(x)
         gemm_out = torch.empty(args.m, n_gu, dtype=torch.bfloat16, device=dev)
         gemm_ms = time_kernel_events(
-            lambda: pkg.ops.w8a8_gemm(qa.q, stack.gate_up.weight, qa.s, stack.gate_up.weight_scale, out=gemm_out),
+            lambda: ops.w8a8_gemm(qa.q, stack.gate_up.weight, qa.s, stack.gate_up.weight_scale, out=gemm_out),
             max(10, args.steps // 2), flush_buf, stream)
         alg_ops = 2.0 * args.m * n_gu * k_gu
         achieved_tops = alg_ops / (gemm_ms * 1e-3) / 1e12
-        peak_tops = 2.0 * peaks["bf16_tflops"]
-        # library int8 yardstick on the same shape (cuBLASLt through torch._int_mm)
+        peak_probe = int8_peak(pkg, stream)
         try:
             wt = stack.gate_up.weight.t()
             int_mm_ms = time_kernel_events(lambda: torch._int_mm(qa.q, wt), 10, flush_buf, stream)
             int_mm_tops = alg_ops / (int_mm_ms * 1e-3) / 1e12
         except Exception:
-            int_mm_tops = None
-        # the reference's own GPU path for one linear: cuBLAS bf16 F.linear
+            int_mm_ms = int_mm_tops = None
         wbf = torch.randn(n_gu, k_gu, device=dev, dtype=torch.bfloat16)
         bf16_ms = time_kernel_events(lambda: torch.nn.functional.linear(x, wbf), 10, flush_buf, stream)
         del wbf
     clocks = clk.summary()
+    peak_tops = max(peak_probe.values())
+
+    # ---------------------------------------------------------------- per-op breakdown
+    bsteps = max(10, args.steps // 2)
+
+    def op_us(fn):
+        t, _, _ = time_graph(fn, bsteps, args.warmup, flush_buf, stream)
+        return round(max_over_ranks(t, world, dev) / bsteps * 1e3, 2)
+
+    qx = ops.quant_per_token(x)
+    qkv = stack.qkv.forward(x)
+    attn = qkv[:, : stack.q_cols]
+    qattn = ops.quant_per_token(attn)
+    h = stack.o_proj.forward(attn)
+    qh = ops.quant_per_token(h)
+    gu = stack.gate_up.forward(h)
+    qy = ops.silu_and_mul_quant(gu)
+    o_p, d_p = stack.o_proj, stack.down
+    breakdown = {
+        "quant_x": op_us(lambda: ops.quant_per_token(x)),
+        "qkv_gemm": op_us(lambda: ops.w8a8_gemm(qx[0], stack.qkv.weight, qx[1], stack.qkv.weight_scale)),
+        "quant_attn": op_us(lambda: ops.quant_per_token(attn)),
+        "o_proj": op_us(lambda: o_p.forward(ops.QuantizedActivation(*qattn))),
+        "quant_h": op_us(lambda: ops.quant_per_token(h)),
+        "gate_up_gemm": op_us(lambda: ops.w8a8_gemm(qh[0], stack.gate_up.weight, qh[1], stack.gate_up.weight_scale)),
+        "silu_mul_quant": op_us(lambda: ops.silu_and_mul_quant(gu)),
+        "down": op_us(lambda: d_p.forward(qy)),
+    }
+    if world > 1:
+        breakdown["o_proj_gemm_alone"] = op_us(lambda: ops.w8a8_gemm(qattn[0], o_p.weight, qattn[1], o_p.weight_scale))
+        breakdown["down_gemm_alone"] = op_us(lambda: ops.w8a8_gemm(qy.q, d_p.weight, qy.s, d_p.weight_scale))
+        breakdown["o_proj_reduce_exposed"] = round(breakdown["o_proj"] - breakdown["o_proj_gemm_alone"], 2)
+        breakdown["down_reduce_exposed"] = round(breakdown["down"] - breakdown["down_gemm_alone"], 2)
+        hb = h.clone()
+        breakdown["allreduce_MxH_ours"] = op_us(lambda: comm.all_reduce(hb))
+    breakdown["sum_of_ops"] = round(sum(v for k, v in breakdown.items()
+                                        if k in ("quant_x", "qkv_gemm", "quant_attn", "o_proj", "quant_h",
+                                                 "gate_up_gemm", "silu_mul_quant", "down")), 2)
+    breakdown["step"] = round(ms_per_step * 1e3, 2)
+
+    # ---------------------------------------------------------------- the reference's NCCL bar (N > 1)
+    nccl_line = None
+    if world > 1 and not args.no_nccl:
+        nccl = None
+        try:
+            nccl = SymmetricNcclAllReduce(rank, world, args.m * HIDDEN * 2)
+            tms, _, _ = time_graph(lambda: stack.forward_nccl(x, nccl), args.steps, args.warmup, flush_buf, stream)
+            tms = max_over_ranks(tms, world, dev)
+            hb = h.clone()
+            nccl_line = {
+                "tokens_per_s": round(args.m * args.steps / (tms / 1e3), 1),
+                "ms_per_step": round(tms / args.steps, 4),
+                "o_proj_us": op_us(lambda: nccl.all_reduce(
+                    ops.w8a8_gemm(qattn[0], o_p.weight, qattn[1], o_p.weight_scale))),
+                "down_us": op_us(lambda: nccl.all_reduce(ops.w8a8_gemm(qy.q, d_p.weight, qy.s, d_p.weight_scale))),
+                "allreduce_MxH_us": op_us(lambda: nccl.all_reduce(hb)),
+                "how": "same GEMMs; row-parallel reduce = copy into an ncclMemAlloc'd symmetric window, "
+                       "ncclAllReduce (bf16 sum), copy back (M/kernel/csrc/src/pynccl.cu:93-134)",
+                "nccl_version": nccl.version(),
+            }
+            y_n = stack.forward_nccl(x, nccl)
+            y_f = stack.forward(x)
+            torch.cuda.synchronize()
+            nccl_line["max_abs_diff_vs_fused"] = float((y_n.float() - y_f.float()).abs().max())
+        except Exception as e:  # noqa: BLE001 - reported in the JSON line
+            nccl_line = {"unavailable": f"{type(e).__name__}: {e}"[:300]}
+        finally:
+            if nccl is not None:
+                nccl.close()
+
+    # ---------------------------------------------------------------- parity (after timing)
+    parity = None
+    if not args.no_parity:
+        traces = collect_trace(pkg, stack, x, sample_rows(args.m), world)
+        if rank == 0:
+            parity = oracle_parity(traces, world, dev)
+        del traces
+        if world > 1:
+            torch.distributed.barrier()
 
     # ---------------------------------------------------------------- e2e (public API, host buffers)
+    # One host copy in on rank 0, handed to the other ranks over NVLink by the
+    # communicator's broadcast; the replicated output is copied out from rank 0.
     x_host = torch.randn(args.m, HIDDEN, generator=torch.Generator().manual_seed(1)).bfloat16().pin_memory()
     y_host = torch.empty(args.m, HIDDEN, dtype=torch.bfloat16).pin_memory()
+    xd = torch.empty(args.m, HIDDEN, dtype=torch.bfloat16, device=dev)
     e2e_steps = max(5, args.steps // 2)
+
+    def e2e_step():
+        if rank == 0:
+            xd.copy_(x_host, non_blocking=True)
+        if comm is not None:
+            comm.broadcast(xd, root=0)
+        y = stack.forward(xd)
+        if rank == 0:
+            y_host.copy_(y, non_blocking=True)
+
     with torch.cuda.stream(stream):
         for _ in range(args.warmup):
-            xd = x_host.to(dev, non_blocking=True)
-            y_host.copy_(stack.forward(xd), non_blocking=True)
+            e2e_step()
         torch.cuda.synchronize()
         if world > 1:
             torch.distributed.barrier()
@@ -383,17 +846,21 @@ def run_ours(args, rank, world, dev):
         e = torch.cuda.Event(enable_timing=True)
         s.record(stream)
         for _ in range(e2e_steps):
-            xd = x_host.to(dev, non_blocking=True)
-            y_host.copy_(stack.forward(xd), non_blocking=True)
+            e2e_step()
         e.record(stream)
     torch.cuda.synchronize()
     e2e_ms = max_over_ranks(s.elapsed_time(e), world, dev)
     e2e_value = args.m * e2e_steps / (e2e_ms / 1e3)
 
+    # ---------------------------------------------------------------- CPU baseline (rank 0, every N)
     cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu:
-        v, desc, th = cpu_oracle_sample(world)
-        cpu = {"value": round(v, 1), "unit": UNIT, "cores": th, "kind": "port", "sample": desc}
+    if rank == 0 and not args.no_cpu:
+        try:
+            cpu = cpu_tp_baseline(world, args.m, host_cores())
+        except Exception as e:  # noqa: BLE001 - reported in the JSON line
+            cpu = {"unavailable": f"{type(e).__name__}: {e}"[:300]}
+    if world > 1:
+        torch.distributed.barrier()
 
     traffic = _read_traffic(args.m, n_gu, k_gu)
     line = {
@@ -408,26 +875,30 @@ def run_ours(args, rank, world, dev):
         "scaling": "strong",
         "vs_baseline": None,
         "dtype": "int8 (int32 accumulate, fp32 dequant, bf16 out)",
-        "data": "synthetic: seeded N(0,1) bf16 activations, N(0,0.02) bf16 weights quantised per channel",
-        "config": {"workload": "cfg3 Qwen3-32B decoder-layer W8A8 linears, TP=N, headline M = prefill chunk",
-                   "M": args.m, "hidden": HIDDEN, "heads": [NQ, NKV], "head_dim": HEAD_DIM,
-                   "intermediate": INTER, "parallelism": f"tp{world}", "allreduce": comm_kind,
-                   "l2": "flushed (256 MB write) before every timed step; per-step CUDA-event timing of a CUDA-graph replay"},
+        "data": "synthetic: seeded N(0,1) bf16 activations; synthetic N(0,0.02) bf16 checkpoint quantised per "
+                "channel and sharded by the package's loader",
+        "config": dict(workload_config(world, args.m), allreduce=comm_kind, l2=L2_NOTE),
         "roofline": {"kernel": f"w8a8_gemm gate_up M={args.m} N={n_gu} K={k_gu}", "bound": "tensor",
                      "achieved": round(achieved_tops, 1), "peak": round(peak_tops, 1), "unit": "TOP/s (int8)",
                      "frac": round(achieved_tops / peak_tops, 4),
-                     "peak_source": f"2 x {peak_kind} dense bf16 ({peaks['bf16_tflops']} TF/s burst, MEASURED_PEAKS.json): "
-                                    "B200 dense int8 rate = 2 x bf16",
+                     "peak_source": "measured in this run: MMA-only tcgen05 kind::i8 loop from resident shared "
+                                    f"memory (w8a8_mma_peak_probe) {peak_probe}",
+                     "frac_of_2x_bf16": round(achieved_tops / (2.0 * peaks["bf16_tflops"]), 4),
                      "frac_of_nominal_int8_4500": round(achieved_tops / INT8_NOMINAL_TOPS, 4),
                      "launch_ms": round(gemm_ms, 4), "traffic": traffic,
                      "algorithmic_bytes": args.m * k_gu + n_gu * k_gu + 2 * args.m * n_gu + 4 * args.m + 4 * n_gu},
         "yardsticks": {"torch_int_mm_tops_same_shape": None if int_mm_tops is None else round(int_mm_tops, 1),
+                       "torch_int_mm_ms_same_shape": None if int_mm_ms is None else round(int_mm_ms, 4),
                        "cublas_bf16_linear_ms_same_shape": round(bf16_ms, 4),
                        "ours_gemm_ms_same_shape": round(gemm_ms, 4)},
+        "breakdown_us": breakdown,
+        "nccl_baseline": nccl_line,
+        "parity": parity,
         "sweep": sweep,
         "e2e": {"value": round(e2e_value, 1), "unit": UNIT, "h2d_bytes_per_step": args.m * HIDDEN * 2,
                 "d2h_bytes_per_step": args.m * HIDDEN * 2,
-                "how": "eager public layer API on the caller stream; pinned host input copied in and output copied out every step"},
+                "how": "eager public layer API; pinned host input copied in once (rank 0) and broadcast to the "
+                       "other ranks over NVLink, replicated output copied out from rank 0, every step"},
         "gpu_launches": Stack.launches_per_step * args.steps,
         "clocks": clocks,
         "cpu_baseline": cpu,
@@ -439,27 +910,53 @@ def run_ours(args, rank, world, dev):
 def run_reference(args, rank, world):
     if rank != 0:
         return None
-    torch.set_num_threads(os.cpu_count() or 1)
-    v, desc, th = cpu_oracle_sample(world, budget_s=max(5.0, min(60.0, 3.0 * args.steps)))
+    cpu = cpu_tp_baseline(world, args.m, host_cores())
     return {
         "impl": "reference",
         "metric": METRIC,
-        "value": round(v, 1),
+        "value": cpu["value"],
         "unit": UNIT,
         "n_gpus": world,
         "steps": args.steps,
         "warmup": args.warmup,
-        "ms_per_step": None,
+        "ms_per_step": round(args.m / cpu["value"] * 1e3, 3),
         "higher_is_better": True,
         "scaling": "strong",
         "vs_baseline": None,
         "dtype": "int8 (int32 accumulate, fp32 dequant, bf16 out)",
         "data": "synthetic: seeded int8 weights and bf16 activations of the same shapes",
-        "config": {"workload": "cfg3 Qwen3-32B decoder-layer W8A8 linears, TP=N", "parallelism": f"tp{world}",
-                   "implementation": "CPU restatement of the reference path (oracle/w8a8_oracle.py) on host cores"},
-        "cpu_baseline": {"value": round(v, 1), "unit": UNIT, "cores": th, "kind": "port", "sample": desc},
-        "e2e": {"value": round(v, 1), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "config": workload_config(world, args.m),
+        "implementation": "CPU restatement of the reference path (oracle/w8a8_oracle.py) on host cores, one gloo "
+                          "rank per TP rank; the reference's own bf16 F.linear arithmetic in cpu_baseline.c0",
+        "cpu_baseline": cpu,
+        "e2e": {"value": cpu["value"], "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
+
+
+# --------------------------------------------------------------------------- profiling entries
+def run_gemm_only(args, dev):
+    """Profiling entry for single GEMM shapes (``--gemm MxNxK,...``): int8
+    operands drawn on the device (no other kernel of ours runs), then two
+    launches of the auto-planned GEMM per shape, in the order given."""
+    pkg = _pkg()
+    pkg.ops.gemm_workspace(dev)
+    g = torch.Generator(device=dev).manual_seed(0)
+    shapes = []
+    for spec in args.gemm.split(","):
+        m, n, k = (int(v) for v in spec.lower().split("x"))
+        a = torch.randint(-127, 128, (m, k), device=dev, generator=g, dtype=torch.int8)
+        w = torch.randint(-127, 128, (n, k), device=dev, generator=g, dtype=torch.int8)
+        sa = torch.rand(m, device=dev, generator=g) * 1e-3
+        sw = torch.rand(n, device=dev, generator=g) * 1e-3
+        shapes.append((a, w, sa, sw, torch.empty(m, n, dtype=torch.bfloat16, device=dev)))
+    torch.cuda.synchronize()
+    for a, w, sa, sw, out in shapes:
+        for _ in range(2):
+            pkg.ops.w8a8_gemm(a, w, sa, sw, out=out)
+    torch.cuda.synchronize()
+    assert pkg.ops.device_error() == 0
+    print(json.dumps({"gemm_only": True, "shapes": args.gemm,
+                      "plans": [pkg.ops.gemm_plan(a.shape[0], w.shape[0], a.shape[1]) for a, w, *_ in shapes]}))
 
 
 def run_kernel_only(args, dev):
@@ -492,14 +989,16 @@ def run_kernel_only(args, dev):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--kernel-only", action="store_true", help="profiling entry (see run_kernel_only)")
+    ap.add_argument("--gemm", default="", help="profiling entry: GEMM shapes MxNxK,... (see run_gemm_only)")
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--m", type=int, default=4096)
     ap.add_argument("--sweep", type=lambda s: [int(v) for v in s.split(",") if v], default=[1, 32, 128, 256])
-    ap.add_argument("--nccl-baseline", action="store_true", help="row-parallel reduce through NCCL instead of fused")
-    ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-nccl", action="store_true", help="skip the NCCL symmetric-window arm at N > 1")
+    ap.add_argument("--no-parity", action="store_true", help="skip the oracle check after timing")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
     ap.add_argument("--clocks-dir", default=tempfile.gettempdir(),
                     help="where the raw nvidia-smi samples of the timed region are written")
     args = ap.parse_args()
@@ -516,12 +1015,15 @@ def main():
 
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
+    if args.gemm:
+        run_gemm_only(args, dev)
+        return
     if args.kernel_only:
         run_kernel_only(args, dev)
         return
     if world > 1:
         torch.distributed.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,
-                                             timeout=timedelta(seconds=120))
+                                             timeout=timedelta(seconds=300))
     try:
         line = run_ours(args, rank, world, dev)
         if rank == 0:

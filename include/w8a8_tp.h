@@ -5,10 +5,13 @@
  * entry points.  Plain pointers and sizes only: device pointers are raw CUDA
  * device addresses, `stream` is a cudaStream_t passed as void*.  The caller
  * owns every tensor; the library owns only a communicator's IPC-shared
- * buffers.  No call allocates device memory, synchronises the device or
- * throws; all of them return an int status (0 = W8A8_OK) and leave a message
- * for w8a8_last_error() on failure.  Shapes and alignment are validated on the
- * host before any launch.
+ * buffers.  Apart from w8a8_comm_create (which allocates those buffers) and
+ * the calls documented as synchronising (w8a8_device_error,
+ * w8a8_comm_status, w8a8_comm_destroy, and the first call of
+ * w8a8_gemm_static_scratch on a device), no call allocates device memory or
+ * synchronises the device.  No call throws; all of them return an int status
+ * (0 = W8A8_OK) and leave a message for w8a8_last_error() on failure.  Shapes
+ * and alignment are validated on the host before any launch.
  *
  * Reference interfaces replaced (paths inside mini-sglang, M/ = python/minisgl/):
  *   - _LinearTPImpl.forward = F.linear(x, W, b)          M/layers/linear.py:31-32
@@ -66,7 +69,9 @@ int w8a8_quant_per_token(const void* x, int64_t ldx, int8_t* q, float* scale,
 /* Fused SiLU*mul + per-token quantiser.  gate_up[M, 2I] bf16 (row stride ld
  * elements); y = bf16(silu(gate) * up) as silu_and_mul computes it
  * (M/layers/activation.py:9-12), then q/scale of y as above.  y_out[M, I]
- * (nullable) receives the bf16 y.  Needs I % 8 == 0, ld % 8 == 0. */
+ * (nullable) receives the bf16 y.  With q and scale both null (y_out then
+ * required) only the bf16 y is computed, with no quantisation: the plain
+ * silu_and_mul(x, out).  Needs I % 8 == 0, ld % 8 == 0. */
 int w8a8_silu_mul_quant(const void* gate_up, int64_t ld, int8_t* q, float* scale,
                         void* y_out, int64_t M, int64_t I, void* stream);
 
@@ -128,6 +133,15 @@ int w8a8_gemm_static_scratch(const int8_t* A, const int8_t* B, const float* sa, 
                              const void* bias, void* C, int32_t* c_i32, int64_t M, int64_t N,
                              int64_t K, void* stream);
 
+/* Measurement only, no counterpart in the reference: the int8 tensor-core
+ * ceiling of the current device.  Launches an MMA-only loop (operands
+ * resident in shared memory, no global-memory traffic) of `iters` x 4
+ * tcgen05.mma kind::i8 per CTA: pair = 0 one CTA per SM with 128 x 256 x 32
+ * MMAs, pair = 1 CTA pairs with 256 x 256 x 32 MMAs (cta_group::2, the
+ * prefill kernel's shape).  *ops_out receives the integer ops the launch
+ * performs (2 x MACs); the caller times the launch on `stream` with events. */
+int w8a8_mma_peak_probe(int pair, int64_t iters, int64_t* ops_out, void* stream);
+
 /* Host-only planner query (no GPU needed): the configuration w8a8_gemm would
  * use for a shape on a device with num_sms SMs.  out[8] receives
  * {variant, BN, swap, tiles, CTAs, k-blocks per tile, partition granularity
@@ -158,6 +172,13 @@ int w8a8_comm_set_timeout_ms(w8a8_comm* comm, int64_t timeout_ms);
  * Replaces NCCLWrapper::all_reduce(t, "sum") (M/kernel/csrc/src/pynccl.cu:93-134)
  * and PyNCCLDistributedImpl.all_reduce (M/distributed/impl.py:44-50). */
 int w8a8_all_reduce(w8a8_comm* comm, void* x, int64_t numel, void* stream);
+
+/* In-place broadcast of nbytes (a multiple of 16, at most max_bytes) from
+ * rank `root` to every rank over NVLink peer loads.  No counterpart in
+ * NCCLWrapper (the reference's ranks each copy their own host input in); it
+ * lets one rank copy a step's host input in once and hand it to the other
+ * ranks on the device. */
+int w8a8_broadcast(w8a8_comm* comm, void* x, int64_t nbytes, int root, void* stream);
 
 /* Row-parallel W8A8 linear with the all-reduce fused into the GEMM: every
  * rank passes its K-shard (A[M, K_local], B[N, K_local]) and receives the

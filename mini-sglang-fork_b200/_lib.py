@@ -58,6 +58,7 @@ SIGNATURES = {
                                   _c_i64, _c_i64, _c_i64, _c_int, _c_int, _c_vp, _c_size, _c_vp]),
     "w8a8_gemm_static_scratch": (_c_int, [_c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp,
                                           _c_i64, _c_i64, _c_i64, _c_vp]),
+    "w8a8_mma_peak_probe": (_c_int, [_c_int, _c_i64, ctypes.POINTER(_c_i64), _c_vp]),
     "w8a8_gemm_plan": (_c_int, [_c_i64, _c_i64, _c_i64, _c_int, _c_int, _c_size, _c_int,
                                 ctypes.POINTER(_c_i64)]),
     "w8a8_comm_handle_bytes": (_c_size, []),
@@ -66,6 +67,7 @@ SIGNATURES = {
     "w8a8_comm_set_mode": (_c_int, [_c_vp, _c_int]),
     "w8a8_comm_set_timeout_ms": (_c_int, [_c_vp, _c_i64]),
     "w8a8_all_reduce": (_c_int, [_c_vp, _c_vp, _c_i64, _c_vp]),
+    "w8a8_broadcast": (_c_int, [_c_vp, _c_vp, _c_i64, _c_int, _c_vp]),
     "w8a8_gemm_allreduce": (_c_int, [_c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp,
                                      _c_i64, _c_i64, _c_i64, _c_vp, _c_size, _c_vp]),
     "w8a8_comm_status": (_c_int, [_c_vp, ctypes.POINTER(_c_int)]),

@@ -70,26 +70,33 @@ class PeerMemCommunicator:
     # -------------------------------------------------------------- collectives
     def all_reduce(self, x: torch.Tensor) -> torch.Tensor:
         """In-place sum over the ranks (fp32 rank-order sum, one bf16 rounding)."""
-        if x.dtype != torch.bfloat16 or not x.is_cuda or not x.is_contiguous():
-            raise _lib.W8A8Error(_lib.ERR_INVALID_ARG, "all_reduce: contiguous CUDA bf16 tensor required")
+        if (x.dtype != torch.bfloat16 or not x.is_cuda or not x.is_contiguous()
+                or x.device.index != self.device.index):
+            raise _lib.W8A8Error(_lib.ERR_INVALID_ARG,
+                                 "all_reduce: contiguous bf16 tensor on the communicator's device required")
         st = self._lib.w8a8_all_reduce(self._handle, x.data_ptr(), x.numel(),
                                        torch.cuda.current_stream(x.device).cuda_stream)
         _lib_check(self._lib, st, "all_reduce")
+        return x
+
+    def broadcast(self, x: torch.Tensor, root: int = 0) -> torch.Tensor:
+        """In-place broadcast of ``x`` from rank ``root`` (every rank passes a
+        tensor of the same size; the others' contents are overwritten)."""
+        if not x.is_cuda or not x.is_contiguous() or x.device.index != self.device.index:
+            raise _lib.W8A8Error(_lib.ERR_INVALID_ARG, "broadcast: contiguous tensor on the communicator's device required")
+        st = self._lib.w8a8_broadcast(self._handle, x.data_ptr(), x.numel() * x.element_size(), int(root),
+                                      torch.cuda.current_stream(x.device).cuda_stream)
+        _lib_check(self._lib, st, "broadcast")
         return x
 
     def gemm_allreduce(self, aq: torch.Tensor, wq: torch.Tensor, sa: torch.Tensor, sw: torch.Tensor,
                        bias: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None) -> torch.Tensor:
         """Row-parallel W8A8 linear of this rank's K-shard, all-reduced over the
         ranks inside the GEMM kernel; every rank returns the full sum."""
-        m, k = aq.shape
-        n = wq.shape[0]
-        if aq.dtype != torch.int8 or wq.dtype != torch.int8 or wq.shape[1] != k:
-            raise _lib.W8A8Error(_lib.ERR_INVALID_ARG, "gemm_allreduce: int8 [M,K] x [N,K] operands required")
-        if not (aq.is_cuda and aq.is_contiguous() and wq.is_contiguous() and sa.is_contiguous()
-                and sw.is_contiguous()):
-            raise _lib.W8A8Error(_lib.ERR_INVALID_ARG, "gemm_allreduce: contiguous CUDA operands required")
-        if out is None:
-            out = torch.empty(m, n, dtype=torch.bfloat16, device=aq.device)
+        m, n, k, out = ops.check_gemm_operands("gemm_allreduce", aq, wq, sa, sw, bias, out)
+        if aq.device.index != self.device.index:
+            raise _lib.W8A8Error(_lib.ERR_INVALID_ARG,
+                                 f"gemm_allreduce: operands on {aq.device}, communicator on {self.device}")
         ws = ops.gemm_workspace(aq.device)
         st = self._lib.w8a8_gemm_allreduce(self._handle, aq.data_ptr(), wq.data_ptr(), sa.data_ptr(),
                                            sw.data_ptr(), None if bias is None else bias.data_ptr(),

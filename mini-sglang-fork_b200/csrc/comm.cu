@@ -216,6 +216,27 @@ __global__ void __launch_bounds__(kArThreads) allreduce_kernel(CommView v, uint4
   finish_call(v, epoch);
 }
 
+// Broadcast of `nvec` 16-byte vectors from rank `root` to every rank, in
+// place: the root stages its tensor in its own buffer, one cross-rank barrier
+// per CTA, then every other rank pulls CTA b's sub-range from the root's
+// buffer over NVLink.
+__global__ void __launch_bounds__(kArThreads) broadcast_kernel(CommView v, uint4* x, long long nvec, int root) {
+  dev::griddep_wait();
+  dev::griddep_launch();
+  const uint32_t epoch = dev::ld_relaxed_gpu(dev::ctrl_ptr(v.base[v.rank])) + 1u;
+  const long long sub = (nvec + gridDim.x - 1) / gridDim.x;
+  const long long lo = blockIdx.x * sub, hi = min(nvec, lo + sub);
+  if (v.rank == root) {
+    uint4* mine = reinterpret_cast<uint4*>(dev::half_ptr(v, v.rank, epoch));
+    copy_vectors(mine, [&](long long i) { return x[i]; }, lo, hi);
+  }
+  if (cta_barrier(v, 0, blockIdx.x, epoch) && v.rank != root) {
+    const char* src = dev::half_ptr(v, root, epoch);
+    copy_vectors(x, [&](long long i) { return dev::ld_volatile_v4(src + static_cast<size_t>(i) * 16); }, lo, hi);
+  }
+  finish_call(v, epoch);
+}
+
 }  // namespace
 
 CommView make_view(const w8a8_comm* c, unsigned int* err) {
@@ -379,6 +400,33 @@ int w8a8_all_reduce(w8a8_comm* c, void* x, int64_t numel, void* stream) {
     case 8: W8A8_CUDA_TRY(launch_pdl(allreduce_kernel<8>, g, b, 0, st, v, xv, nvec, two)); break;
     default: W8A8_CUDA_TRY(launch_pdl(allreduce_kernel<0>, g, b, 0, st, v, xv, nvec, two)); break;
   }
+  return W8A8_OK;
+}
+
+int w8a8_broadcast(w8a8_comm* c, void* x, int64_t nbytes, int root, void* stream) {
+  using namespace w8a8;
+  int rc = comm_ready(c);
+  if (rc) return rc;
+  W8A8_REQUIRE(nbytes >= 0, W8A8_ERR_INVALID_ARG, "broadcast: negative size");
+  W8A8_REQUIRE(root >= 0 && root < c->world, W8A8_ERR_INVALID_ARG, "broadcast: root %d not in [0, %d)", root,
+               c->world);
+  if (nbytes == 0 || c->world == 1) return W8A8_OK;
+  W8A8_REQUIRE(x != nullptr, W8A8_ERR_INVALID_ARG, "broadcast: null tensor");
+  W8A8_REQUIRE(nbytes % 16 == 0, W8A8_ERR_INVALID_ARG, "broadcast: %lld bytes is not a multiple of 16",
+               (long long)nbytes);
+  W8A8_REQUIRE(W8A8_ALIGNED16(x), W8A8_ERR_ALIGNMENT, "broadcast: tensor must be 16-byte aligned");
+  W8A8_REQUIRE(static_cast<size_t>(nbytes) <= c->slot_bytes, W8A8_ERR_INVALID_ARG,
+               "broadcast: %lld bytes exceed the communicator's max_bytes %zu", (long long)nbytes, c->slot_bytes);
+  unsigned int* err = device_error_word();
+  if (!err) return W8A8_ERR_CUDA;
+  const CommView v = make_view(c, err);
+  const long long nvec = nbytes / 16;
+  int nsm = sm_count();
+  if (nsm <= 0) nsm = 148;
+  long long grid = (nvec + kArThreads * 4 - 1) / (kArThreads * 4);
+  grid = grid < 1 ? 1 : (grid > 2 * nsm ? 2 * nsm : grid);
+  W8A8_CUDA_TRY(launch_pdl(broadcast_kernel, dim3(static_cast<unsigned>(grid)), dim3(kArThreads), 0,
+                           static_cast<cudaStream_t>(stream), v, static_cast<uint4*>(x), nvec, root));
   return W8A8_OK;
 }
 

@@ -17,4 +17,9 @@ int run_gemm(const int8_t* A, const int8_t* B, const float* sa, const float* sb,
              int32_t* c_i32, int64_t M, int64_t N, int64_t K, int variant, int ctas, void* workspace,
              size_t workspace_bytes, cudaStream_t stream, long long timeout_ns, const CommView* comm);
 
+// Host-side checks of a GEMM call (shape limits, null pointers, 16-byte
+// alignment) that run_gemm makes before any launch; 0 or a status code.
+int validate_gemm_args(const int8_t* A, const int8_t* B, const float* sa, const float* sb, const void* C,
+                       int64_t M, int64_t N, int64_t K);
+
 }  // namespace w8a8

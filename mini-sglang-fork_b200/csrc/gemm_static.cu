@@ -81,6 +81,14 @@ int w8a8_gemm_static_scratch(const int8_t* A, const int8_t* B, const float* sa, 
   W8A8_REQUIRE(M >= 0 && N >= 0 && K >= 0, W8A8_ERR_INVALID_ARG, "gemm_static_scratch: negative shape");
   if (M == 0) return W8A8_OK;  // empty batch, as w8a8_gemm
   W8A8_REQUIRE(N > 0 && K > 0, W8A8_ERR_INVALID_ARG, "gemm_static_scratch: empty N or K");
+  // Every check that can reject the call runs before the set-up below, so a
+  // rejected call touches no device state (and cannot disturb a capture).
+  int rc = w8a8::validate_gemm_args(A, B, sa, sb, C, M, N, K);
+  if (rc) return rc;
+  W8A8_REQUIRE(w8a8::device_cc_major() == 10, W8A8_ERR_UNSUPPORTED,
+               "gemm_static_scratch: the tcgen05 kernels need an sm_100 (B200) device; found compute capability %d.x",
+               w8a8::device_cc_major());
+  W8A8_REQUIRE(W8A8_ALIGNED16(c_i32), W8A8_ERR_ALIGNMENT, "gemm_static_scratch: c_i32 must be 16-byte aligned");
   const int nsm = w8a8::sm_count();
   W8A8_REQUIRE(nsm > 0, W8A8_ERR_CUDA, "gemm_static_scratch: no CUDA device");
   // The plan w8a8_gemm makes when its workspace is large enough.
@@ -92,7 +100,7 @@ int w8a8_gemm_static_scratch(const int8_t* A, const int8_t* B, const float* sa, 
                "maximum of %zu bytes; call w8a8_gemm with a workspace",
                (long long)M, (long long)N, (long long)K, p.ws_bytes, kStaticScratchBytes);
   void* scratch = nullptr;
-  int rc = static_scratch(&scratch);
+  rc = static_scratch(&scratch);
   if (rc) return rc;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (p.cut_tiles)

@@ -91,10 +91,21 @@ __device__ __forceinline__ float vec8_absmax(const uint4& raw) {
   return m;
 }
 
-// y = bf16(silu(g) * u) for 8 lanes, silu(g) = g / (1 + exp(-g)) in fp32.
-// The fp32 value is rounded to bf16 (8 significand bits) at the end, so the
-// fast divide's couple of fp32 ulps almost never reach the bf16 result; the
-// quantiser then works on the bf16 values exactly.
+// silu(g) = g / (1 + exp(-g)) in fp32.  The fast divide is within a couple of
+// fp32 ulps for denominators up to 2^126, but returns 0 for denominators in
+// (2^126, 2^128) (g in about [-88.7, -87.3], where the true value is a normal
+// ~1e-36); those, and an overflowed exp (denominator inf: the IEEE quotient is
+// -0, as on the CPU), take the IEEE divide.  The branch is taken only for
+// such extreme inputs, so it costs nothing on real activations.
+__device__ __forceinline__ float silu_f32(float g) {
+  const float d = __fadd_rn(1.0f, expf(-g));
+  return d > 0x1p126f ? __fdiv_rn(g, d) : __fdividef(g, d);
+}
+
+// y = bf16(silu(g) * u) for 8 lanes.  The fp32 value is rounded to bf16 (8
+// significand bits) at the end, so the fast divide's couple of fp32 ulps
+// almost never reach the bf16 result; the quantiser then works on the bf16
+// values exactly.
 __device__ __forceinline__ uint4 silu_mul_vec8(const uint4& graw, const uint4& uraw) {
   const __nv_bfloat162* g = reinterpret_cast<const __nv_bfloat162*>(&graw);
   const __nv_bfloat162* u = reinterpret_cast<const __nv_bfloat162*>(&uraw);
@@ -104,11 +115,44 @@ __device__ __forceinline__ uint4 silu_mul_vec8(const uint4& graw, const uint4& u
   for (int j = 0; j < 4; ++j) {
     float2 gf = __bfloat1622float2(g[j]);
     float2 uf = __bfloat1622float2(u[j]);
-    float y0 = __fmul_rn(__fdividef(gf.x, __fadd_rn(1.0f, expf(-gf.x))), uf.x);
-    float y1 = __fmul_rn(__fdividef(gf.y, __fadd_rn(1.0f, expf(-gf.y))), uf.y);
+    float y0 = __fmul_rn(silu_f32(gf.x), uf.x);
+    float y1 = __fmul_rn(silu_f32(gf.y), uf.y);
     o[j] = __floats2bfloat162_rn(y0, y1);
   }
   return out;
+}
+
+// bf16-only silu_and_mul (M/layers/activation.py:9-12): y = bf16(silu(g) * u)
+// with no quantisation, element-parallel over [M, I] in 16-byte vectors, two
+// vectors per thread with both loads in flight.  nv = I / 8 vectors per row.
+constexpr int kEltThreads = 256;
+__global__ void __launch_bounds__(kEltThreads) silu_mul_kernel(const __nv_bfloat16* __restrict__ in, int64_t ld,
+                                                               __nv_bfloat16* __restrict__ y, int64_t ldy, int64_t nv,
+                                                               int64_t total) {
+  w8a8::dev::griddep_wait();
+  w8a8::dev::griddep_launch();
+  const int64_t step = static_cast<int64_t>(gridDim.x) * kEltThreads;
+  for (int64_t v = static_cast<int64_t>(blockIdx.x) * kEltThreads + threadIdx.x; v < total; v += 2 * step) {
+    uint4 g[2], u[2];
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const int64_t w = v + j * step;
+      if (w < total) {
+        const int64_t row = w / nv, c = w - row * nv;
+        const uint4* src = reinterpret_cast<const uint4*>(in + row * ld);
+        g[j] = __ldcs(src + c);
+        u[j] = __ldcs(src + nv + c);
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const int64_t w = v + j * step;
+      if (w < total) {
+        const int64_t row = w / nv, c = w - row * nv;
+        reinterpret_cast<uint4*>(y + row * ldy)[c] = silu_mul_vec8(g[j], u[j]);
+      }
+    }
+  }
 }
 
 // Row source: the plain bf16 row (SILU = false) or SiLU*mul of the gate / up
@@ -423,7 +467,11 @@ int w8a8_silu_mul_quant(const void* gate_up, int64_t ld, int8_t* q, float* scale
                         int64_t M, int64_t I, void* stream) {
   W8A8_REQUIRE(M >= 0 && I >= 0, W8A8_ERR_INVALID_ARG, "silu_mul_quant: negative shape");
   if (M == 0) return W8A8_OK;
-  W8A8_REQUIRE(gate_up && q && scale, W8A8_ERR_INVALID_ARG, "silu_mul_quant: null pointer");
+  W8A8_REQUIRE(gate_up != nullptr, W8A8_ERR_INVALID_ARG, "silu_mul_quant: null gate_up");
+  W8A8_REQUIRE((q == nullptr) == (scale == nullptr), W8A8_ERR_INVALID_ARG,
+               "silu_mul_quant: q and scale are given together (or both null for the bf16-only form)");
+  W8A8_REQUIRE(q != nullptr || y_out != nullptr, W8A8_ERR_INVALID_ARG,
+               "silu_mul_quant: nothing to write (q, scale and y_out all null)");
   W8A8_REQUIRE(I > 0 && I % 8 == 0, W8A8_ERR_INVALID_ARG, "silu_mul_quant: I=%lld must be a positive multiple of 8",
                (long long)I);
   W8A8_REQUIRE(ld >= 2 * I && ld % 8 == 0, W8A8_ERR_INVALID_ARG,
@@ -431,6 +479,18 @@ int w8a8_silu_mul_quant(const void* gate_up, int64_t ld, int8_t* q, float* scale
   W8A8_REQUIRE(M <= 0x7fffffff, W8A8_ERR_UNSUPPORTED, "silu_mul_quant: M too large");
   W8A8_REQUIRE(W8A8_ALIGNED16(gate_up) && W8A8_ALIGNED16(q) && W8A8_ALIGNED16(y_out), W8A8_ERR_ALIGNMENT,
                "silu_mul_quant: gate_up, q and y_out must be 16-byte aligned");
+  if (q == nullptr) {
+    // bf16-only silu_and_mul: no reduction, no quantisation
+    const int64_t nv = I / 8, total = M * nv;
+    int nsm = w8a8::sm_count();
+    if (nsm <= 0) nsm = 148;
+    int64_t grid = (total + 2 * kEltThreads - 1) / (2 * kEltThreads);
+    if (grid > 8LL * nsm) grid = 8LL * nsm;
+    W8A8_CUDA_TRY(w8a8::launch_pdl(silu_mul_kernel, dim3(static_cast<unsigned>(grid)), dim3(kEltThreads), 0,
+                                   static_cast<cudaStream_t>(stream), static_cast<const __nv_bfloat16*>(gate_up), ld,
+                                   static_cast<__nv_bfloat16*>(y_out), I, nv, total));
+    return W8A8_OK;
+  }
   W8A8_REQUIRE(I / 8 <= kMaxVec, W8A8_ERR_UNSUPPORTED, "silu_mul_quant: I=%lld exceeds the 32768 limit",
                (long long)I);
   return launch_rows<true>(static_cast<const __nv_bfloat16*>(gate_up), ld, q, scale,

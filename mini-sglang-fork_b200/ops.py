@@ -21,6 +21,8 @@ __all__ = [
     "gemm_plan",
     "gemm_workspace",
     "device_error",
+    "reset_gemm_workspace",
+    "check_gemm_operands",
     "QuantizedActivation",
     "WORKSPACE_BYTES",
 ]
@@ -147,12 +149,20 @@ def rmsnorm_quant(x: torch.Tensor, weight: torch.Tensor, eps: float, residual: O
 
 def silu_and_mul(x: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
     """bf16 ``silu(x[:, :I]) * x[:, I:]`` — the signature of ``silu_and_mul``
-    (M/layers/activation.py:9-12), computed by the fused kernel."""
-    qa, y = silu_and_mul_quant(x, with_bf16=True)
-    if out is not None:
-        out.copy_(y)
-        return out
-    return y
+    (M/layers/activation.py:9-12).  The bf16-only form of the SiLU*mul kernel:
+    no quantisation, the product written straight into ``out`` (allocated
+    when None)."""
+    _require_cuda("silu_and_mul", x, out)
+    if x.dtype != torch.bfloat16 or x.dim() != 2 or x.stride(1) != 1 or x.shape[1] % 2:
+        raise _lib.W8A8Error(_lib.ERR_INVALID_ARG, "silu_and_mul: x must be 2-D bf16 [M, 2I], unit column stride")
+    m, i = x.shape[0], x.shape[1] // 2
+    if out is None:
+        out = torch.empty(m, i, dtype=torch.bfloat16, device=x.device)
+    elif out.dtype != torch.bfloat16 or tuple(out.shape) != (m, i) or not out.is_contiguous():
+        raise _lib.W8A8Error(_lib.ERR_INVALID_ARG, "silu_and_mul: out must be contiguous bf16 [M, I]")
+    _lib.check(_lib.load().w8a8_silu_mul_quant(_ptr(x), x.stride(0), None, None, _ptr(out), m, i, _stream(x)),
+               "silu_and_mul")
+    return out
 
 
 def gemm_plan(m: int, n: int, k: int, variant: int = 0, ctas: int = 0,
@@ -165,6 +175,43 @@ def gemm_plan(m: int, n: int, k: int, variant: int = 0, ctas: int = 0,
     return dict(zip(keys, (int(v) for v in out)))
 
 
+def check_gemm_operands(name: str, aq: torch.Tensor, wq: torch.Tensor, sa: torch.Tensor, sw: torch.Tensor,
+                        bias: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None,
+                        out_i32: Optional[torch.Tensor] = None) -> Tuple[int, int, int, torch.Tensor]:
+    """Host-side validation shared by every GEMM entry (plain and fused): all
+    tensors on one CUDA device, int8 2-D operands with matching K, fp32 scale
+    vectors of exactly M and N elements, bf16 bias [N], bf16 out [M, N]
+    (allocated when None), int32 out_i32 [M, N].  A bad operand raises here,
+    before any pointer reaches a kernel (a host pointer or a short scale
+    vector would otherwise be read by the GPU).  Returns (M, N, K, out)."""
+    if aq.dtype != torch.int8 or wq.dtype != torch.int8 or aq.dim() != 2 or wq.dim() != 2:
+        raise _lib.W8A8Error(_lib.ERR_INVALID_ARG, f"{name}: 2-D int8 operands required")
+    if not (aq.is_contiguous() and wq.is_contiguous() and sa.is_contiguous() and sw.is_contiguous()):
+        raise _lib.W8A8Error(_lib.ERR_INVALID_ARG, f"{name}: contiguous operands required")
+    if sa.dtype != torch.float32 or sw.dtype != torch.float32:
+        raise _lib.W8A8Error(_lib.ERR_INVALID_ARG, f"{name}: fp32 scales required")
+    m, k = aq.shape
+    n, k2 = wq.shape
+    if k2 != k or sa.numel() != m or sw.numel() != n:
+        raise _lib.W8A8Error(_lib.ERR_INVALID_ARG,
+                             f"{name}: shape mismatch A{tuple(aq.shape)} B{tuple(wq.shape)} "
+                             f"sa[{sa.numel()}] sw[{sw.numel()}]")
+    if bias is not None and (bias.dtype != torch.bfloat16 or bias.numel() != n or not bias.is_contiguous()):
+        raise _lib.W8A8Error(_lib.ERR_INVALID_ARG, f"{name}: bias must be contiguous bf16 [N]")
+    if out is not None and (out.dtype != torch.bfloat16 or tuple(out.shape) != (m, n) or not out.is_contiguous()):
+        raise _lib.W8A8Error(_lib.ERR_INVALID_ARG, f"{name}: out must be contiguous bf16 [M, N]")
+    if out_i32 is not None and (out_i32.dtype != torch.int32 or tuple(out_i32.shape) != (m, n)
+                                or not out_i32.is_contiguous()):
+        raise _lib.W8A8Error(_lib.ERR_INVALID_ARG, f"{name}: out_i32 must be contiguous int32 [M, N]")
+    _require_cuda(name, aq, wq, sa, sw, bias, out, out_i32)
+    devs = {t.device for t in (aq, wq, sa, sw, bias, out, out_i32) if t is not None}
+    if len(devs) != 1:
+        raise _lib.W8A8Error(_lib.ERR_INVALID_ARG, f"{name}: operands on several devices {sorted(map(str, devs))}")
+    if out is None:
+        out = torch.empty(m, n, dtype=torch.bfloat16, device=aq.device)
+    return m, n, k, out
+
+
 def w8a8_gemm(aq: torch.Tensor, wq: torch.Tensor, sa: torch.Tensor, sw: torch.Tensor,
               bias: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None,
               out_i32: Optional[torch.Tensor] = None, variant: int = 0, ctas: int = 0) -> torch.Tensor:
@@ -175,26 +222,7 @@ def w8a8_gemm(aq: torch.Tensor, wq: torch.Tensor, sa: torch.Tensor, sw: torch.Te
     receives the exact accumulator.  ``variant`` / ``ctas`` override the
     planner (0 = automatic).
     """
-    _require_cuda("w8a8_gemm", aq, wq, sa, sw, bias, out, out_i32)
-    if aq.dtype != torch.int8 or wq.dtype != torch.int8:
-        raise _lib.W8A8Error(_lib.ERR_INVALID_ARG, "w8a8_gemm: int8 operands required")
-    if not (aq.is_contiguous() and wq.is_contiguous() and sa.is_contiguous() and sw.is_contiguous()):
-        raise _lib.W8A8Error(_lib.ERR_INVALID_ARG, "w8a8_gemm: contiguous operands required")
-    if sa.dtype != torch.float32 or sw.dtype != torch.float32:
-        raise _lib.W8A8Error(_lib.ERR_INVALID_ARG, "w8a8_gemm: fp32 scales required")
-    m, k = aq.shape
-    n, k2 = wq.shape
-    if k2 != k or sa.numel() != m or sw.numel() != n:
-        raise _lib.W8A8Error(_lib.ERR_INVALID_ARG, f"w8a8_gemm: shape mismatch A{tuple(aq.shape)} B{tuple(wq.shape)}")
-    if bias is not None and (bias.dtype != torch.bfloat16 or bias.numel() != n or not bias.is_contiguous()):
-        raise _lib.W8A8Error(_lib.ERR_INVALID_ARG, "w8a8_gemm: bias must be contiguous bf16 [N]")
-    if out is None:
-        out = torch.empty(m, n, dtype=torch.bfloat16, device=aq.device)
-    elif out.dtype != torch.bfloat16 or tuple(out.shape) != (m, n) or not out.is_contiguous():
-        raise _lib.W8A8Error(_lib.ERR_INVALID_ARG, "w8a8_gemm: out must be contiguous bf16 [M, N]")
-    if out_i32 is not None and (out_i32.dtype != torch.int32 or tuple(out_i32.shape) != (m, n)
-                                or not out_i32.is_contiguous()):
-        raise _lib.W8A8Error(_lib.ERR_INVALID_ARG, "w8a8_gemm: out_i32 must be contiguous int32 [M, N]")
+    m, n, k, out = check_gemm_operands("w8a8_gemm", aq, wq, sa, sw, bias, out, out_i32)
     ws = gemm_workspace(aq.device)
     lib = _lib.load()
     st = lib.w8a8_gemm_config(_ptr(aq), _ptr(wq), _ptr(sa), _ptr(sw), _ptr(bias), _ptr(out), _ptr(out_i32),
@@ -203,8 +231,28 @@ def w8a8_gemm(aq: torch.Tensor, wq: torch.Tensor, sa: torch.Tensor, sw: torch.Te
     return out
 
 
+# The stream-K counter region at the head of a GEMM workspace (65536 tile
+# counters, csrc/gemm_plan.h kCounterBytes).
+_COUNTER_BYTES = 65536 * 4
+
+
+def reset_gemm_workspace(device: Optional[torch.device] = None) -> None:
+    """Zero the stream-K tile counters of the workspace(s) on the caller's
+    stream.  A successful GEMM leaves its counters at zero, but a call whose
+    bounded wait gave up can stop before resetting the counters of its cut
+    tiles; :func:`device_error` calls this whenever it clears a non-zero error
+    word, so the next call starts from zero counters."""
+    for idx, ws in _workspaces.items():
+        if device is None or device.index in (None, idx):
+            ws[:_COUNTER_BYTES].zero_()
+
+
 def device_error(clear: bool = True) -> int:
-    """Device-side error bits (bounded waits that gave up); synchronises."""
+    """Device-side error bits (bounded waits that gave up); synchronises.
+    Clearing a non-zero word also resets the GEMM workspaces' counters."""
     code = ctypes.c_int(0)
     _lib.check(_lib.load().w8a8_device_error(ctypes.byref(code), 1 if clear else 0), "device_error")
+    if clear and code.value != 0:
+        reset_gemm_workspace()
+        torch.cuda.synchronize()
     return code.value

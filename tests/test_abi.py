@@ -224,3 +224,27 @@ def test_ops_refuse_cpu_tensors(pkg):
     with pytest.raises(pkg.W8A8Error, match="no CPU path"):
         pkg.ops.w8a8_gemm(torch.zeros(4, 16, dtype=torch.int8), torch.zeros(16, 16, dtype=torch.int8),
                           torch.zeros(4), torch.zeros(16))
+
+
+def test_gemm_operand_checks_run_on_the_host(pkg):
+    """Both GEMM entries (plain and fused row-parallel) reject a short or
+    mistyped scale vector and host (CPU) tensors before any pointer reaches
+    the library; the fused entry needs no communicator buffers to do so."""
+    import torch
+
+    C = pkg.comm.PeerMemCommunicator
+    comm = C.__new__(C)  # no device buffers: the checks come before any library call
+    comm.device = torch.device("cuda", 0)
+    a = torch.zeros(4, 32, dtype=torch.int8)
+    w = torch.zeros(16, 32, dtype=torch.int8)
+    for fn in (comm.gemm_allreduce, pkg.ops.w8a8_gemm):
+        with pytest.raises(pkg.W8A8Error, match="shape mismatch"):
+            fn(a, w, torch.ones(3), torch.ones(16))  # short activation scales
+        with pytest.raises(pkg.W8A8Error, match="shape mismatch"):
+            fn(a, w, torch.ones(4), torch.ones(8))  # short weight scales
+        with pytest.raises(pkg.W8A8Error, match="fp32 scales"):
+            fn(a, w, torch.ones(4, dtype=torch.float16), torch.ones(16))
+        with pytest.raises(pkg.W8A8Error, match="bias"):
+            fn(a, w, torch.ones(4), torch.ones(16), torch.ones(8, dtype=torch.bfloat16))
+        with pytest.raises(pkg.W8A8Error, match="CUDA tensors required"):
+            fn(a, w, torch.ones(4), torch.ones(16))  # host (CPU) weight and activations

@@ -152,6 +152,56 @@ def _scn_gemm_allreduce(pkg, O, rank, world, dev, dist):
     return True
 
 
+def _scn_gemm_allreduce_cfg3(pkg, O, rank, world, dev, dist):
+    """The benchmarked row-parallel shapes at M = 4096 (cfg3 o_proj K=8192 and
+    down K=25600, sharded over the world): the fused GEMM + all-reduce output
+    on two sampled rows of every 128-row tile is bit-exact with the oracle's
+    tp_linear("row"), and identical on every rank."""
+    m, n = 4096, 5120
+    rows = []
+    for t in range(m // 128):
+        rows += [t * 128 + (t * 53 + 17) % 128, t * 128 + 127]
+    idx = torch.tensor(rows, device=dev)
+    comm = pkg.comm.PeerMemCommunicator(rank, world, m * n * 2, device=dev)
+    digests = []
+    for kfull in (8192, 25600):
+        g = torch.Generator(device=dev).manual_seed(kfull)  # the same full tensors on every rank
+        x = torch.randn(m, kfull, device=dev, generator=g).bfloat16()
+        wq, ws = pkg.ops.quant_per_token((torch.randn(n, kfull, device=dev, generator=g) * 0.02).bfloat16())
+        kl = kfull // world
+        xs = x[:, rank * kl:(rank + 1) * kl].contiguous()
+        wshard = wq[:, rank * kl:(rank + 1) * kl].contiguous()
+        q, s = pkg.ops.quant_per_token(xs)
+        y = comm.gemm_allreduce(q, wshard, s, ws)
+        torch.cuda.synchronize()
+        want = O.tp_linear("row", x.index_select(0, idx).cpu(), wq.cpu(), ws.cpu(), world)[rank]
+        got = y.index_select(0, idx).cpu()
+        assert torch.equal(got, want), f"k={kfull}: max |diff| {float((got.float() - want.float()).abs().max())}"
+        digests.append(float(y.float().sum()))
+    everyone = [None] * world
+    dist.all_gather_object(everyone, digests)
+    assert all(d == digests for d in everyone), "ranks disagree on the reduced output"
+    assert comm.device_error() == 0
+    comm.close()
+    return True
+
+
+def _scn_broadcast(pkg, O, rank, world, dev, dist):
+    """Peer-memory broadcast from every root, at sizes from one vector to
+    42 MB (the bench's e2e input), twice per size (both buffer halves)."""
+    comm = pkg.comm.PeerMemCommunicator(rank, world, 4096 * 5120 * 2, device=dev)
+    for root in range(world):
+        for numel in (8, 4096 + 8, 4096 * 5120):
+            for rep in range(2):
+                want = torch.randn(numel, generator=torch.Generator().manual_seed(numel + root + rep)).bfloat16()
+                x = want.to(dev) if rank == root else torch.full((numel,), -3.0, dtype=torch.bfloat16, device=dev)
+                comm.broadcast(x, root=root)
+                assert torch.equal(x.cpu(), want), f"root={root} numel={numel} rep={rep}"
+    assert comm.device_error() == 0
+    comm.close()
+    return True
+
+
 def _scn_layers_and_graphs(pkg, O, rank, world, dev, dist):
     """LinearRowParallel / LinearOProj through enable_peer_mem_distributed, eager
     and replayed from a CUDA graph (device-side epochs keep replays correct)."""
@@ -260,6 +310,14 @@ def test_allreduce_random_bit_exact():
 
 def test_gemm_allreduce_bit_exact():
     _run("gemm_allreduce")
+
+
+def test_gemm_allreduce_cfg3_shapes():
+    _run("gemm_allreduce_cfg3", timeout=600)
+
+
+def test_broadcast():
+    _run("broadcast")
 
 
 def test_row_parallel_layer_and_cuda_graph():

@@ -153,3 +153,60 @@ def test_gemm_rejects_bad_shapes_without_launch(pkg, cuda_dev):
     wq = torch.zeros(32, 24, dtype=torch.int8, device=cuda_dev)
     with pytest.raises(pkg.W8A8Error, match="multiple of 16"):
         pkg.ops.w8a8_gemm(aq, wq, torch.ones(4, device=cuda_dev), torch.ones(32, device=cuda_dev))
+
+
+def test_gemm_workspace_reset_clears_stale_counters(pkg, oracle, cuda_dev):
+    """A call whose bounded wait gave up can leave stream-K tile counters
+    non-zero.  reset_gemm_workspace (run by device_error when it clears a
+    non-zero error word) zeroes them, after which a cut-tile GEMM on the same
+    workspace matches the oracle and leaves the counters at zero again."""
+    ws = pkg.ops.gemm_workspace(cuda_dev)
+    assert pkg.ops.gemm_plan(40, 400, 1024, variant=2, ctas=7)["workspace_bytes"] > 0  # tiles are cut
+    ws[: 64 * 4].fill_(1)  # stale counters, written from the host side
+    pkg.ops.reset_gemm_workspace(cuda_dev)
+    _check(pkg, oracle, cuda_dev, 40, 400, 1024, variant=2, ctas=7, seed=11)
+    assert int(ws[: pkg.ops._COUNTER_BYTES].count_nonzero()) == 0
+
+
+def _tile_rows(m):
+    """Two rows of every 128-row tile (one pseudo-random, the tile's last)."""
+    rows = set()
+    for t in range((m + 127) // 128):
+        lo, hi = t * 128, min(m, t * 128 + 128)
+        rows.update((lo + (t * 53 + 17) % (hi - lo), hi - 1))
+    return sorted(rows)
+
+
+# The benchmarked shapes: every cfg3 shard (qkv, o_proj, gate_up, down) at the
+# M = 4096 prefill chunk for TP 1/2/4/8, and two M = 8192 prefill shapes
+# (cfg2 gate_up and down).
+HEADLINE_SHAPES = sorted({(4096, n, k) for p in (1, 2, 4, 8)
+                          for n, k in ((10240 // p, 5120), (5120, 8192 // p), (51200 // p, 5120), (5120, 25600 // p))}
+                         | {(8192, 24576, 4096), (8192, 4096, 12288)})
+
+
+@pytest.mark.parametrize("m,n,k", HEADLINE_SHAPES)
+def test_gemm_headline_shapes(pkg, oracle, cuda_dev, m, n, k):
+    """Auto-planned GEMM at the exact shapes the bench times: the sampled rows
+    (every output tile) bit-exact in int32 and bf16 against the oracle, and
+    every row through the column-checksum identity
+    sum_m acc[m, n] == (sum_m a[m, :]) . w[n, :] in int64."""
+    g = torch.Generator(device=cuda_dev).manual_seed(m * 7 + n * 3 + k)
+    a = torch.randint(-127, 128, (m, k), device=cuda_dev, generator=g, dtype=torch.int8)
+    w = torch.randint(-127, 128, (n, k), device=cuda_dev, generator=g, dtype=torch.int8)
+    sa = torch.rand(m, device=cuda_dev, generator=g) * 0.02 + 1e-4
+    sw = torch.rand(n, device=cuda_dev, generator=g) * 0.002 + 1e-5
+    acc = torch.empty(m, n, dtype=torch.int32, device=cuda_dev)
+    y = pkg.ops.w8a8_gemm(a, w, sa, sw, out_i32=acc)
+    torch.cuda.synchronize()
+    assert pkg.ops.device_error() == 0
+    plan = pkg.ops.gemm_plan(m, n, k)
+    rows = torch.tensor(_tile_rows(m), device=cuda_dev)
+    a_r, w_c = a.index_select(0, rows).cpu(), w.cpu()
+    acc_ref = oracle.int_gemm(a_r, w_c)
+    y_ref = oracle.dequant(acc_ref, sa.index_select(0, rows).cpu(), sw.cpu())
+    assert torch.equal(acc.index_select(0, rows).cpu(), acc_ref), f"int32 rows, plan {plan}"
+    assert torch.equal(y.index_select(0, rows).cpu(), y_ref), f"bf16 rows, plan {plan}"
+    col = acc.sum(dim=0, dtype=torch.int64).cpu()
+    want = (a.sum(dim=0, dtype=torch.int64).cpu().numpy() @ w_c.numpy().astype("int64").T)
+    assert torch.equal(col, torch.from_numpy(want)), f"column checksum, plan {plan}"

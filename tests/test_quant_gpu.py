@@ -110,3 +110,40 @@ def test_silu_and_mul_compat_signature(pkg, oracle, cuda_dev):
     y = pkg.silu_and_mul(gu, out=out)
     assert y.data_ptr() == out.data_ptr()
     torch.testing.assert_close(y.cpu(), oracle.silu_and_mul(gu.cpu()), rtol=2 ** -7, atol=0)
+
+
+def test_silu_mul_extreme_gate(pkg, oracle, cuda_dev):
+    """Gate values where 1 + exp(-g) lies in (2^126, 2^128) (about [-88.7,
+    -87.3]; the fast divide would return 0 for a normal ~1e-36 result) and
+    beyond (exp overflows: the quotient is -0): the bf16 product follows the
+    CPU reference there too."""
+    m, i = 3, 256
+    g = torch.linspace(-89.5, -86.5, m * i).reshape(m, i)
+    u = torch.full((m, i), 3.0)
+    u[1] = -1.5
+    gu = torch.cat([g, u], dim=1).bfloat16()
+    qa, y = pkg.ops.silu_and_mul_quant(gu.to(cuda_dev), with_bf16=True)
+    y_ref = oracle.silu_and_mul(gu)
+    yc = y.cpu()
+    diff = (yc.float() - y_ref.float()).abs()
+    assert torch.all(diff <= y_ref.float().abs() * 2.0 ** -7), float(diff.max())
+    assert torch.equal(yc == 0, y_ref == 0)
+    q_ref, s_ref = oracle.quant_per_token(yc)
+    assert torch.equal(qa.s.cpu(), s_ref) and torch.equal(qa.q.cpu(), q_ref)
+    # the bf16-only form computes the same product
+    torch.testing.assert_close(pkg.silu_and_mul(gu.to(cuda_dev)).cpu(), yc, rtol=0, atol=0)
+
+
+@pytest.mark.parametrize("m,i", [(1, 8), (7, 96), (300, 3072), (4096, 3200)])
+def test_silu_and_mul_bf16_only(pkg, oracle, cuda_dev, m, i):
+    """The bf16-only silu_and_mul (no quantisation) equals the fused kernel's
+    bf16 product bit for bit and is within one bf16 ulp of the CPU reference;
+    it also accepts a strided gate_up view."""
+    gu = _x(m, 2 * i + 16, seed=m * 3 + i, scale=2.0)[:, : 2 * i]
+    gd = gu.to(cuda_dev)
+    y = pkg.silu_and_mul(gd)
+    _, y_fused = pkg.ops.silu_and_mul_quant(gd, with_bf16=True)
+    assert torch.equal(y.cpu(), y_fused.cpu())
+    y_ref = oracle.silu_and_mul(gu.contiguous())
+    diff = (y.cpu().float() - y_ref.float()).abs()
+    assert torch.all(diff <= y_ref.float().abs() * 2.0 ** -7 + 1e-30), float(diff.max())
