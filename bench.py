@@ -243,7 +243,8 @@ class Stack:
 
 # --------------------------------------------------------------------------- the reference's NCCL path
 class NcclUniqueId(ctypes.Structure):
-    _fields_ = [("internal", ctypes.c_char * 128)]
+    # unsigned bytes: a c_char array would convert to bytes only up to its first zero byte
+    _fields_ = [("internal", ctypes.c_ubyte * 128)]
 
 
 class SymmetricNcclAllReduce:
@@ -279,7 +280,9 @@ class SymmetricNcclAllReduce:
             self._check(self.nccl.ncclGetUniqueId(ctypes.byref(uid)), "ncclGetUniqueId")
         obj = [bytes(uid.internal) if rank == 0 else None]
         torch.distributed.broadcast_object_list(obj, src=0)
-        ctypes.memmove(uid.internal, obj[0], 128)
+        if len(obj[0]) != 128:
+            raise RuntimeError("malformed NCCL unique id")
+        ctypes.memmove(ctypes.addressof(uid), obj[0], 128)
         self.comm, self.buf, self.win = vp(), vp(), vp()
         self._check(self.nccl.ncclCommInitRank(ctypes.byref(self.comm), world, uid, rank), "ncclCommInitRank")
         self._check(self.nccl.ncclMemAlloc(ctypes.byref(self.buf), self.max_bytes), "ncclMemAlloc")
@@ -352,22 +355,12 @@ def time_graph(fn, steps, warmup, flush_buf, stream):
 
 
 def time_kernel_events(fn, reps, flush_buf, stream):
-    """Average device time of one launch of fn (CUDA events on `stream`)."""
-    with torch.cuda.stream(stream):
-        for _ in range(3):
-            fn()
-        torch.cuda.synchronize()
-        ts = []
-        for _ in range(reps):
-            _flush(flush_buf)
-            s = torch.cuda.Event(enable_timing=True)
-            e = torch.cuda.Event(enable_timing=True)
-            s.record(stream)
-            fn()
-            e.record(stream)
-            ts.append((s, e))
-    torch.cuda.synchronize()
-    return sum(s.elapsed_time(e) for s, e in ts) / reps
+    """Average device time (ms) of one call of fn: fn is captured in a CUDA
+    graph and each replay is bracketed by CUDA events on `stream`, so host-side
+    argument checks and launch latency stay outside the measurement; L2 is
+    flushed before each replay."""
+    total, _, _ = time_graph(fn, reps, 3, flush_buf, stream)
+    return total / reps
 
 
 def max_over_ranks(v: float, world: int, dev) -> float:
@@ -784,7 +777,15 @@ def run_ours(args, rank, world, dev):
     if world > 1 and not args.no_nccl:
         nccl = None
         try:
-            nccl = SymmetricNcclAllReduce(rank, world, args.m * HIDDEN * 2)
+            err = None
+            try:
+                nccl = SymmetricNcclAllReduce(rank, world, args.m * HIDDEN * 2)
+            except Exception as e:  # noqa: BLE001 - every rank learns of it below
+                err = e
+            ok = torch.tensor([0 if err else 1], device=dev)
+            torch.distributed.all_reduce(ok, op=torch.distributed.ReduceOp.MIN)
+            if not int(ok.item()):
+                raise err or RuntimeError("NCCL symmetric-window set-up failed on another rank")
             tms, _, _ = time_graph(lambda: stack.forward_nccl(x, nccl), args.steps, args.warmup, flush_buf, stream)
             tms = max_over_ranks(tms, world, dev)
             hb = h.clone()
@@ -820,37 +821,65 @@ def run_ours(args, rank, world, dev):
             torch.distributed.barrier()
 
     # ---------------------------------------------------------------- e2e (public API, host buffers)
-    # One host copy in on rank 0, handed to the other ranks over NVLink by the
-    # communicator's broadcast; the replicated output is copied out from rank 0.
+    # Every step copies its input in from pinned host memory (once, on rank 0,
+    # handed to the other ranks over NVLink by the communicator's broadcast)
+    # and reads the replicated output back to the host (from rank 0).  Two
+    # buffers per direction and two copy streams pipeline the steps, as a
+    # serving loop does: step i+1's input crosses PCIe and step i-1's output
+    # returns while step i computes.
     x_host = torch.randn(args.m, HIDDEN, generator=torch.Generator().manual_seed(1)).bfloat16().pin_memory()
-    y_host = torch.empty(args.m, HIDDEN, dtype=torch.bfloat16).pin_memory()
-    xd = torch.empty(args.m, HIDDEN, dtype=torch.bfloat16, device=dev)
-    e2e_steps = max(5, args.steps // 2)
+    y_host = [torch.empty(args.m, HIDDEN, dtype=torch.bfloat16).pin_memory() for _ in range(2)]
+    xd = [torch.empty(args.m, HIDDEN, dtype=torch.bfloat16, device=dev) for _ in range(2)]
+    s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    ev_in = [torch.cuda.Event() for _ in range(2)]
+    ev_used = [torch.cuda.Event() for _ in range(2)]
+    ev_y = [torch.cuda.Event() for _ in range(2)]
+    ev_out = [torch.cuda.Event() for _ in range(2)]
+    e2e_steps = max(8, args.steps // 2)
 
-    def e2e_step():
-        if rank == 0:
-            xd.copy_(x_host, non_blocking=True)
-        if comm is not None:
-            comm.broadcast(xd, root=0)
-        y = stack.forward(xd)
-        if rank == 0:
-            y_host.copy_(y, non_blocking=True)
+    def e2e_run(n):
+        for i in range(n):
+            b = i % 2
+            if rank == 0:
+                with torch.cuda.stream(s_in):
+                    s_in.wait_event(ev_used[b])  # step i-2 is done reading this buffer
+                    xd[b].copy_(x_host, non_blocking=True)
+                    ev_in[b].record(s_in)
+                stream.wait_event(ev_in[b])
+            with torch.cuda.stream(stream):
+                stream.wait_event(ev_out[b])  # step i-2's output is back on the host
+                if comm is not None:
+                    comm.broadcast(xd[b], root=0)
+                y = stack.forward(xd[b])
+                ev_used[b].record(stream)
+                ev_y[b].record(stream)
+            if rank == 0:
+                with torch.cuda.stream(s_out):
+                    s_out.wait_event(ev_y[b])
+                    y_host[b].copy_(y, non_blocking=True)
+                    y.record_stream(s_out)
+                    ev_out[b].record(s_out)
+            else:
+                ev_out[b].record(stream)
 
-    with torch.cuda.stream(stream):
-        for _ in range(args.warmup):
-            e2e_step()
-        torch.cuda.synchronize()
-        if world > 1:
-            torch.distributed.barrier()
-        s = torch.cuda.Event(enable_timing=True)
-        e = torch.cuda.Event(enable_timing=True)
-        s.record(stream)
-        for _ in range(e2e_steps):
-            e2e_step()
-        e.record(stream)
+    e2e_run(args.warmup)
+    torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    s = torch.cuda.Event(enable_timing=True)
+    e = torch.cuda.Event(enable_timing=True)
+    s.record(s_in if rank == 0 else stream)
+    e2e_run(e2e_steps)
+    for st in (s_in, s_out):
+        stream.wait_stream(st)
+    e.record(stream)
     torch.cuda.synchronize()
     e2e_ms = max_over_ranks(s.elapsed_time(e), world, dev)
     e2e_value = args.m * e2e_steps / (e2e_ms / 1e3)
+    # the pipelined outputs are the stack's output for x_host
+    y_ref = stack.forward(x_host.to(dev))
+    torch.cuda.synchronize()
+    e2e_ok = bool(torch.equal(y_host[(e2e_steps - 1) % 2], y_ref.cpu())) if rank == 0 else True
 
     # ---------------------------------------------------------------- CPU baseline (rank 0, every N)
     cpu = None
@@ -897,8 +926,10 @@ def run_ours(args, rank, world, dev):
         "sweep": sweep,
         "e2e": {"value": round(e2e_value, 1), "unit": UNIT, "h2d_bytes_per_step": args.m * HIDDEN * 2,
                 "d2h_bytes_per_step": args.m * HIDDEN * 2,
-                "how": "eager public layer API; pinned host input copied in once (rank 0) and broadcast to the "
-                       "other ranks over NVLink, replicated output copied out from rank 0, every step"},
+                "output_matches": e2e_ok,
+                "how": "eager public layer API; every step: pinned host input copied in once (rank 0) and "
+                       "broadcast to the other ranks over NVLink, replicated output copied back from rank 0; "
+                       "double-buffered copy streams overlap step i+1's input and step i-1's output with step i"},
         "gpu_launches": Stack.launches_per_step * args.steps,
         "clocks": clocks,
         "cpu_baseline": cpu,
@@ -999,6 +1030,7 @@ def main():
     ap.add_argument("--no-nccl", action="store_true", help="skip the NCCL symmetric-window arm at N > 1")
     ap.add_argument("--no-parity", action="store_true", help="skip the oracle check after timing")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
+    ap.add_argument("--pg-timeout", type=int, default=300, help="process-group timeout in seconds (N > 1)")
     ap.add_argument("--clocks-dir", default=tempfile.gettempdir(),
                     help="where the raw nvidia-smi samples of the timed region are written")
     args = ap.parse_args()
@@ -1023,7 +1055,7 @@ def main():
         return
     if world > 1:
         torch.distributed.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,
-                                             timeout=timedelta(seconds=300))
+                                             timeout=timedelta(seconds=args.pg_timeout))
     try:
         line = run_ours(args, rank, world, dev)
         if rank == 0:

@@ -54,6 +54,7 @@ template <int BN, int STAGES, bool SWAP, bool FUSED>
 int launch_variant(const GemmPlan& p, const CUtensorMap& tw, const CUtensorMap& tn, const GemmArgs& args,
                    const CommView& cv, cudaStream_t stream) {
   using T = GemmTraits<BN, STAGES, SWAP>;
+  constexpr int kSmem = T::smem_bytes(FUSED);
   auto kern = w8a8_gemm_kernel<BN, STAGES, SWAP, FUSED>;
   static std::mutex mu;
   static bool configured[64] = {false};
@@ -62,11 +63,11 @@ int launch_variant(const GemmPlan& p, const CUtensorMap& tw, const CUtensorMap& 
   {
     std::lock_guard<std::mutex> lk(mu);
     if (!configured[dev]) {
-      W8A8_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, T::kSmemBytes));
+      W8A8_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem));
       configured[dev] = true;
     }
   }
-  W8A8_CUDA_TRY(launch_pdl(kern, dim3(p.grid), dim3(gemm_block_threads<FUSED>()), T::kSmemBytes, stream, tw, tn,
+  W8A8_CUDA_TRY(launch_pdl(kern, dim3(p.grid), dim3(gemm_block_threads<FUSED>()), kSmem, stream, tw, tn,
                            args, cv));
   return W8A8_OK;
 }
@@ -92,6 +93,8 @@ template <int STAGES, bool FUSED>
 int launch_pair_variant(const GemmPlan& p, const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& args,
                         const CommView& cv, cudaStream_t stream) {
   using T = Gemm2Traits<STAGES>;
+  constexpr int kSmem = T::smem_bytes(FUSED);
+  static_assert(kSmem <= 227 * 1024, "shared memory");
   auto kern = w8a8_gemm2_kernel<STAGES, FUSED>;
   static std::mutex mu;
   static bool configured[64] = {false};
@@ -100,11 +103,11 @@ int launch_pair_variant(const GemmPlan& p, const CUtensorMap& ta, const CUtensor
   {
     std::lock_guard<std::mutex> lk(mu);
     if (!configured[dev]) {
-      W8A8_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, T::kSmemBytes));
+      W8A8_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem));
       configured[dev] = true;
     }
   }
-  W8A8_CUDA_TRY(launch_pdl(kern, dim3(p.grid), dim3(gemm_block_threads<FUSED>()), T::kSmemBytes, stream, ta, tb,
+  W8A8_CUDA_TRY(launch_pdl(kern, dim3(p.grid), dim3(gemm_block_threads<FUSED>()), kSmem, stream, ta, tb,
                            args, cv));
   return W8A8_OK;
 }
@@ -119,7 +122,8 @@ int dispatch_variant(const GemmPlan& p, const CUtensorMap& tw, const CUtensorMap
     case 4: return launch_variant<32, 9, true, FUSED>(p, tw, tn, args, cv, stream);
     case 5: return launch_variant<64, 8, true, FUSED>(p, tw, tn, args, cv, stream);
     case 6: return launch_variant<128, 6, true, FUSED>(p, tw, tn, args, cv, stream);
-    case 7: return launch_pair_variant<6, FUSED>(p, tw, tn, args, cv, stream);
+    // the plain pair kernel spends the fused-only staging bytes on a 7th stage
+    case 7: return launch_pair_variant<FUSED ? 6 : 7, FUSED>(p, tw, tn, args, cv, stream);
     default: return fail(W8A8_ERR_INVALID_ARG, "gemm: unknown variant %d", p.variant);
   }
 }
@@ -252,7 +256,8 @@ int w8a8_gemm(const int8_t* A, const int8_t* B, const float* sa, const float* sb
 int w8a8_gemm_config(const int8_t* A, const int8_t* B, const float* sa, const float* sb, const void* bias,
                      void* C, int32_t* c_i32, int64_t M, int64_t N, int64_t K, int variant, int ctas,
                      void* workspace, size_t workspace_bytes, void* stream) {
-  W8A8_REQUIRE(variant >= 0 && variant <= 7, W8A8_ERR_INVALID_ARG, "gemm_config: variant %d out of range",
+  W8A8_REQUIRE(variant >= 0 && variant <= w8a8::kMaxVariant, W8A8_ERR_INVALID_ARG,
+               "gemm_config: variant %d out of range",
                variant);
   W8A8_REQUIRE(ctas >= 0, W8A8_ERR_INVALID_ARG, "gemm_config: negative ctas");
   return w8a8::run_gemm(A, B, sa, sb, bias, C, c_i32, M, N, K, variant, ctas, workspace, workspace_bytes,

@@ -42,9 +42,13 @@ struct Gemm2Traits {
   static constexpr int kBarrierBytes = 256;
   static constexpr int kStagingBytes = 4 * 2048;
   static constexpr int kTileOutBytes = 128 * kBN * 2;
-  static constexpr int kSmemBytes = 1024 + STAGES * kStageBytes + kBarrierBytes + kStagingBytes + kSignalBytes;
+  static constexpr int kSmemBytesPlain = 1024 + STAGES * kStageBytes + kBarrierBytes;
+  static constexpr int kSmemBytes = kSmemBytesPlain + kStagingBytes + kSignalBytes;
+  static constexpr int smem_bytes(bool fused) { return fused ? kSmemBytes : kSmemBytesPlain; }
   static constexpr uint32_t kIdesc = dev::idesc_i8(256, 256);
-  static_assert(kSmemBytes <= 227 * 1024, "shared memory");
+  // (the launch checks the footprint of the mode it launches: a 7-stage ring
+  // fits only without the fused-mode buffers)
+  static_assert(kSmemBytesPlain <= 227 * 1024, "shared memory");
 };
 
 // Pair p -> (pw, tn): 256-row block index and 256-column block index.
@@ -93,7 +97,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(gemm_block_threads<F
   const int num_pairs = pairs_w * args.tiles_n;
 
   if (threadIdx.x == 0) {
-    init_fused_state(sigq);
+    if constexpr (FUSED) init_fused_state(sigq);  // plain launches carry no staging / hand-over region
     for (int s = 0; s < STAGES; ++s) {
       dev::mbar_init(dev::smem_u32(full + s), 1);
       dev::mbar_init(dev::smem_u32(empty + s), 1);

@@ -35,9 +35,11 @@ struct GemmPlan {
   size_t ws_bytes;          // total workspace bytes needed (0 if no tile is cut)
 };
 
+constexpr int kMaxVariant = 7;
+
 inline int variant_bn(int v) {
   static const int kBn[] = {0, 256, 128, 16, 32, 64, 128, 256};
-  return (v >= 1 && v <= 7) ? kBn[v] : 0;
+  return (v >= 1 && v <= kMaxVariant) ? kBn[v] : 0;
 }
 
 inline bool variant_swap(int v) { return v >= 3 && v <= 6; }
@@ -84,7 +86,7 @@ inline int plan_gemm(int64_t M, int64_t N, int64_t K, int variant, int ctas_req,
       v = 2;
     }
   }
-  if (v < 1 || v > 7) return 1;
+  if (v < 1 || v > kMaxVariant) return 1;
   p->variant = v;
   p->bn = variant_bn(v);
   p->swap = variant_swap(v);

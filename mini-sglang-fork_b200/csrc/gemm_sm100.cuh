@@ -108,7 +108,11 @@ struct GemmTraits {
   static constexpr int kBarrierBytes = 256;
   static constexpr int kStagingBytes = 4 * 2048;  // fused epilogue: 2 KB transpose buffer per warp
   static constexpr int kTileOutBytes = 128 * BN * 2;  // one tile's bf16 block in a receive slot
-  static constexpr int kSmemBytes = 1024 + STAGES * kStageBytes + kBarrierBytes + kStagingBytes + kSignalBytes;
+  // The staging buffer and the hand-over state exist only in fused mode; a
+  // plain GEMM's footprint is the operand ring and the barriers.
+  static constexpr int kSmemBytesPlain = 1024 + STAGES * kStageBytes + kBarrierBytes;
+  static constexpr int kSmemBytes = kSmemBytesPlain + kStagingBytes + kSignalBytes;
+  static constexpr int smem_bytes(bool fused) { return fused ? kSmemBytes : kSmemBytesPlain; }
   static constexpr uint32_t kIdesc = dev::idesc_i8(kBM, BN);
   static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "MMA N");
   static_assert(kSmemBytes <= 227 * 1024, "shared memory");
@@ -603,7 +607,7 @@ __global__ void __launch_bounds__(gemm_block_threads<FUSED>(), 1)
   const int lane = threadIdx.x & 31;
 
   if (threadIdx.x == 0) {
-    init_fused_state(sigq);
+    if constexpr (FUSED) init_fused_state(sigq);  // plain launches carry no staging / hand-over region
     for (int s = 0; s < STAGES; ++s) {
       dev::mbar_init(dev::smem_u32(full + s), 1);
       dev::mbar_init(dev::smem_u32(empty + s), 1);

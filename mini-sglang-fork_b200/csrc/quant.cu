@@ -52,43 +52,52 @@ __device__ __forceinline__ float block_max(float v, float* red) {
 // rint(fl(v/s)) differed, a half-integer would lie between them, i.e. within
 // 2.3e-5 of r; so outside a 6.1e-5 band around half-integers the cheap
 // rint(r) is exact, and inside it the quotient is taken with the IEEE divide.
-// `inv` is only used when s > 0.
-__device__ __forceinline__ int8_t quant_one(float v, float s, float inv) {
-  if (s == 0.0f) return 0;
-  const float r = __fmul_rn(v, inv);
-  const float f = r - floorf(r);
-  const float t = fabsf(f - 0.5f) < 6.1e-5f ? __fdiv_rn(v, s) : r;
-  int q = __float2int_rn(t);
-  q = q > 127 ? 127 : (q < -127 ? -127 : q);
-  return static_cast<int8_t>(q);
+//
+// rint(r) itself uses no conversion-unit instruction (those issue at a
+// quarter of the FP32 rate and bounded the fused SiLU kernel): for |r| < 2^22
+// the sum t = r + 1.5 * 2^23 lies in [2^23, 2^24), where the float spacing is
+// 1, so the addition rounds r to the nearest integer, ties to even, and that
+// integer is the low mantissa field: rint(r) = bits(t) - bits(1.5 * 2^23).
+// r - (t - 1.5 * 2^23) = r - rint(r) is exact (Sterbenz) and gives the
+// distance to the half-integer band.  Two lanes at a time in packed f32x2
+// arithmetic (each lane correctly rounded, as the scalar operations).
+__device__ __forceinline__ void quant_pair(float2 v, float s, float inv, int& q0, int& q1) {
+  constexpr float kRound = 12582912.0f;  // 1.5 * 2^23
+  constexpr int kRoundBits = 0x4B400000;
+  const float2 r = __fmul2_rn(v, make_float2(inv, inv));
+  const float2 t = __fadd2_rn(r, make_float2(kRound, kRound));
+  const float2 ri = __fadd2_rn(t, make_float2(-kRound, -kRound));
+  const float2 f = __fadd2_rn(r, make_float2(-ri.x, -ri.y));  // in [-0.5, 0.5]
+  q0 = __float_as_int(t.x) - kRoundBits;
+  q1 = __float_as_int(t.y) - kRoundBits;
+  if (fabsf(fabsf(f.x) - 0.5f) < 6.1e-5f) q0 = __float2int_rn(__fdiv_rn(v.x, s));
+  if (fabsf(fabsf(f.y) - 0.5f) < 6.1e-5f) q1 = __float2int_rn(__fdiv_rn(v.y, s));
+  q0 = max(-127, min(127, q0));
+  q1 = max(-127, min(127, q1));
 }
 
+// Eight bf16 values -> eight int8 (packed little-endian in a uint2).  s == 0
+// (an all-zero row) has inv == 0, so r == 0 and every q is 0.
 __device__ __forceinline__ uint2 quant_vec8(const uint4& raw, float s, float inv) {
   const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw);
-  uint32_t lo = 0, hi = 0;
+  uint32_t w[2];
 #pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    float2 f = __bfloat1622float2(h[j]);
-    uint32_t b0 = static_cast<uint8_t>(quant_one(f.x, s, inv));
-    uint32_t b1 = static_cast<uint8_t>(quant_one(f.y, s, inv));
-    uint32_t pair = b0 | (b1 << 8);
-    if (j < 2)
-      lo |= pair << (16 * j);
-    else
-      hi |= pair << (16 * (j - 2));
+  for (int j = 0; j < 2; ++j) {
+    int a, b, c, d;
+    quant_pair(__bfloat1622float2(h[2 * j]), s, inv, a, b);
+    quant_pair(__bfloat1622float2(h[2 * j + 1]), s, inv, c, d);
+    w[j] = (static_cast<uint32_t>(a) & 0xffu) | ((static_cast<uint32_t>(b) & 0xffu) << 8) |
+           ((static_cast<uint32_t>(c) & 0xffu) << 16) | (static_cast<uint32_t>(d) << 24);
   }
-  return make_uint2(lo, hi);
+  return make_uint2(w[0], w[1]);
 }
 
+// max |x| over eight bf16 values, compared as bf16 pairs (exact: a maximum
+// involves no rounding) and widened once.
 __device__ __forceinline__ float vec8_absmax(const uint4& raw) {
   const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw);
-  float m = 0.0f;
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    float2 f = __bfloat1622float2(h[j]);
-    m = fmaxf(m, fmaxf(fabsf(f.x), fabsf(f.y)));
-  }
-  return m;
+  const __nv_bfloat162 m = __hmax2(__hmax2(__habs2(h[0]), __habs2(h[1])), __hmax2(__habs2(h[2]), __habs2(h[3])));
+  return fmaxf(__low2float(m), __high2float(m));
 }
 
 // silu(g) = g / (1 + exp(-g)) in fp32.  The fast divide is within a couple of
@@ -129,8 +138,8 @@ constexpr int kEltThreads = 256;
 __global__ void __launch_bounds__(kEltThreads) silu_mul_kernel(const __nv_bfloat16* __restrict__ in, int64_t ld,
                                                                __nv_bfloat16* __restrict__ y, int64_t ldy, int64_t nv,
                                                                int64_t total) {
+  w8a8::dev::griddep_launch();  // the next kernel may start its prologue now (see rows_reg_kernel)
   w8a8::dev::griddep_wait();
-  w8a8::dev::griddep_launch();
   const int64_t step = static_cast<int64_t>(gridDim.x) * kEltThreads;
   for (int64_t v = static_cast<int64_t>(blockIdx.x) * kEltThreads + threadIdx.x; v < total; v += 2 * step) {
     uint4 g[2], u[2];
@@ -187,8 +196,13 @@ __global__ void __launch_bounds__(kRegThreads) rows_reg_kernel(const __nv_bfloat
                                                                int8_t* __restrict__ q, float* __restrict__ scale,
                                                                __nv_bfloat16* __restrict__ y_out, int width) {
   __shared__ float red[32];
-  w8a8::dev::griddep_wait();  // the row is the previous kernel's output
+  // Dependent launch is triggered before waiting for this kernel's own input:
+  // the next kernel (typically a GEMM) may then start its prologue and weight
+  // prefetch while the kernel before this one drains.  That is safe because
+  // the next kernel waits for this grid's completion (which follows the wait
+  // below) before it reads anything this grid writes.
   w8a8::dev::griddep_launch();
+  w8a8::dev::griddep_wait();  // the row is the previous kernel's output
   const int64_t row = blockIdx.x;
   const int nvec = width >> 3;
   const RowSrc<SILU> src(in, row, ld, width);
@@ -230,8 +244,8 @@ __global__ void __launch_bounds__(kSmemThreads) rows_smem_kernel(const __nv_bflo
                                                                  __nv_bfloat16* __restrict__ y_out, int width) {
   extern __shared__ uint4 stage[];
   __shared__ float red[32];
-  w8a8::dev::griddep_wait();  // the row is the previous kernel's output
-  w8a8::dev::griddep_launch();
+  w8a8::dev::griddep_launch();  // early trigger, as in rows_reg_kernel
+  w8a8::dev::griddep_wait();    // the row is the previous kernel's output
   const int64_t row = blockIdx.x;
   const int nvec = width >> 3;
   const RowSrc<SILU> src(in, row, ld, width);
@@ -272,6 +286,171 @@ __global__ void __launch_bounds__(kSmemThreads) rows_smem_kernel(const __nv_bflo
   if (threadIdx.x == 0) scale[row] = s;
 }
 
+// Staged path (the plain quantiser, many rows of at most 24 KB): persistent
+// CTAs, CTA b taking rows b, b + G, b + 2G, ...  Thread 0 keeps DEPTH whole
+// rows in flight with 1-D bulk copies (cp.async.bulk, global -> shared
+// memory, completing on one mbarrier per stage); every thread then reads its
+// VPT vectors of the current row from shared memory, and as soon as the
+// block's absmax reduction shows that the row has been read, thread 0 reuses
+// the stage for the row DEPTH ahead.  The loads of later rows therefore stay
+// in flight while a row is reduced and quantised, which the one-row-per-CTA
+// path cannot do (its load phase drains before each reduction).
+// Waits on the stage barriers are bounded; on expiry the kernel records the
+// error, waits (bounded) for its copies still in flight and returns.
+constexpr int kStagedMaxRowBytes = 24 * 1024;
+constexpr int kStagedSmemBytes = 48 * 1024;
+
+constexpr int kStagedMaxThreads = 512;  // nvec / 4 threads: <= 384 for 24 KB rows
+
+template <int VPT>
+__global__ void __launch_bounds__(kStagedMaxThreads) rows_staged_kernel(const __nv_bfloat16* __restrict__ in, int64_t ld,
+                                                                  int8_t* __restrict__ q, float* __restrict__ scale,
+                                                                  int64_t M, int width, int depth, unsigned int* err,
+                                                                  long long timeout_ns) {
+  extern __shared__ __align__(128) uint4 rows_smem[];
+  __shared__ float red[32];
+  __shared__ uint64_t full[8];
+  __shared__ int abort_flag;
+  w8a8::dev::griddep_launch();  // early trigger, as in rows_reg_kernel
+  const int nvec = width >> 3;
+  const uint32_t row_bytes = static_cast<uint32_t>(width) * 2u;
+  const uint32_t stage_vecs = (row_bytes + 127u) / 128u * 8u;  // stages 128-byte aligned
+  const int64_t G = gridDim.x;
+  const int64_t nrows = (M - blockIdx.x + G - 1) / G;  // rows of this CTA
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < depth; ++i) w8a8::dev::mbar_init(w8a8::dev::smem_u32(&full[i]), 1);
+    abort_flag = 0;
+    w8a8::dev::fence_mbar_init();
+  }
+  __syncthreads();
+  w8a8::dev::griddep_wait();  // the rows are the previous kernel's output
+  const uint64_t policy = w8a8::dev::policy_evict_first();
+  auto issue = [&](int64_t i) {  // row i of this CTA into stage i % depth
+    const int st = static_cast<int>(i % depth);
+    const uint32_t bar = w8a8::dev::smem_u32(&full[st]);
+    w8a8::dev::mbar_expect_tx(bar, row_bytes);
+    w8a8::dev::bulk_load_1d(w8a8::dev::smem_u32(rows_smem + st * stage_vecs), in + (blockIdx.x + i * G) * ld,
+                            row_bytes, bar, policy);
+  };
+  if (threadIdx.x == 0)
+    for (int64_t i = 0; i < depth && i < nrows; ++i) issue(i);
+  int64_t issued = nrows < depth ? nrows : depth;
+  for (int64_t i = 0; i < nrows; ++i) {
+    const int st = static_cast<int>(i % depth);
+    const uint32_t parity = static_cast<uint32_t>((i / depth) & 1);
+    const bool ok = w8a8::dev::mbar_wait(w8a8::dev::smem_u32(&full[st]), parity, &abort_flag, err,
+                                         w8a8::kErrGemmWait, timeout_ns);
+    if (__syncthreads_or(!ok)) break;
+    const uint4* row = rows_smem + st * stage_vecs;
+    uint4 buf[VPT];
+    float amax = 0.0f;
+#pragma unroll
+    for (int j = 0; j < VPT; ++j) {
+      const int vi = threadIdx.x + j * blockDim.x;
+      if (vi < nvec) {
+        buf[j] = row[vi];
+        amax = fmaxf(amax, vec8_absmax(buf[j]));
+      }
+    }
+    amax = block_max(amax, red);  // its barrier also means every thread has read the stage
+    if (threadIdx.x == 0 && issued < nrows) issue(issued);
+    ++issued;
+    const float sc = __fdiv_rn(amax, 127.0f);
+    const float inv = sc > 0.0f ? __frcp_rn(sc) : 0.0f;
+    const int64_t r = blockIdx.x + i * G;
+    uint2* qr = reinterpret_cast<uint2*>(q + r * static_cast<int64_t>(width));
+#pragma unroll
+    for (int j = 0; j < VPT; ++j) {
+      const int vi = threadIdx.x + j * blockDim.x;
+      if (vi < nvec) qr[vi] = quant_vec8(buf[j], sc, inv);
+    }
+    if (threadIdx.x == 0) scale[r] = sc;
+    __syncthreads();  // `red` is reused by the next row's reduction
+  }
+  // After an abort, copies may still be landing: wait (bounded) for every
+  // issued stage before the CTA's shared memory is released.
+  if (threadIdx.x == 0 && abort_flag) {
+    const int64_t last = issued < nrows ? issued : nrows;
+    for (int64_t i = last - depth < 0 ? 0 : last - depth; i < last; ++i) {
+      if (!w8a8::dev::mbar_wait_drain(w8a8::dev::smem_u32(&full[i % depth]), static_cast<uint32_t>((i / depth) & 1),
+                                      timeout_ns) && err)
+        atomicOr(err, w8a8::kErrGemmDrain);
+    }
+  }
+}
+
+// Cluster path (few rows): one row per cluster of C CTAs (C = the cluster
+// size, 2..8), CTA c taking vectors [c*nvec/C, (c+1)*nvec/C) of the row in
+// registers (VPT per thread).  Each CTA reduces its share's absmax, publishes
+// it in its shared memory, and after a cluster barrier reads all C values
+// through distributed shared memory (ld.shared::cluster), so every CTA
+// quantises its share with the row's scale.  At decode sizes (M of 1..64)
+// that spreads the row's HBM traffic and SiLU arithmetic over M*C SMs instead
+// of M.  Same arithmetic as the one-CTA paths, so the results are identical.
+__device__ __forceinline__ float cluster_max(float v, float* slot) {
+  *slot = v;
+  w8a8::dev::cluster_sync();  // every CTA's slot written (release / acquire at cluster scope)
+  uint32_t n;
+  asm volatile("mov.u32 %0, %%cluster_nctarank;" : "=r"(n));
+  const uint32_t local = w8a8::dev::smem_u32(slot);
+  float m = 0.0f;
+  for (uint32_t r = 0; r < n; ++r) {
+    float x;
+    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(x) : "r"(w8a8::dev::mapa(local, r)) : "memory");
+    m = fmaxf(m, x);
+  }
+  return m;
+}
+
+template <int VPT, bool SILU>
+__global__ void __launch_bounds__(kRegThreads) rows_cluster_kernel(const __nv_bfloat16* __restrict__ in, int64_t ld,
+                                                                   int8_t* __restrict__ q, float* __restrict__ scale,
+                                                                   __nv_bfloat16* __restrict__ y_out, int width) {
+  __shared__ float red[32];
+  __shared__ float share_max;
+  w8a8::dev::griddep_launch();  // early trigger, as in rows_reg_kernel
+  w8a8::dev::griddep_wait();
+  uint32_t c, nc;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(c));
+  asm volatile("mov.u32 %0, %%cluster_nctarank;" : "=r"(nc));
+  const int64_t row = blockIdx.x / nc;
+  const int nvec = width >> 3;
+  const int lo = static_cast<int>((static_cast<int64_t>(nvec) * c) / nc);
+  const int hi = static_cast<int>((static_cast<int64_t>(nvec) * (c + 1)) / nc);
+  const RowSrc<SILU> src(in, row, ld, width);
+  uint4 buf[VPT], aux[VPT];
+  float amax = 0.0f;
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    const int vi = lo + threadIdx.x + i * kRegThreads;
+    if (vi < hi) src.fetch(vi, buf[i], aux[i]);
+  }
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    const int vi = lo + threadIdx.x + i * kRegThreads;
+    if (vi < hi) {
+      buf[i] = src.combine(buf[i], aux[i]);
+      amax = fmaxf(amax, vec8_absmax(buf[i]));
+    }
+  }
+  amax = block_max(amax, red);
+  amax = cluster_max(amax, &share_max);
+  const float s = __fdiv_rn(amax, 127.0f);
+  const float inv = s > 0.0f ? __frcp_rn(s) : 0.0f;
+  uint2* qr = reinterpret_cast<uint2*>(q + row * static_cast<int64_t>(width));
+  uint4* yr = y_out ? reinterpret_cast<uint4*>(y_out + row * static_cast<int64_t>(width)) : nullptr;
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    const int vi = lo + threadIdx.x + i * kRegThreads;
+    if (vi < hi) {
+      qr[vi] = quant_vec8(buf[i], s, inv);
+      if (SILU && yr) yr[vi] = buf[i];
+    }
+  }
+  if (c == 0 && threadIdx.x == 0) scale[row] = s;
+  w8a8::dev::cluster_sync();  // no CTA leaves while a peer may still read its share_max
+}
+
 // ------------------------------------------------------------------ RMSNorm
 // RMSNorm (optionally after a residual add) fused with the per-token quantiser:
 // the input side of qkv and gate_up (RMSNorm / RMSNormFused,
@@ -304,8 +483,8 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_quant_kernel(
     const __nv_bfloat16* __restrict__ w, float eps, int8_t* __restrict__ q, float* __restrict__ scale,
     __nv_bfloat16* residual_out, __nv_bfloat16* __restrict__ y_out, int width) {
   __shared__ float red[32];
-  w8a8::dev::griddep_wait();  // x / residual are the previous kernel's output
-  w8a8::dev::griddep_launch();
+  w8a8::dev::griddep_launch();  // early trigger, as in rows_reg_kernel
+  w8a8::dev::griddep_wait();    // x / residual are the previous kernel's output
   const int64_t row = blockIdx.x;
   const int nvec = width >> 3;
   const uint4* xr = reinterpret_cast<const uint4*>(x + row * ldx);
@@ -403,11 +582,95 @@ int launch_rmsnorm(const __nv_bfloat16* x, int64_t ldx, const __nv_bfloat16* res
   return W8A8_OK;
 }
 
+// Cluster size for the split-row path: the smallest power of two (2..8) that
+// gives at least two CTAs per SM over the M rows and at most four vectors per
+// thread; 0 = use the one-CTA-per-row paths (enough rows, or short rows).
+inline int row_cluster_size(int64_t M, int nvec, int nsm) {
+  if (nvec < 2 * kRegThreads || M >= 2LL * nsm) return 0;
+  for (int c = 2; c <= 8; c *= 2)
+    if (M * c >= 2LL * nsm && (nvec + c - 1) / c <= 4 * kRegThreads) return c;
+  return (nvec + 7) / 8 <= 4 * kRegThreads ? 8 : 0;
+}
+
+template <int VPT, bool SILU>
+cudaError_t launch_cluster_rows(const __nv_bfloat16* in, int64_t ld, int8_t* q, float* scale, __nv_bfloat16* y,
+                                int64_t M, int width, int csize, cudaStream_t s) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(M * csize));
+  cfg.blockDim = dim3(kRegThreads);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = static_cast<unsigned>(csize);
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  return cudaLaunchKernelEx(&cfg, rows_cluster_kernel<VPT, SILU>, in, ld, q, scale, y, width);
+}
+
+// Staged path launch: VPT = 4 vectors per thread (threads = nvec / 4
+// rounded up to a warp), DEPTH rows in flight within 48 KB of shared memory,
+// as many persistent CTAs as fit on the SMs (by threads and by shared memory).
+int launch_staged_rows(const __nv_bfloat16* in, int64_t ld, int8_t* q, float* scale, int64_t M, int width,
+                       int nsm, cudaStream_t s) {
+  const int nvec = width / 8;
+  const int threads = ((nvec + 3) / 4 + 31) / 32 * 32;
+  const int stage_bytes = (width * 2 + 127) / 128 * 128;
+  int depth = kStagedSmemBytes / stage_bytes;
+  depth = depth < 2 ? 2 : (depth > 8 ? 8 : depth);
+  const int smem = depth * stage_bytes;
+  int per_sm = 2048 / threads;
+  const int by_smem = (227 * 1024) / (smem + 1024 + 512);
+  per_sm = per_sm < by_smem ? per_sm : by_smem;
+  per_sm = per_sm < 1 ? 1 : (per_sm > 16 ? 16 : per_sm);
+  int64_t grid = static_cast<int64_t>(nsm) * per_sm;
+  if (grid > M) grid = M;
+  unsigned int* err = w8a8::device_error_word();
+  if (!err) return W8A8_ERR_CUDA;
+  static std::mutex mu;
+  static bool configured[64] = {false};
+  const int dev = w8a8::current_device();
+  W8A8_REQUIRE(dev >= 0 && dev < 64, W8A8_ERR_CUDA, "no current device");
+  {
+    std::lock_guard<std::mutex> lk(mu);
+    if (!configured[dev]) {
+      W8A8_CUDA_TRY(cudaFuncSetAttribute(rows_staged_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         kStagedSmemBytes));
+      configured[dev] = true;
+    }
+  }
+  W8A8_CUDA_TRY(w8a8::launch_pdl(rows_staged_kernel<4>, dim3(static_cast<unsigned>(grid)), dim3(threads),
+                                 static_cast<size_t>(smem), s, in, ld, q, scale, M, width, depth, err,
+                                 w8a8::kDefaultGemmTimeoutNs));
+  return W8A8_OK;
+}
+
 template <bool SILU>
 int launch_rows(const __nv_bfloat16* in, int64_t ld, int8_t* q, float* scale, __nv_bfloat16* y, int64_t M,
                 int width, cudaStream_t s) {
   const int nvec = width / 8;
   const dim3 grid(static_cast<unsigned>(M));
+  int nsm = w8a8::sm_count();
+  if (nsm <= 0) nsm = 148;
+  const int csize = row_cluster_size(M, nvec, nsm);
+  // many rows of the plain quantiser: the bulk-copy staged persistent kernel
+  if (!SILU && csize == 0 && width * 2 <= kStagedMaxRowBytes && nvec >= 64 &&
+      (reinterpret_cast<uintptr_t>(in) & 15u) == 0 && ld % 8 == 0)
+    return launch_staged_rows(in, ld, q, scale, M, width, nsm, s);
+  if (csize > 0) {
+    const int per = (nvec + csize - 1) / csize;
+    const int vpt = per <= kRegThreads ? 1 : (per <= 2 * kRegThreads ? 2 : 4);
+    switch (vpt) {
+      case 1: W8A8_CUDA_TRY((launch_cluster_rows<1, SILU>(in, ld, q, scale, y, M, width, csize, s))); break;
+      case 2: W8A8_CUDA_TRY((launch_cluster_rows<2, SILU>(in, ld, q, scale, y, M, width, csize, s))); break;
+      default: W8A8_CUDA_TRY((launch_cluster_rows<4, SILU>(in, ld, q, scale, y, M, width, csize, s))); break;
+    }
+    return W8A8_OK;
+  }
   if (nvec <= 4 * kRegThreads) {
     const int vpt = nvec <= kRegThreads ? 1 : (nvec <= 2 * kRegThreads ? 2 : 4);
     const int need = (nvec + vpt - 1) / vpt;

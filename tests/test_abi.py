@@ -70,7 +70,15 @@ def test_host_validation_rejects_bad_arguments(pkg):
     assert lib.w8a8_quant_per_token(None, 16, None, None, 0, 16, None) == L.OK
     assert lib.w8a8_silu_mul_quant(None, 32, None, None, None, 0, 16, None) == L.OK
     assert lib.w8a8_gemm_config(16, 16, 16, 16, None, 16, None, 0, 32, 32, 0, 0, None, 0, None) == L.OK
-    assert lib.w8a8_gemm_config(16, 16, 16, 16, None, 16, None, 8, 32, 32, 9, 0, None, 0, None) == L.ERR_INVALID_ARG
+    assert lib.w8a8_gemm_config(16, 16, 16, 16, None, 16, None, 8, 32, 32, 8, 0, None, 0, None) == L.ERR_INVALID_ARG
+    # silu_mul_quant: q and scale come together; the bf16-only form needs y_out
+    st = lib.w8a8_silu_mul_quant(16, 32, 16, None, 16, 2, 16, None)
+    assert st == L.ERR_INVALID_ARG and b"together" in lib.w8a8_last_error()
+    st = lib.w8a8_silu_mul_quant(16, 32, None, None, None, 2, 16, None)
+    assert st == L.ERR_INVALID_ARG and b"nothing to write" in lib.w8a8_last_error()
+    # broadcast / peak probe: rejected on the host
+    assert lib.w8a8_broadcast(None, 16, 16, 0, None) == L.ERR_INVALID_ARG
+    assert lib.w8a8_mma_peak_probe(2, 10, None, None) == L.ERR_INVALID_ARG
 
 
 @pytest.mark.parametrize("m,n,k,variant,bn,swap", [

@@ -147,3 +147,69 @@ def test_silu_and_mul_bf16_only(pkg, oracle, cuda_dev, m, i):
     y_ref = oracle.silu_and_mul(gu.contiguous())
     diff = (y.cpu().float() - y_ref.float()).abs()
     assert torch.all(diff <= y_ref.float().abs() * 2.0 ** -7 + 1e-30), float(diff.max())
+
+
+# Few rows (decode): each row is split over a cluster of 2..8 CTAs whose
+# absmax meets through distributed shared memory; 1..4 vectors per thread.
+CLUSTER_SHAPES = [(1, 4096), (1, 5120), (1, 32768), (16, 5120), (32, 8192), (37, 25600), (64, 12800),
+                  (100, 6400), (200, 4096), (295, 5120)]
+
+
+@pytest.mark.parametrize("m,k", CLUSTER_SHAPES)
+def test_quant_per_token_cluster_rows(pkg, oracle, cuda_dev, m, k):
+    x = _x(m, k, seed=m * 11 + k, scale=3.0)
+    x[0, k // 3] = 40.0  # absmax in a middle CTA of the cluster
+    if m > 2:
+        x[2].zero_()  # all-zero row: scale 0, q 0
+    q, s = pkg.ops.quant_per_token(x.to(cuda_dev))
+    q_ref, s_ref = oracle.quant_per_token(x)
+    assert torch.equal(s.cpu(), s_ref) and torch.equal(q.cpu(), q_ref)
+
+
+@pytest.mark.parametrize("m,i", [(1, 25600), (1, 3200), (8, 12800), (32, 25600), (64, 6400), (150, 4096)])
+def test_silu_mul_quant_cluster_rows(pkg, oracle, cuda_dev, m, i):
+    gu = _x(m, 2 * i, seed=m + 3 * i, scale=2.0)
+    qa, y = pkg.ops.silu_and_mul_quant(gu.to(cuda_dev), with_bf16=True)
+    y_ref = oracle.silu_and_mul(gu)
+    yc = y.cpu()
+    diff = (yc.float() - y_ref.float()).abs()
+    assert torch.all(diff <= y_ref.float().abs() * 2.0 ** -7 + 1e-30), float(diff.max())
+    q_ref, s_ref = oracle.quant_per_token(yc)
+    assert torch.equal(qa.s.cpu(), s_ref) and torch.equal(qa.q.cpu(), q_ref)
+    # the quantisation without the bf16 output is the same
+    qa2 = pkg.ops.silu_and_mul_quant(gu.to(cuda_dev))
+    assert torch.equal(qa2.q.cpu(), qa.q.cpu()) and torch.equal(qa2.s.cpu(), qa.s.cpu())
+
+
+# Many rows of at most 24 KB: the persistent kernel that keeps several rows in
+# flight with bulk copies into shared memory (rows per CTA > pipeline depth,
+# ragged last wave, strided rows as in the q slice of a qkv output).
+STAGED_SHAPES = [(296, 5120, 5120), (4096, 5120, 5120), (4096, 8192, 10240), (1000, 12288, 12288),
+                 (777, 512, 520), (3000, 2048, 2048), (513, 1024, 1536)]
+
+
+@pytest.mark.parametrize("m,k,ld", STAGED_SHAPES)
+def test_quant_per_token_staged_rows(pkg, oracle, cuda_dev, m, k, ld):
+    full = _x(m, ld, seed=m + k + ld, scale=2.5)
+    full[m // 2, k - 1] = -77.0  # absmax at a row's last element
+    full[m - 1].zero_()
+    x = full.to(cuda_dev)[:, :k]
+    q, s = pkg.ops.quant_per_token(x)
+    q_ref, s_ref = oracle.quant_per_token(full[:, :k].contiguous())
+    assert torch.equal(s.cpu(), s_ref) and torch.equal(q.cpu(), q_ref)
+
+
+def test_quant_half_integer_ties(pkg, oracle, cuda_dev):
+    """Values whose quotient lies on or within the guard band of a
+    half-integer (the rounding path that falls back to the IEEE divide),
+    through every quantiser path (register, cluster, staged)."""
+    k = 5120
+    for m in (1, 64, 600):
+        x = torch.zeros(m, k)
+        x[:, 0] = 127.0
+        ticks = torch.arange(1, k, dtype=torch.float32)
+        x[:, 1:] = ((ticks % 254) - 127 + 0.5) * (1 + 1e-6 * (ticks % 7 - 3))
+        xb = x.bfloat16()
+        q, s = pkg.ops.quant_per_token(xb.to(cuda_dev))
+        q_ref, s_ref = oracle.quant_per_token(xb)
+        assert torch.equal(s.cpu(), s_ref) and torch.equal(q.cpu(), q_ref), m
