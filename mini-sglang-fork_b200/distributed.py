@@ -1,16 +1,26 @@
 """Tensor-parallel geometry and the all-reduce plugin stack.
 
-Mirrors mini-sglang's ``minisgl.distributed`` (M/distributed/info.py:1-38,
-M/distributed/impl.py:15-97): a process-global ``DistributedInfo`` set once per
-rank, and a ``DistributedCommunicator`` that dispatches ``all_reduce`` /
-``all_gather`` to the last registered plugin.  ``TorchDistributedImpl`` is the
-plain ``torch.distributed`` plugin (NCCL on GPUs, gloo on CPU ranks);
-``PeerMemDistributedImpl`` routes ``all_reduce`` to this package's NVLink
-peer-memory communicator (``enable_peer_mem_distributed``, the counterpart of
-``enable_pynccl_distributed``).
+Inside mini-sglang the layers use the reference's own state: when
+``minisgl.distributed`` (M/distributed/) is importable and its
+``set_tp_info`` has been called, ``get_tp_info`` returns the reference's
+``DistributedInfo``, ``communicator()`` returns the reference's
+``DistributedCommunicator`` (so a row-parallel layer without the fused reduce
+all-reduces through whatever plugin the engine enabled, PyNCCL included), and
+``enable_peer_mem_distributed`` appends its plugin to the reference's plugin
+list exactly as ``enable_pynccl_distributed`` does (M/distributed/impl.py:73-90).
+
+Standalone (the reference not importable, or its TP info unset) the same
+surface is served by this module's own copy of it, mirroring
+M/distributed/info.py:1-38 and M/distributed/impl.py:15-97: a process-global
+``DistributedInfo`` set once per rank and a ``DistributedCommunicator`` that
+dispatches ``all_reduce`` / ``all_gather`` to the last registered plugin.
+``TorchDistributedImpl`` is the plain ``torch.distributed`` plugin (NCCL on
+GPUs, gloo on CPU ranks); ``PeerMemDistributedImpl`` routes ``all_reduce`` to
+this package's NVLink peer-memory communicator.
 """
 from __future__ import annotations
 
+import importlib
 from abc import ABC, abstractmethod
 from dataclasses import dataclass
 from typing import TYPE_CHECKING, List, Optional
@@ -35,7 +45,29 @@ __all__ = [
     "get_peer_mem_comm",
     "destroy_distributed",
     "div_even",
+    "communicator",
+    "reference_distributed",
 ]
+
+
+def reference_distributed():
+    """The reference's ``minisgl.distributed`` module when it is importable
+    (mini-sglang installed beside this package), else None."""
+    try:
+        return importlib.import_module("minisgl.distributed")
+    except ImportError:
+        return None
+
+
+def _bound_reference():
+    """The reference's module when the layers should use its state: it is
+    importable, its TP info is set and this module's own is not."""
+    if _TP_INFO is not None:
+        return None
+    ref = reference_distributed()
+    if ref is None or ref.try_get_tp_info() is None:
+        return None
+    return ref
 
 
 @dataclass(frozen=True)
@@ -64,13 +96,21 @@ def set_tp_info(rank: int, size: int) -> None:
 
 
 def get_tp_info() -> DistributedInfo:
-    if _TP_INFO is None:
-        raise RuntimeError("TP info has not been set")
-    return _TP_INFO
+    """This process's TP info: this module's own when set, else the
+    reference's (M/distributed/info.py:28-31) when it has been set there."""
+    if _TP_INFO is not None:
+        return _TP_INFO
+    ref = _bound_reference()
+    if ref is not None:
+        return ref.get_tp_info()
+    raise RuntimeError("TP info has not been set")
 
 
 def try_get_tp_info() -> Optional[DistributedInfo]:
-    return _TP_INFO
+    if _TP_INFO is not None:
+        return _TP_INFO
+    ref = _bound_reference()
+    return ref.try_get_tp_info() if ref is not None else None
 
 
 def reset_tp_info() -> None:
@@ -146,6 +186,15 @@ class DistributedCommunicator:
         return self.plugins[-1].all_gather(x)
 
 
+def communicator():
+    """The all-reduce dispatcher the row-parallel layers fall back to when
+    the reduce is not fused: the reference's ``DistributedCommunicator`` when
+    its state is in use (so the engine's PyNCCL plugin is reached), else this
+    module's."""
+    ref = _bound_reference()
+    return ref.DistributedCommunicator() if ref is not None else DistributedCommunicator()
+
+
 _PEER_MEM_COMM: Optional["PeerMemCommunicator"] = None
 
 
@@ -162,7 +211,11 @@ def enable_peer_mem_distributed(tp_info: DistributedInfo, tp_cpu_group, max_byte
 
     comm = PeerMemCommunicator(tp_info.rank, tp_info.size, max_bytes, tp_cpu_group, device=device)
     _PEER_MEM_COMM = comm
-    DistributedCommunicator.plugins.append(PeerMemDistributedImpl(comm))
+    plugin = PeerMemDistributedImpl(comm)
+    DistributedCommunicator.plugins.append(plugin)
+    ref = _bound_reference()
+    if ref is not None:  # the engine's own dispatcher reaches it too, as PyNCCL's plugin does
+        ref.DistributedCommunicator.plugins.append(plugin)
     return comm
 
 
@@ -171,8 +224,13 @@ def get_peer_mem_comm() -> Optional["PeerMemCommunicator"]:
 
 
 def destroy_distributed() -> None:
-    """Drop every plugin and the peer-memory communicator (M/distributed/impl.py:93-97)."""
+    """Drop every plugin and the peer-memory communicator (M/distributed/impl.py:93-97);
+    this package's plugin also leaves the reference's list."""
     global _PEER_MEM_COMM
+    ref = reference_distributed()
+    if ref is not None:
+        ref.DistributedCommunicator.plugins = [p for p in ref.DistributedCommunicator.plugins
+                                               if not isinstance(p, PeerMemDistributedImpl)]
     if _PEER_MEM_COMM is not None:
         _PEER_MEM_COMM.close()
     _PEER_MEM_COMM = None

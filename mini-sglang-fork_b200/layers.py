@@ -21,7 +21,7 @@ from typing import Any, Dict, List, Optional, Union
 import torch
 
 from . import ops
-from .distributed import DistributedCommunicator, div_even, get_peer_mem_comm, get_tp_info
+from .distributed import communicator, div_even, get_peer_mem_comm, get_tp_info
 from .ops import QuantizedActivation
 
 _STATE_DICT = Dict[str, torch.Tensor]
@@ -142,7 +142,7 @@ class _RowParallel(_LinearTPImpl):
     communicator the reduction runs inside the GEMM kernel."""
 
     _tp_size: int
-    _comm: DistributedCommunicator
+    _comm: object  # a DistributedCommunicator: the reference's when its state is in use
 
     def forward(self, x: Union[torch.Tensor, QuantizedActivation]) -> torch.Tensor:
         qa = self._quantize_input(x)
@@ -160,7 +160,7 @@ class LinearOProj(_RowParallel):
 
     def __init__(self, input_size: int, output_size: int, has_bias: bool):
         tp_info = get_tp_info()
-        self._comm = DistributedCommunicator()
+        self._comm = communicator()
         self._tp_size = tp_info.size
         super().__init__(input_size, output_size, div_even(input_size, tp_info.size), output_size, has_bias)
 
@@ -170,7 +170,7 @@ class LinearRowParallel(_RowParallel):
 
     def __init__(self, input_size: int, output_size: int, has_bias: bool):
         tp_info = get_tp_info()
-        self._comm = DistributedCommunicator()
+        self._comm = communicator()
         self._tp_size = tp_info.size
         super().__init__(input_size, output_size, div_even(input_size, tp_info.size), output_size, has_bias)
 

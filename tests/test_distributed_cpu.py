@@ -183,3 +183,116 @@ def test_rank_that_never_joins_times_out():
     assert out[1][0] == "ok"
     assert out[0][0] == "error"
     assert "timed out" in out[0][1].lower() or "timeout" in out[0][1].lower()
+
+
+# ---------------------------------------------------------------- binding to the reference's own state
+def _fresh_reference_modules(monkeypatch):
+    """The reference's minisgl.distributed: the real package when
+    MINISGL_PYTHON names mini-sglang's python/ directory (or it is already
+    importable), else None."""
+    import importlib
+    import sys
+
+    path = os.environ.get("MINISGL_PYTHON")
+    if path:
+        monkeypatch.syspath_prepend(path)
+    try:
+        ref = importlib.import_module("minisgl.distributed")
+    except ImportError:
+        return None
+    info = sys.modules["minisgl.distributed.info"]
+    monkeypatch.setattr(info, "_TP_INFO", None)
+    monkeypatch.setattr(ref.DistributedCommunicator, "plugins", list(ref.DistributedCommunicator.plugins))
+    return ref
+
+
+def _stand_in_reference(monkeypatch):
+    """A minimal module with the reference's distributed surface
+    (set_tp_info / get_tp_info / try_get_tp_info / DistributedCommunicator
+    with a class-level plugin list), registered as minisgl.distributed."""
+    import sys
+    import types
+
+    mod = types.ModuleType("minisgl.distributed")
+    state = {"info": None}
+
+    class Info:
+        def __init__(self, rank, size):
+            self.rank, self.size = rank, size
+
+    class Communicator:
+        plugins = []
+
+        def all_reduce(self, x):
+            return self.plugins[-1].all_reduce(x)
+
+    def set_tp_info(rank, size):
+        state["info"] = Info(rank, size)
+
+    mod.set_tp_info = set_tp_info
+    mod.get_tp_info = lambda: state["info"]
+    mod.try_get_tp_info = lambda: state["info"]
+    mod.DistributedCommunicator = Communicator
+    pkg = types.ModuleType("minisgl")
+    pkg.__path__ = []
+    monkeypatch.setitem(sys.modules, "minisgl", pkg)
+    monkeypatch.setitem(sys.modules, "minisgl.distributed", mod)
+    return mod
+
+
+def _check_layers_follow_reference(pkg, ref, monkeypatch):
+    D = pkg.distributed
+    D.reset_tp_info()
+    ref.set_tp_info(1, 4)  # the reference engine's call (M/engine/engine.py:32); none to this package
+    assert D.get_tp_info().size == 4 and D.get_tp_info().rank == 1
+    qkv = pkg.LinearQKVMerged(5120, 128, 64, 8, has_bias=False)
+    gate_up = pkg.LinearColParallelMerged(5120, [25600, 25600], has_bias=False)
+    down = pkg.LinearRowParallel(25600, 5120, has_bias=False)
+    assert tuple(qkv.weight.shape) == ((16 + 2 * 2) * 128, 5120)
+    assert tuple(gate_up.weight.shape) == (12800, 5120)
+    assert tuple(down.weight.shape) == (5120, 6400) and tuple(down.weight_scale.shape) == (5120,)
+    # the row-parallel fallback reduce goes through the reference's dispatcher
+    assert isinstance(down._comm, ref.DistributedCommunicator)
+    seen = []
+
+    class Probe:
+        def all_reduce(self, x):
+            seen.append(x)
+            return x
+
+    ref.DistributedCommunicator.plugins.append(Probe())
+    t = torch.ones(3)
+    assert down._comm.all_reduce(t) is t and seen == [t]
+    # enable_peer_mem_distributed registers its plugin with the reference's list too
+    created = []
+
+    class FakeComm:
+        def __init__(self, rank, world, max_bytes, group, device=None):
+            created.append((rank, world))
+
+        def close(self):
+            pass
+
+    monkeypatch.setattr(pkg.comm, "PeerMemCommunicator", FakeComm)
+    D.enable_peer_mem_distributed(D.get_tp_info(), None, max_bytes=1024)
+    assert created == [(1, 4)]
+    assert isinstance(ref.DistributedCommunicator.plugins[-1], D.PeerMemDistributedImpl)
+    D.destroy_distributed()
+    assert not any(isinstance(p, D.PeerMemDistributedImpl) for p in ref.DistributedCommunicator.plugins)
+    D.DistributedCommunicator.plugins = [D.TorchDistributedImpl()]
+
+
+def test_layers_follow_a_reference_style_distributed_module(pkg, monkeypatch):
+    ref = _stand_in_reference(monkeypatch)
+    _check_layers_follow_reference(pkg, ref, monkeypatch)
+    # this package's own set_tp_info takes precedence once called
+    pkg.distributed.set_tp_info(0, 2)
+    assert pkg.distributed.get_tp_info().size == 2
+    pkg.distributed.reset_tp_info()
+
+
+def test_layers_follow_the_reference_distributed_state(pkg, monkeypatch):
+    ref = _fresh_reference_modules(monkeypatch)
+    if ref is None:
+        pytest.skip("mini-sglang is not importable here (set MINISGL_PYTHON to its python/ directory)")
+    _check_layers_follow_reference(pkg, ref, monkeypatch)
