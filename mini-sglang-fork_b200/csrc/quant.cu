@@ -54,42 +54,65 @@ __device__ __forceinline__ float block_max(float v, float* red) {
 // rint(r) is exact, and inside it the quotient is taken with the IEEE divide.
 //
 // rint(r) itself uses no conversion-unit instruction (those issue at a
-// quarter of the FP32 rate and bounded the fused SiLU kernel): for |r| < 2^22
-// the sum t = r + 1.5 * 2^23 lies in [2^23, 2^24), where the float spacing is
-// 1, so the addition rounds r to the nearest integer, ties to even, and that
-// integer is the low mantissa field: rint(r) = bits(t) - bits(1.5 * 2^23).
-// r - (t - 1.5 * 2^23) = r - rint(r) is exact (Sterbenz) and gives the
-// distance to the half-integer band.  Two lanes at a time in packed f32x2
-// arithmetic (each lane correctly rounded, as the scalar operations).
-__device__ __forceinline__ void quant_pair(float2 v, float s, float inv, int& q0, int& q1) {
-  constexpr float kRound = 12582912.0f;  // 1.5 * 2^23
-  constexpr int kRoundBits = 0x4B400000;
-  const float2 r = __fmul2_rn(v, make_float2(inv, inv));
-  const float2 t = __fadd2_rn(r, make_float2(kRound, kRound));
-  const float2 ri = __fadd2_rn(t, make_float2(-kRound, -kRound));
-  const float2 f = __fadd2_rn(r, make_float2(-ri.x, -ri.y));  // in [-0.5, 0.5]
-  q0 = __float_as_int(t.x) - kRoundBits;
-  q1 = __float_as_int(t.y) - kRoundBits;
-  if (fabsf(fabsf(f.x) - 0.5f) < 6.1e-5f) q0 = __float2int_rn(__fdiv_rn(v.x, s));
-  if (fabsf(fabsf(f.y) - 0.5f) < 6.1e-5f) q1 = __float2int_rn(__fdiv_rn(v.y, s));
-  q0 = max(-127, min(127, q0));
-  q1 = max(-127, min(127, q1));
+// quarter of the FP32 rate): for |r| < 2^22 the sum t = r + 1.5 * 2^23 lies in
+// [2^23, 2^24), where the float spacing is 1, so the addition rounds r to the
+// nearest integer, ties to even, and that integer is the low mantissa field:
+// rint(r) = bits(t) - bits(1.5 * 2^23).  f = r - (t - 1.5 * 2^23) = r - rint(r)
+// is exact (Sterbenz), |f| <= 0.5, and r lies in the band exactly when
+// |f| > 0.5 - 6.1e-5.
+// The clamp to +-127 never binds for finite inputs: |v| <= amax, so
+// |r| <= 127 (1 + 2^-23) < 127.5 and rint(r) <= 127 (likewise for fl(v/s)).
+// One branch per vector of eight sends a vector with any value in the band
+// to the exact path, which is kept out of line so that it costs nothing when
+// not taken.
+constexpr float kRound = 12582912.0f;  // 1.5 * 2^23
+constexpr int kRoundBits = 0x4B400000;
+constexpr float kBand = 0.5f - 6.1e-5f;
+
+__device__ __forceinline__ uint32_t pack4_s8(int a, int b, int c, int d) {
+  return __byte_perm(__byte_perm(a, b, 0x0040), __byte_perm(c, d, 0x0040), 0x5410);
+}
+
+__device__ __noinline__ uint2 quant_vec8_exact(uint4 raw, float s, float inv) {
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw);
+  int q[8];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const float2 v = __bfloat1622float2(h[j]);
+    const float vv[2] = {v.x, v.y};
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      const float r = __fmul_rn(vv[e], inv);
+      const float t = __fadd_rn(r, kRound);
+      const float f = __fsub_rn(r, __fsub_rn(t, kRound));
+      q[2 * j + e] = fabsf(f) > kBand ? __float2int_rn(__fdiv_rn(vv[e], s)) : __float_as_int(t) - kRoundBits;
+    }
+  }
+  return make_uint2(pack4_s8(q[0], q[1], q[2], q[3]), pack4_s8(q[4], q[5], q[6], q[7]));
 }
 
 // Eight bf16 values -> eight int8 (packed little-endian in a uint2).  s == 0
-// (an all-zero row) has inv == 0, so r == 0 and every q is 0.
+// (an all-zero row) has inv == 0, so r == 0 and every q is 0.  Two lanes at a
+// time in packed f32x2 arithmetic (each lane correctly rounded, as the scalar
+// operations are).
 __device__ __forceinline__ uint2 quant_vec8(const uint4& raw, float s, float inv) {
   const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw);
-  uint32_t w[2];
+  const float2 inv2 = make_float2(inv, inv);
+  const float2 rnd = make_float2(kRound, kRound), nrnd = make_float2(-kRound, -kRound);
+  int q[8];
+  bool band = false;
 #pragma unroll
-  for (int j = 0; j < 2; ++j) {
-    int a, b, c, d;
-    quant_pair(__bfloat1622float2(h[2 * j]), s, inv, a, b);
-    quant_pair(__bfloat1622float2(h[2 * j + 1]), s, inv, c, d);
-    w[j] = (static_cast<uint32_t>(a) & 0xffu) | ((static_cast<uint32_t>(b) & 0xffu) << 8) |
-           ((static_cast<uint32_t>(c) & 0xffu) << 16) | (static_cast<uint32_t>(d) << 24);
+  for (int j = 0; j < 4; ++j) {
+    const float2 r = __fmul2_rn(__bfloat1622float2(h[j]), inv2);
+    const float2 t = __fadd2_rn(r, rnd);
+    const float2 ri = __fadd2_rn(t, nrnd);
+    const float2 f = __fadd2_rn(r, make_float2(-ri.x, -ri.y));
+    band |= (fabsf(f.x) > kBand) | (fabsf(f.y) > kBand);
+    q[2 * j] = __float_as_int(t.x) - kRoundBits;
+    q[2 * j + 1] = __float_as_int(t.y) - kRoundBits;
   }
-  return make_uint2(w[0], w[1]);
+  if (band) return quant_vec8_exact(raw, s, inv);
+  return make_uint2(pack4_s8(q[0], q[1], q[2], q[3]), pack4_s8(q[4], q[5], q[6], q[7]));
 }
 
 // max |x| over eight bf16 values, compared as bf16 pairs (exact: a maximum
@@ -100,34 +123,80 @@ __device__ __forceinline__ float vec8_absmax(const uint4& raw) {
   return fmaxf(__low2float(m), __high2float(m));
 }
 
-// silu(g) = g / (1 + exp(-g)) in fp32.  The fast divide is within a couple of
-// fp32 ulps for denominators up to 2^126, but returns 0 for denominators in
-// (2^126, 2^128) (g in about [-88.7, -87.3], where the true value is a normal
-// ~1e-36); those, and an overflowed exp (denominator inf: the IEEE quotient is
-// -0, as on the CPU), take the IEEE divide.  The branch is taken only for
-// such extreme inputs, so it costs nothing on real activations.
-__device__ __forceinline__ float silu_f32(float g) {
-  const float d = __fadd_rn(1.0f, expf(-g));
-  return d > 0x1p126f ? __fdiv_rn(g, d) : __fdividef(g, d);
+// silu(g) = g / (1 + exp(-g)) in fp32, y = bf16(silu(g) * u).  The fast
+// divide (g * rcp.approx(d)) is within a couple of fp32 ulps for
+// denominators up to 2^126, but
+// returns 0 for denominators in (2^126, 2^128) (g in about [-88.7, -87.3],
+// where the true value is a normal ~1e-36); a vector with such a denominator,
+// or an overflowed exp (denominator inf: the IEEE quotient is -0, as on the
+// CPU), is recomputed out of line with the IEEE divide.  The fp32 value is
+// rounded to bf16 (8 significand bits) at the end, so the fast divide's couple
+// of fp32 ulps almost never reach the bf16 result; the quantiser then works on
+// the bf16 values exactly.
+
+// 1/x with the MUFU rcp unit (the reciprocal step of the fast divide).
+__device__ __forceinline__ float rcp_approx(float x) {
+  float y;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
 }
 
-// y = bf16(silu(g) * u) for 8 lanes.  The fp32 value is rounded to bf16 (8
-// significand bits) at the end, so the fast divide's couple of fp32 ulps
-// almost never reach the bf16 result; the quantiser then works on the bf16
-// values exactly.
-__device__ __forceinline__ uint4 silu_mul_vec8(const uint4& graw, const uint4& uraw) {
+// 2^x with the MUFU ex2 unit (relative error ~2^-22 over the range used here).
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+constexpr float kNegLog2e = -1.4426950408889634f;
+
+// The same values as the fast path below, with the quotient of a lane whose
+// denominator exceeds 2^126 taken by the IEEE divide.
+__device__ __noinline__ uint4 silu_mul_vec8_exact(uint4 graw, uint4 uraw) {
   const __nv_bfloat162* g = reinterpret_cast<const __nv_bfloat162*>(&graw);
   const __nv_bfloat162* u = reinterpret_cast<const __nv_bfloat162*>(&uraw);
   uint4 out;
   __nv_bfloat162* o = reinterpret_cast<__nv_bfloat162*>(&out);
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
-    float2 gf = __bfloat1622float2(g[j]);
-    float2 uf = __bfloat1622float2(u[j]);
-    float y0 = __fmul_rn(silu_f32(gf.x), uf.x);
-    float y1 = __fmul_rn(silu_f32(gf.y), uf.y);
-    o[j] = __floats2bfloat162_rn(y0, y1);
+    const float2 gf = __bfloat1622float2(g[j]);
+    const float2 uf = __bfloat1622float2(u[j]);
+    const float gv[2] = {gf.x, gf.y}, uv[2] = {uf.x, uf.y};
+    float y[2];
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      const float d = __fadd_rn(ex2_approx(__fmul_rn(gv[e], kNegLog2e)), 1.0f);
+      const float sl = d > 0x1p126f ? __fdiv_rn(gv[e], d) : __fmul_rn(gv[e], rcp_approx(d));
+      y[e] = __fmul_rn(sl, uv[e]);
+    }
+    o[j] = __floats2bfloat162_rn(y[0], y[1]);
   }
+  return out;
+}
+
+// Fast path: exp(-g) from the identity e^x = 2^(x * log2 e), one multiply and
+// one ex2 per value; with |g| of a few units the argument's rounding adds
+// ~1e-7 relative error, and in all ~1e-6 at |g| = 20, far below the bf16
+// rounding step (2^-8) -- the fused product differs from the CPU's in the last
+// bf16 bit on a small fraction of elements, never by more.  Then the fast
+// divide, and the two multiplies as packed f32x2 arithmetic.
+__device__ __forceinline__ uint4 silu_mul_vec8(const uint4& graw, const uint4& uraw) {
+  const __nv_bfloat162* g = reinterpret_cast<const __nv_bfloat162*>(&graw);
+  const __nv_bfloat162* u = reinterpret_cast<const __nv_bfloat162*>(&uraw);
+  uint4 out;
+  __nv_bfloat162* o = reinterpret_cast<__nv_bfloat162*>(&out);
+  bool huge = false;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const float2 gf = __bfloat1622float2(g[j]);
+    const float2 uf = __bfloat1622float2(u[j]);
+    const float2 a = __fmul2_rn(gf, make_float2(kNegLog2e, kNegLog2e));
+    const float2 d = __fadd2_rn(make_float2(ex2_approx(a.x), ex2_approx(a.y)), make_float2(1.0f, 1.0f));
+    huge |= (d.x > 0x1p126f) | (d.y > 0x1p126f);
+    const float2 y = __fmul2_rn(__fmul2_rn(gf, make_float2(rcp_approx(d.x), rcp_approx(d.y))), uf);
+    o[j] = __floats2bfloat162_rn(y.x, y.y);
+  }
+  if (huge) return silu_mul_vec8_exact(graw, uraw);
   return out;
 }
 
@@ -338,9 +407,15 @@ __global__ void __launch_bounds__(kStagedMaxThreads) rows_staged_kernel(const __
   for (int64_t i = 0; i < nrows; ++i) {
     const int st = static_cast<int>(i % depth);
     const uint32_t parity = static_cast<uint32_t>((i / depth) & 1);
-    const bool ok = w8a8::dev::mbar_wait(w8a8::dev::smem_u32(&full[st]), parity, &abort_flag, err,
-                                         w8a8::kErrGemmWait, timeout_ns);
+    // One thread waits for the stage (the others idle at the barrier instead
+    // of spinning through issue slots), then every thread tests the completed
+    // phase once, which gives it the acquire of the bulk copy's bytes.
+    bool ok = true;
+    if (threadIdx.x == 0)
+      ok = w8a8::dev::mbar_wait(w8a8::dev::smem_u32(&full[st]), parity, &abort_flag, err, w8a8::kErrGemmWait,
+                                timeout_ns);
     if (__syncthreads_or(!ok)) break;
+    (void)w8a8::dev::mbar_test(w8a8::dev::smem_u32(&full[st]), parity);
     const uint4* row = rows_smem + st * stage_vecs;
     uint4 buf[VPT];
     float amax = 0.0f;
