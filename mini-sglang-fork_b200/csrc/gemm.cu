@@ -122,8 +122,7 @@ int dispatch_variant(const GemmPlan& p, const CUtensorMap& tw, const CUtensorMap
     case 4: return launch_variant<32, 9, true, FUSED>(p, tw, tn, args, cv, stream);
     case 5: return launch_variant<64, 8, true, FUSED>(p, tw, tn, args, cv, stream);
     case 6: return launch_variant<128, 6, true, FUSED>(p, tw, tn, args, cv, stream);
-    // the plain pair kernel spends the fused-only staging bytes on a 7th stage
-    case 7: return launch_pair_variant<FUSED ? 6 : 7, FUSED>(p, tw, tn, args, cv, stream);
+    case 7: return launch_pair_variant<6, FUSED>(p, tw, tn, args, cv, stream);
     default: return fail(W8A8_ERR_INVALID_ARG, "gemm: unknown variant %d", p.variant);
   }
 }
@@ -204,6 +203,7 @@ int run_gemm(const int8_t* A, const int8_t* B, const float* sa, const float* sb,
   args.kblocks = p.kblocks;
   args.units = p.units;
   args.wide_fast = p.wide_fast;
+  args.vec_scales = ((reinterpret_cast<uintptr_t>(sb) & 15u) == 0 && (reinterpret_cast<uintptr_t>(bias) & 15u) == 0) ? 1 : 0;
 
   if (comm) {
     CommView cv = *comm;

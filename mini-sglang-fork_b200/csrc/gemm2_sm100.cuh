@@ -42,8 +42,11 @@ struct Gemm2Traits {
   static constexpr int kBarrierBytes = 256;
   static constexpr int kStagingBytes = 4 * 2048;
   static constexpr int kTileOutBytes = 128 * kBN * 2;
-  static constexpr int kSmemBytesPlain = 1024 + STAGES * kStageBytes + kBarrierBytes;
-  static constexpr int kSmemBytes = kSmemBytesPlain + kStagingBytes + kSignalBytes;
+  // the staging buffer serves both modes (the epilogue's row-contiguous
+  // stores); the hand-over state only the fused one
+  static constexpr int kScaleBytes = 2 * 2 * kBN * 4;  // double-buffered scales and bias of the tile (fp32)
+  static constexpr int kSmemBytesPlain = 1024 + STAGES * kStageBytes + kBarrierBytes + kStagingBytes + kScaleBytes;
+  static constexpr int kSmemBytes = kSmemBytesPlain + kSignalBytes;
   static constexpr int smem_bytes(bool fused) { return fused ? kSmemBytes : kSmemBytesPlain; }
   static constexpr uint32_t kIdesc = dev::idesc_i8(256, 256);
   // (the launch checks the footprint of the mode it launches: a 7-stage ring
@@ -86,7 +89,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(gemm_block_threads<F
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   volatile uint32_t* epoch_slot = reinterpret_cast<volatile uint32_t*>(abort_flag + 2);
   uint8_t* staging = reinterpret_cast<uint8_t*>(bars) + T::kBarrierBytes;
-  FusedState* sigq = reinterpret_cast<FusedState*>(staging + T::kStagingBytes);
+  float* scale_stage = reinterpret_cast<float*>(staging + T::kStagingBytes);  // [2][256] sb, then [2][256] bias
+  FusedState* sigq = reinterpret_cast<FusedState*>(staging + T::kStagingBytes + T::kScaleBytes);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -228,14 +232,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(gemm_block_threads<F
                            static_cast<size_t>(cv.rank) * cv.slot_bytes;
     uint4* stg = reinterpret_cast<uint4*>(staging + (warp & 3) * 2048);
     int cur_m0 = 0, cur_hm = 1, cur_n0 = 0, cur_tile = 0;
-    auto emit16 = [&](int m, int n, const uint4& val) {
-      if constexpr (!FUSED) {
-        *reinterpret_cast<uint4*>(args.C + static_cast<size_t>(m) * args.ldc + n) = val;
-      } else {
-        stg[lane * 4 + ((n - cur_n0) & 31) / 8] = val;
-      }
-    };
-    auto emit2 = [&](int, int, __nv_bfloat16) {};  // normal orientation only
+    auto emit16 = [&](int, int n, const uint4& val) { stg[stage_slot(lane, (n & 31) >> 3)] = val; };
     auto push_chunk = [&](int c) {
       if constexpr (FUSED) {
         __syncwarp();
@@ -246,7 +243,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(gemm_block_threads<F
           const int k = lane + 32 * j;
           const int r = (warp & 3) * 32 + (k >> 2);
           if (r >= cur_hm) continue;
-          const uint4 val = stg[k];
+          const uint4 val = stg[stage_slot(k >> 2, k & 3)];
           const size_t off = blk + static_cast<size_t>(k) * 16;
           if (cv.two_shot) {
             const int owner = min(row_owner(cur_m0 + r, cur_m0, cur_hm, cv.world), cv.world - 1);
@@ -265,6 +262,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(gemm_block_threads<F
     int acc = 0;
     uint32_t acc_phase = 0;
     uint32_t sig_n = 0;
+    uint32_t blk = 0;
     bool aborted = false;
     for (int p = cluster; p < num_pairs; p += nclusters) {
       int pw, tn;
@@ -279,6 +277,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(gemm_block_threads<F
           cur_tile = tile;
         }
       }
+      const int row = tw * 128 + row_in_tile;
+      // the tile's scales into shared memory (buffer blk & 1) before waiting;
+      // the barrier below publishes them (see the single-CTA kernel)
+      float* sbs = scale_stage + (blk & 1u) * 256;
+      float* bss = scale_stage + 512 + (blk & 1u) * 256;
+      const float sam = stage_tile_scales(args, tn * 256, 256, et, real, row, sbs, bss);
+      ++blk;
       const bool ok = dev::mbar_wait(dev::smem_u32(acc_full + acc), acc_phase, abort_flag, args.err, kErrGemmWait,
                                      tmo);
       if (dev::named_bar_or(1, 128, !ok)) {
@@ -287,12 +292,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(gemm_block_threads<F
       }
       dev::tc_fence_after();
       const uint32_t t_acc = tmem_base + lane_base + static_cast<uint32_t>(acc * T::kAccCols);
-      const int row = tw * 128 + row_in_tile;
+      uint32_t vn[32];
+      dev::tmem_ld32(t_acc, vn);  // chunk c + 1 loads while chunk c is processed
 #pragma unroll 1
       for (int c = 0; c < 8; ++c) {
         uint32_t v[32];
-        dev::tmem_ld32(t_acc + c * 32, v);
-        dev::tmem_wait_ld(v);
+        dev::tmem_wait_ld(vn);
+#pragma unroll
+        for (int q = 0; q < 32; ++q) v[q] = vn[q];
+        if (c < 7) dev::tmem_ld32(t_acc + (c + 1) * 32, vn);
         if (c == 7) {
           dev::tc_fence_before();
           const uint32_t bar = dev::smem_u32(acc_empty + acc);
@@ -303,8 +311,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(gemm_block_threads<F
           }
         }
         if (real) {
-          store_chunk<false, 32>(args, row, tn * 256 + c * 32, v, emit16, emit2);
-          push_chunk(c);
+          store_chunk_smem(args, row, tn * 256 + c * 32, sam, sbs + c * 32, bss + c * 32, v, emit16);
+          if constexpr (FUSED) {
+            push_chunk(c);
+          } else {
+            store_staged_chunk(args, stg, lane, tw * 128 + quarter * 32, tn * 256 + c * 32);
+          }
         }
       }
       if constexpr (FUSED) {

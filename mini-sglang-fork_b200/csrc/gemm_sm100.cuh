@@ -87,6 +87,7 @@ struct GemmArgs {
   long long units;            // (num_tiles - dp_tiles) * kblocks / gran
   int sk_ctas;                // CTAs sharing the stream-K part: min(G, units), >= 1
   int wide_fast;              // raster: 1 = consecutive tiles walk the 128-row side
+  int vec_scales;             // 1: sb (and bias) are 16-byte aligned, read 8 columns per load
 };
 
 // Shared memory of the fused epilogue and reduction state (FusedState, below).
@@ -108,10 +109,16 @@ struct GemmTraits {
   static constexpr int kBarrierBytes = 256;
   static constexpr int kStagingBytes = 4 * 2048;  // fused epilogue: 2 KB transpose buffer per warp
   static constexpr int kTileOutBytes = 128 * BN * 2;  // one tile's bf16 block in a receive slot
-  // The staging buffer and the hand-over state exist only in fused mode; a
-  // plain GEMM's footprint is the operand ring and the barriers.
-  static constexpr int kSmemBytesPlain = 1024 + STAGES * kStageBytes + kBarrierBytes;
-  static constexpr int kSmemBytes = kSmemBytesPlain + kStagingBytes + kSignalBytes;
+  // The hand-over state exists only in fused mode.  The staging buffer serves
+  // both modes in the normal orientation (the epilogue transposes each chunk
+  // through it so that stores are row-contiguous); weight-stationary tiles
+  // store token rows directly, so a plain swap launch has no staging.
+  // double-buffered weight scales and bias of the tile's BN columns (fp32)
+  static constexpr int kScaleBytes = SWAP ? 0 : 2 * 2 * BN * 4;
+  static constexpr int kSmemBytesPlain =
+      1024 + STAGES * kStageBytes + kBarrierBytes + (SWAP ? 0 : kStagingBytes + kScaleBytes);
+  static constexpr int kSmemBytes =
+      1024 + STAGES * kStageBytes + kBarrierBytes + kStagingBytes + kScaleBytes + kSignalBytes;
   static constexpr int smem_bytes(bool fused) { return fused ? kSmemBytes : kSmemBytesPlain; }
   static constexpr uint32_t kIdesc = dev::idesc_i8(kBM, BN);
   static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "MMA N");
@@ -192,16 +199,41 @@ __device__ __forceinline__ void store_chunk(const GemmArgs& a, int row, int col0
     for (int g = 0; g < CH / 8; ++g) {
       const int n = col0 + g * 8;
       if (n >= a.N) break;  // N % 16 == 0: granules are either fully in or out
+      // the granule's eight weight scales (and bias values): two 16-byte loads
+      // (one for the bias), the same addresses in every lane of the warp
+      float sb[8], bs[8];
+      if (a.vec_scales) {
+        const float4 s0 = __ldg(reinterpret_cast<const float4*>(a.sb + n));
+        const float4 s1 = __ldg(reinterpret_cast<const float4*>(a.sb + n + 4));
+        sb[0] = s0.x; sb[1] = s0.y; sb[2] = s0.z; sb[3] = s0.w;
+        sb[4] = s1.x; sb[5] = s1.y; sb[6] = s1.z; sb[7] = s1.w;
+        if (a.bias) {
+          const uint4 braw = __ldg(reinterpret_cast<const uint4*>(a.bias + n));
+          const __nv_bfloat162* bh = reinterpret_cast<const __nv_bfloat162*>(&braw);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float2 f = __bfloat1622float2(bh[e]);
+            bs[2 * e] = f.x;
+            bs[2 * e + 1] = f.y;
+          }
+        }
+      } else {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          sb[e] = __ldg(a.sb + n + e);
+          if (a.bias) bs[e] = __bfloat162float(a.bias[n + e]);
+        }
+      }
       uint4 pk;
       __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&pk);
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         const int c0 = g * 8 + 2 * j;
-        float y0 = dequant1(static_cast<int32_t>(v[c0]), sam, __ldg(a.sb + n + 2 * j));
-        float y1 = dequant1(static_cast<int32_t>(v[c0 + 1]), sam, __ldg(a.sb + n + 2 * j + 1));
+        float y0 = dequant1(static_cast<int32_t>(v[c0]), sam, sb[2 * j]);
+        float y1 = dequant1(static_cast<int32_t>(v[c0 + 1]), sam, sb[2 * j + 1]);
         if (a.bias) {
-          y0 = __fadd_rn(y0, __bfloat162float(a.bias[n + 2 * j]));
-          y1 = __fadd_rn(y1, __bfloat162float(a.bias[n + 2 * j + 1]));
+          y0 = __fadd_rn(y0, bs[2 * j]);
+          y1 = __fadd_rn(y1, bs[2 * j + 1]);
         }
         h[j] = __floats2bfloat162_rn(y0, y1);
       }
@@ -227,6 +259,85 @@ __device__ __forceinline__ void store_chunk(const GemmArgs& a, int row, int col0
       if (a.c_i32) a.c_i32[static_cast<int64_t>(m) * a.N + n] = static_cast<int32_t>(v[j]);
     }
   }
+}
+
+// Per-warp staging of one 32-row x 32-column bf16 chunk of the output tile
+// (2 KB): row r (the lane that computed it), 16-byte piece g (8 columns) at
+// slot r * 4 + (g ^ ((r >> 1) & 3)).  The XOR spreads both access patterns
+// over distinct banks -- the writes (one lane per row, one piece each) and the
+// reads (four lanes per row, so that a warp store covers 8 whole 64-byte row
+// segments instead of 32 scattered 16-byte pieces).
+__device__ __forceinline__ int stage_slot(int r, int g) { return r * 4 + (g ^ ((r >> 1) & 3)); }
+
+// Write a staged chunk (rows m_base.., columns n0..n0+31) to C with
+// row-contiguous 16-byte stores; rows >= M and columns >= N are skipped.
+__device__ __forceinline__ void store_staged_chunk(const GemmArgs& a, const uint4* stg, int lane, int m_base,
+                                                   int n0) {
+  __syncwarp();
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int r = j * 8 + (lane >> 2), g = lane & 3;
+    const int m = m_base + r, n = n0 + g * 8;
+    if (m < a.M && n < a.N) *reinterpret_cast<uint4*>(a.C + static_cast<size_t>(m) * a.ldc + n) = stg[stage_slot(r, g)];
+  }
+  __syncwarp();  // the next chunk may overwrite the staging buffer
+}
+
+// Normal orientation, with the tile's weight scales (and bias) staged in
+// shared memory by the epilogue before it waited for the accumulator:
+// dequantise one 32-column chunk of row m (activation scale sam) and emit it.
+// Reading the scales as shared-memory broadcasts instead of global loads keeps
+// an L2 round trip per chunk off the epilogue's critical path.
+template <class Emit16>
+__device__ __forceinline__ void store_chunk_smem(const GemmArgs& a, int m, int col0, float sam, const float* sbs,
+                                                 const float* bss, const uint32_t (&v)[32], Emit16&& emit16) {
+  if (m >= a.M) return;
+#pragma unroll
+  for (int g = 0; g < 4; ++g) {
+    const int n = col0 + g * 8;
+    if (n >= a.N) break;  // N % 16 == 0: granules are either fully in or out
+    const float4 s0 = reinterpret_cast<const float4*>(sbs)[g * 2];
+    const float4 s1 = reinterpret_cast<const float4*>(sbs)[g * 2 + 1];
+    const float sb[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+    uint4 pk;
+    __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&pk);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      float y0 = dequant1(static_cast<int32_t>(v[g * 8 + 2 * j]), sam, sb[2 * j]);
+      float y1 = dequant1(static_cast<int32_t>(v[g * 8 + 2 * j + 1]), sam, sb[2 * j + 1]);
+      if (a.bias) {
+        y0 = __fadd_rn(y0, bss[g * 8 + 2 * j]);
+        y1 = __fadd_rn(y1, bss[g * 8 + 2 * j + 1]);
+      }
+      h[j] = __floats2bfloat162_rn(y0, y1);
+    }
+    emit16(m, n, pk);
+    if (a.c_i32) {
+      int4* dst = reinterpret_cast<int4*>(a.c_i32 + static_cast<int64_t>(m) * a.N + n);
+      dst[0] = make_int4(v[g * 8 + 0], v[g * 8 + 1], v[g * 8 + 2], v[g * 8 + 3]);
+      dst[1] = make_int4(v[g * 8 + 4], v[g * 8 + 5], v[g * 8 + 6], v[g * 8 + 7]);
+    }
+  }
+}
+
+// Stage the weight scales (and bias, 0 without one) of output columns
+// [n0, n0 + cols) into sbs / bss (cols <= 2 * nthreads), thread t taking
+// columns 2t and 2t + 1; and return row m's activation scale (0 past M).
+__device__ __forceinline__ float stage_tile_scales(const GemmArgs& a, int n0, int cols, int t, bool real, int m,
+                                                   float* sbs, float* bss) {
+  if (2 * t < cols) {
+    const int n = n0 + 2 * t;
+    float2 sv = make_float2(0.0f, 0.0f), bv = make_float2(0.0f, 0.0f);
+    if (real && n < a.N) {  // N even: the pair is in or out together
+      sv = make_float2(__ldg(a.sb + n), __ldg(a.sb + n + 1));
+      if (a.bias) bv = make_float2(__bfloat162float(a.bias[n]), __bfloat162float(a.bias[n + 1]));
+    }
+    sbs[2 * t] = sv.x;
+    sbs[2 * t + 1] = sv.y;
+    bss[2 * t] = bv.x;
+    bss[2 * t + 1] = bv.y;
+  }
+  return (real && m < a.M) ? __ldg(a.sa + m) : 0.0f;
 }
 
 // Fused mode: rank of the owner of row (m - m0) of a tile of hm rows when the
@@ -601,7 +712,8 @@ __global__ void __launch_bounds__(gemm_block_threads<FUSED>(), 1)
   volatile int* last_flag = abort_flag + 1;
   volatile uint32_t* epoch_slot = reinterpret_cast<volatile uint32_t*>(last_flag + 1);
   uint8_t* staging = reinterpret_cast<uint8_t*>(bars) + T::kBarrierBytes;  // 16-byte aligned
-  FusedState* sigq = reinterpret_cast<FusedState*>(staging + T::kStagingBytes);
+  float* scale_stage = reinterpret_cast<float*>(staging + T::kStagingBytes);  // [2][BN] sb, then [2][BN] bias
+  FusedState* sigq = reinterpret_cast<FusedState*>(staging + T::kStagingBytes + T::kScaleBytes);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -790,13 +902,9 @@ __global__ void __launch_bounds__(gemm_block_threads<FUSED>(), 1)
                            static_cast<size_t>(cv.rank) * cv.slot_bytes;
     uint4* stg = reinterpret_cast<uint4*>(staging + (warp & 3) * 2048);
     int cur_m0 = 0, cur_hm = 1, cur_n0 = 0, cur_tile = 0;
-    auto emit16 = [&](int m, int n, const uint4& val) {
-      if constexpr (!FUSED) {
-        *reinterpret_cast<uint4*>(args.C + static_cast<size_t>(m) * args.ldc + n) = val;
-      } else {
-        stg[lane * 4 + ((n - cur_n0) & 31) / 8] = val;  // [row in warp][16-byte piece of the 64-byte chunk]
-      }
-    };
+    // normal orientation, both modes: [row in warp][16-byte piece] through the
+    // staging buffer (chunks start at multiples of 32 columns)
+    auto emit16 = [&](int, int n, const uint4& val) { stg[stage_slot(lane, (n & 31) >> 3)] = val; };
     auto emit2 = [&](int m, int n, __nv_bfloat16 val) {
       if constexpr (!FUSED) {
         args.C[static_cast<size_t>(m) * args.ldc + n] = val;
@@ -818,7 +926,7 @@ __global__ void __launch_bounds__(gemm_block_threads<FUSED>(), 1)
           const int k = lane + 32 * j;  // 16-byte piece k of the warp's 2 KB
           const int r = (warp & 3) * 32 + (k >> 2);
           if (r >= cur_hm) continue;    // padding rows of a bottom tile are never read: not pushed
-          const uint4 val = stg[k];
+          const uint4 val = stg[stage_slot(k >> 2, k & 3)];
           const size_t off = blk + static_cast<size_t>(k) * 16;
           if (cv.two_shot) {
             const int owner = min(row_owner(cur_m0 + r, cur_m0, cur_hm, cv.world), cv.world - 1);
@@ -831,6 +939,14 @@ __global__ void __launch_bounds__(gemm_block_threads<FUSED>(), 1)
       }
     };
     const int quarter = warp & 3;
+    // plain normal orientation: chunk c of tile (tw, tn) goes to C from the staging buffer
+    auto out_chunk = [&](int tw, int tn, int c) {
+      if constexpr (FUSED) {
+        push_chunk(c);
+      } else if constexpr (!SWAP) {
+        store_staged_chunk(args, stg, lane, tw * T::kBM + quarter * 32, tn * BN + c * T::kChunk);
+      }
+    };
     const int row_in_tile = quarter * 32 + lane;
     const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
     const int et = threadIdx.x - 64;  // 0..127 among the epilogue threads
@@ -841,6 +957,7 @@ __global__ void __launch_bounds__(gemm_block_threads<FUSED>(), 1)
     bool aborted = false;
     FragmentWalk walk(args);
     int tile, kb0, kb1;
+    uint32_t frag = 0;
     while (walk.next(tile, kb0, kb1)) {
       int tw, tn;
       tile_coords(args, tile, tw, tn);
@@ -849,6 +966,15 @@ __global__ void __launch_bounds__(gemm_block_threads<FUSED>(), 1)
         tile_rect<BN, SWAP>(args, tile, cur_m0, cur_hm, cur_n0, wn_);
         cur_tile = tile;
       }
+      const int row = tw * T::kBM + row_in_tile;
+      // Normal orientation: the tile's scales into shared memory (buffer
+      // frag & 1) before waiting; the barrier below publishes them, and no
+      // warp still reads this buffer (it belonged to fragment frag - 2).
+      float* sbs = scale_stage + (frag & 1u) * BN;
+      float* bss = scale_stage + 2 * BN + (frag & 1u) * BN;
+      float sam = 0.0f;
+      if constexpr (!SWAP) sam = stage_tile_scales(args, tn * BN, BN, et, true, row, sbs, bss);
+      ++frag;
       const bool ok = dev::mbar_wait(dev::smem_u32(acc_full + acc), acc_phase, abort_flag, args.err,
                                      kErrGemmWait, tmo);
       if (dev::named_bar_or(1, 128, !ok)) {  // uniform exit of all epilogue threads
@@ -857,21 +983,35 @@ __global__ void __launch_bounds__(gemm_block_threads<FUSED>(), 1)
       }
       dev::tc_fence_after();
       const uint32_t t_acc = tmem_base + lane_base + static_cast<uint32_t>(acc * T::kAccCols);
-      const int row = tw * T::kBM + row_in_tile;
+      // normal orientation from the staged scales, weight-stationary as before
+      auto dequant_chunk = [&](int c, const uint32_t (&v)[32]) {
+        if constexpr (!SWAP) {
+          store_chunk_smem(args, row, tn * BN + c * T::kChunk, sam, sbs + c * T::kChunk, bss + c * T::kChunk, v,
+                           emit16);
+        } else {
+          store_chunk<SWAP, T::kChunk>(args, row, tn * BN + c * T::kChunk, v, emit16, emit2);
+        }
+      };
       bool wrote_tile = true;
       if (kb0 == 0 && kb1 == args.kblocks) {
-        // whole tile in this CTA: dequantise straight from TMEM
+        // whole tile in this CTA: dequantise straight from TMEM, the next
+        // chunk's columns loading while this one is processed
+        uint32_t vn[32];
+        dev::tmem_ld<T::kChunk>(t_acc, vn);
 #pragma unroll 1
         for (int c = 0; c < T::kChunks; ++c) {
           uint32_t v[32];
-          dev::tmem_ld<T::kChunk>(t_acc + c * T::kChunk, v);
-          dev::tmem_wait_ld(v);
-          if (c == T::kChunks - 1) {
+          dev::tmem_wait_ld(vn);
+#pragma unroll
+          for (int q = 0; q < 32; ++q) v[q] = vn[q];
+          if (c + 1 < T::kChunks) {
+            dev::tmem_ld<T::kChunk>(t_acc + (c + 1) * T::kChunk, vn);
+          } else {
             dev::tc_fence_before();
             dev::mbar_arrive(dev::smem_u32(acc_empty + acc));
           }
-          store_chunk<SWAP, T::kChunk>(args, row, tn * BN + c * T::kChunk, v, emit16, emit2);
-          push_chunk(c);
+          dequant_chunk(c, v);
+          out_chunk(tw, tn, c);
         }
       } else {
         // Partial fragment: park the int32 values in this CTA's slot.  Slot
@@ -935,8 +1075,8 @@ __global__ void __launch_bounds__(gemm_block_threads<FUSED>(), 1)
               dev::tc_fence_before();
               dev::mbar_arrive(dev::smem_u32(acc_empty + acc));
             }
-            store_chunk<SWAP, T::kChunk>(args, row, tn * BN + c * T::kChunk, v, emit16, emit2);
-            push_chunk(c);
+            dequant_chunk(c, v);
+            out_chunk(tw, tn, c);
           }
           if (et == 0) args.counters[tile] = 0u;
         }
