@@ -45,8 +45,26 @@ import torch
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
-HIDDEN, HEAD_DIM, NQ, NKV, INTER = 5120, 128, 64, 8, 25600
-METRIC = "W8A8 TP-layer tokens/s (Qwen3-32B decoder-layer linears: qkv, o_proj+AR, gate_up, silu*mul+quant, down+AR)"
+# BASELINE configs 2-4; cfg3 (the headline the driver runs) is the default.
+WORKLOADS = {
+    "cfg3": {"hidden": 5120, "head_dim": 128, "nq": 64, "nkv": 8, "inter": 25600, "layers": 1, "mlp_only": False,
+             "m": 4096, "sweep": [1, 32, 128, 256],
+             "metric": "W8A8 TP-layer tokens/s (Qwen3-32B decoder-layer linears: qkv, o_proj+AR, gate_up, "
+                       "silu*mul+quant, down+AR)",
+             "desc": "cfg3 Qwen3-32B decoder-layer W8A8 linears, TP=N, headline M = prefill chunk"},
+    "cfg2": {"hidden": 4096, "head_dim": 128, "nq": 32, "nkv": 8, "inter": 12288, "layers": 1, "mlp_only": True,
+             "m": 8192, "sweep": [1, 16, 64, 256, 2048],
+             "metric": "W8A8 MLP tokens/s (Qwen3-8B GatedMLP: gate_up, silu*mul+quant, down)",
+             "desc": "cfg2 Qwen3-8B W8A8 MLP block (gate_up 4096->24576, silu*mul+quant, down 12288->4096)"},
+    "cfg4": {"hidden": 8192, "head_dim": 128, "nq": 64, "nkv": 8, "inter": 28672, "layers": 4, "mlp_only": False,
+             "m": 8192, "sweep": [256],
+             "metric": "W8A8 TP-layer tokens/s (Llama-3.1-70B, 4 consecutive decoder layers' linears with fused "
+                       "row-parallel all-reduce)",
+             "desc": "cfg4 Llama-3.1-70B 4-layer W8A8 linear stack, TP=N"},
+}
+WORKLOAD = "cfg3"
+HIDDEN, HEAD_DIM, NQ, NKV, INTER, LAYERS, MLP_ONLY = 5120, 128, 64, 8, 25600, 1, False
+METRIC = WORKLOADS["cfg3"]["metric"]
 UNIT = "tokens/s"
 L2_FLUSH_BYTES = 256 << 20
 INT8_NOMINAL_TOPS = 4500.0
@@ -66,6 +84,28 @@ PROJ = {
 PREFIX = "model.layers.0."
 
 
+def _proj_table():
+    return {
+        "q_proj": ("self_attn", NQ * HEAD_DIM, HIDDEN),
+        "k_proj": ("self_attn", NKV * HEAD_DIM, HIDDEN),
+        "v_proj": ("self_attn", NKV * HEAD_DIM, HIDDEN),
+        "o_proj": ("self_attn", HIDDEN, NQ * HEAD_DIM),
+        "gate_proj": ("mlp", INTER, HIDDEN),
+        "up_proj": ("mlp", INTER, HIDDEN),
+        "down_proj": ("mlp", HIDDEN, INTER),
+    }
+
+
+def select_workload(name: str) -> None:
+    """Rebind the module's workload shape (3 or 4)."""
+    global WORKLOAD, HIDDEN, HEAD_DIM, NQ, NKV, INTER, LAYERS, MLP_ONLY, METRIC, PROJ
+    w = WORKLOADS[name]
+    WORKLOAD = name
+    HIDDEN, HEAD_DIM, NQ, NKV, INTER = w["hidden"], w["head_dim"], w["nq"], w["nkv"], w["inter"]
+    LAYERS, MLP_ONLY, METRIC = w["layers"], w["mlp_only"], w["metric"]
+    PROJ = _proj_table()
+
+
 def _pkg():
     return importlib.import_module("mini-sglang-fork_b200")
 
@@ -79,43 +119,50 @@ def _peaks():
 
 
 def local_shapes(tp: int):
-    """Per-rank (N, K) of qkv, o_proj, gate_up, down (M/layers/linear.py:56-127)."""
+    """Per-rank (N, K) of qkv, o_proj, gate_up, down (M/layers/linear.py:56-127);
+    gate_up and down only for an MLP-only workload."""
     lq = NQ // tp
     lkv = max(1, NKV // tp)
-    return {
+    sh = {
         "qkv": ((lq + 2 * lkv) * HEAD_DIM, HIDDEN),
         "o_proj": (HIDDEN, NQ * HEAD_DIM // tp),
         "gate_up": (2 * INTER // tp, HIDDEN),
         "down": (HIDDEN, INTER // tp),
     }
+    if MLP_ONLY:
+        del sh["qkv"], sh["o_proj"]
+    return sh
 
 
 def layer_ops(tp: int):
-    """Integer ops (2*M*N*K summed) and weight bytes of the four linears per token."""
+    """Integer ops (2*M*N*K summed) and weight bytes of all the step's linears per token."""
     sh = local_shapes(tp)
-    ops_per_token = sum(2 * n * k for n, k in sh.values())
-    wbytes = sum(n * k + 4 * n for n, k in sh.values())
+    ops_per_token = LAYERS * sum(2 * n * k for n, k in sh.values())
+    wbytes = LAYERS * sum(n * k + 4 * n for n, k in sh.values())
     return ops_per_token, wbytes
 
 
 def workload_config(world: int, m: int):
     """The workload keys both arms (GPU and the CPU reference) report."""
-    return {"workload": "cfg3 Qwen3-32B decoder-layer W8A8 linears, TP=N, headline M = prefill chunk",
-            "M": m, "hidden": HIDDEN, "heads": [NQ, NKV], "head_dim": HEAD_DIM, "intermediate": INTER,
-            "parallelism": f"tp{world}"}
+    return {"workload": WORKLOADS[WORKLOAD]["desc"], "M": m, "hidden": HIDDEN, "heads": [NQ, NKV],
+            "head_dim": HEAD_DIM, "intermediate": INTER, "layers": LAYERS, "parallelism": f"tp{world}"}
 
 
-def full_weight(name: str, dev: torch.device) -> torch.Tensor:
-    """The synthetic bf16 checkpoint tensor of one projection (identical on every rank)."""
+def full_weight(name: str, dev: torch.device, layer: int = 0) -> torch.Tensor:
+    """The synthetic bf16 checkpoint tensor of one projection of one layer
+    (identical on every rank)."""
     _, n, k = PROJ[name]
-    g = torch.Generator(device=dev).manual_seed(1000 + list(PROJ).index(name))
+    g = torch.Generator(device=dev).manual_seed(1000 + 16 * layer + list(PROJ).index(name))
     return (torch.randn(n, k, device=dev, generator=g) * 0.02).bfloat16()
 
 
 def checkpoint_items(dev: torch.device):
     """(name, tensor) pairs as safetensors yields them, one projection at a time."""
-    for name, (module, _, _) in PROJ.items():
-        yield f"{PREFIX}{module}.{name}.weight", full_weight(name, dev)
+    for layer in range(LAYERS):
+        for name, (module, _, _) in PROJ.items():
+            if MLP_ONLY and module != "mlp":
+                continue
+            yield f"model.layers.{layer}.{module}.{name}.weight", full_weight(name, dev, layer)
 
 
 # --------------------------------------------------------------------------- clocks
@@ -188,36 +235,53 @@ class ClockSampler:
 
 # --------------------------------------------------------------------------- the layer stack
 class Stack:
-    """The four W8A8 layers of one decoder layer on this rank, built through
-    the package's public layer classes and loaded from the synthetic
-    checkpoint with the package's loader (quantise unsharded, then shard)."""
+    """The workload's W8A8 linears on this rank (LAYERS decoder layers of
+    qkv, o_proj, gate_up, down -- or gate_up, down only), built through the
+    package's public layer classes and loaded from the synthetic checkpoint
+    with the package's loader (quantise unsharded, then shard)."""
 
     def __init__(self, pkg, tp: int, rank: int, dev: torch.device):
         L = pkg.layers
         self.pkg = pkg
-        self.qkv = L.LinearQKVMerged(HIDDEN, HEAD_DIM, NQ, NKV, has_bias=False)
-        self.o_proj = L.LinearOProj(NQ * HEAD_DIM, HIDDEN, has_bias=False)
-        self.gate_up = L.LinearColParallelMerged(HIDDEN, [INTER, INTER], has_bias=False)
-        self.down = L.LinearRowParallel(INTER, HIDDEN, has_bias=False)
+        self.layers = []
+        for _ in range(LAYERS):
+            lay = {}
+            if not MLP_ONLY:
+                lay["qkv"] = L.LinearQKVMerged(HIDDEN, HEAD_DIM, NQ, NKV, has_bias=False)
+                lay["o_proj"] = L.LinearOProj(NQ * HEAD_DIM, HIDDEN, has_bias=False)
+            lay["gate_up"] = L.LinearColParallelMerged(HIDDEN, [INTER, INTER], has_bias=False)
+            lay["down"] = L.LinearRowParallel(INTER, HIDDEN, has_bias=False)
+            self.layers.append(lay)
         self.q_cols = (NQ // tp) * HEAD_DIM
         state = pkg.load_w8a8_state_dict(checkpoint_items(dev), rank, tp, NKV, device=dev)
-        for layer, key in ((self.qkv, "self_attn.qkv_proj"), (self.o_proj, "self_attn.o_proj"),
-                           (self.gate_up, "mlp.gate_up_proj"), (self.down, "mlp.down_proj")):
-            layer.load_state_dict({"weight": state.pop(f"{PREFIX}{key}.weight"),
-                                   "weight_scale": state.pop(f"{PREFIX}{key}.weight_scale")})
+        keys = {"qkv": "self_attn.qkv_proj", "o_proj": "self_attn.o_proj", "gate_up": "mlp.gate_up_proj",
+                "down": "mlp.down_proj"}
+        for i, lay in enumerate(self.layers):
+            for name, layer in lay.items():
+                key = f"model.layers.{i}.{keys[name]}"
+                layer.load_state_dict({"weight": state.pop(f"{key}.weight"),
+                                       "weight_scale": state.pop(f"{key}.weight_scale")})
         assert not state, sorted(state)
+        first = self.layers[0]
+        self.qkv, self.o_proj = first.get("qkv"), first.get("o_proj")
+        self.gate_up, self.down = first["gate_up"], first["down"]
         torch.cuda.synchronize()
 
+    def _layer(self, lay, x: torch.Tensor) -> torch.Tensor:
+        if not MLP_ONLY:
+            qkv = lay["qkv"].forward(x)
+            x = lay["o_proj"].forward(qkv[:, : self.q_cols])
+        gu = lay["gate_up"].forward(x)
+        return lay["down"].forward(self.pkg.ops.silu_and_mul_quant(gu))
+
     def forward(self, x: torch.Tensor) -> torch.Tensor:
-        qkv = self.qkv.forward(x)
-        attn = qkv[:, : self.q_cols]
-        h = self.o_proj.forward(attn)
-        gu = self.gate_up.forward(h)
-        y = self.pkg.ops.silu_and_mul_quant(gu)
-        return self.down.forward(y)
+        for lay in self.layers:
+            x = self._layer(lay, x)
+        return x
 
     def forward_traced(self, x: torch.Tensor):
-        """forward, keeping every layer's input and output (parity check)."""
+        """The first layer's forward, keeping every linear's input and output
+        (parity check; decoder layers only)."""
         t = {"x": x}
         t["qkv"] = self.qkv.forward(x)
         t["attn"] = t["qkv"][:, : self.q_cols]
@@ -232,14 +296,21 @@ class Stack:
         """The same stack with the row-parallel reduce through ``nccl`` (the
         reference's path: GEMM, then an all-reduce call) instead of fused."""
         ops = self.pkg.ops
-        qkv = self.qkv.forward(x)
-        qa = self.o_proj._quantize_input(qkv[:, : self.q_cols])
-        h = nccl.all_reduce(ops.w8a8_gemm(qa.q, self.o_proj.weight, qa.s, self.o_proj.weight_scale))
-        gu = self.gate_up.forward(h)
-        y = ops.silu_and_mul_quant(gu)
-        return nccl.all_reduce(ops.w8a8_gemm(y.q, self.down.weight, y.s, self.down.weight_scale))
+        for lay in self.layers:
+            if not MLP_ONLY:
+                qkv = lay["qkv"].forward(x)
+                qa = lay["o_proj"]._quantize_input(qkv[:, : self.q_cols])
+                x = nccl.all_reduce(ops.w8a8_gemm(qa.q, lay["o_proj"].weight, qa.s, lay["o_proj"].weight_scale))
+            gu = lay["gate_up"].forward(x)
+            y = ops.silu_and_mul_quant(gu)
+            x = nccl.all_reduce(ops.w8a8_gemm(y.q, lay["down"].weight, y.s, lay["down"].weight_scale))
+        return x
 
-    launches_per_step = 8  # 3 quantisers + 1 fused silu*mul+quant + 4 GEMMs (reduce fused or NCCL)
+    @staticmethod
+    def launches_per_step():
+        """Our kernels per step: per layer a quantiser and a GEMM per linear
+        (the SiLU*mul quantiser in place of down's), reduce fused or NCCL's."""
+        return LAYERS * (4 if MLP_ONLY else 8)
 
 
 # --------------------------------------------------------------------------- the reference's NCCL path
@@ -536,13 +607,14 @@ def oracle_parity(traces, tp: int, dev: torch.device):
 
 
 # --------------------------------------------------------------------------- CPU baselines
-def _cpu_rank(rank, world, m, threads, init_file, q, c0_budget_s):
+def _cpu_rank(rank, world, m, threads, init_file, q, c0_budget_s, workload="cfg3"):
     """One CPU TP rank: this rank's shard of the four W8A8 linears through the
     oracle (torch._int_mm on CPU) with the row-parallel partials summed over
     gloo ranks by ``all_reduce`` (TorchDistributedImpl, M/distributed/impl.py:24-32);
     then the reference's own bf16 arithmetic (F.linear, M/layers/linear.py:31-32)
     of the same shard on a bounded token sample."""
     try:
+        select_workload(workload)
         torch.set_num_threads(threads)
         import torch.distributed as dist
         from oracle import w8a8_oracle as O
@@ -563,11 +635,15 @@ def _cpu_rank(rank, world, m, threads, init_file, q, c0_budget_s):
         qc = (NQ // world) * HEAD_DIM
 
         def step_w8a8():
-            qkv = O.w8a8_linear(x, *w8["qkv"])[3]
-            h = all_reduce(O.w8a8_linear(qkv[:, :qc].contiguous(), *w8["o_proj"])[3])
-            gu = O.w8a8_linear(h, *w8["gate_up"])[3]
-            qq, ss, _ = O.silu_mul_quant(gu)
-            return all_reduce(O.dequant(O.int_gemm(qq, w8["down"][0]), ss, w8["down"][1]))
+            h = x
+            for _ in range(LAYERS):  # every layer's shard the same size; one set of weights stands in
+                if not MLP_ONLY:
+                    qkv = O.w8a8_linear(h, *w8["qkv"])[3]
+                    h = all_reduce(O.w8a8_linear(qkv[:, :qc].contiguous(), *w8["o_proj"])[3])
+                gu = O.w8a8_linear(h, *w8["gate_up"])[3]
+                qq, ss, _ = O.silu_mul_quant(gu)
+                h = all_reduce(O.dequant(O.int_gemm(qq, w8["down"][0]), ss, w8["down"][1]))
+            return h
 
         def timed(fn, n):
             ts = []
@@ -586,12 +662,16 @@ def _cpu_rank(rank, world, m, threads, init_file, q, c0_budget_s):
         F = torch.nn.functional
 
         def step_bf16(xb):
-            qkv = F.linear(xb, wb["qkv"])
-            h = all_reduce(F.linear(qkv[:, :qc], wb["o_proj"]))
-            gu = F.linear(h, wb["gate_up"])
-            i = gu.shape[1] // 2
-            y = (F.silu(gu[:, :i].float()) * gu[:, i:].float()).bfloat16()
-            return all_reduce(F.linear(y, wb["down"]))
+            h = xb
+            for _ in range(LAYERS):
+                if not MLP_ONLY:
+                    qkv = F.linear(h, wb["qkv"])
+                    h = all_reduce(F.linear(qkv[:, :qc], wb["o_proj"]))
+                gu = F.linear(h, wb["gate_up"])
+                i = gu.shape[1] // 2
+                y = (F.silu(gu[:, :i].float()) * gu[:, i:].float()).bfloat16()
+                h = all_reduce(F.linear(y, wb["down"]))
+            return h
 
         m0 = 16
         t1 = timed(lambda: step_bf16(x[:m0]), 1)
@@ -605,6 +685,12 @@ def _cpu_rank(rank, world, m, threads, init_file, q, c0_budget_s):
         q.put((rank, t8, tb, mc0))
     except BaseException as e:  # noqa: BLE001 - reported to the parent
         q.put((rank, None, repr(e), 0))
+
+
+def cpu_tokens(m: int) -> int:
+    """Tokens the CPU baseline times: exactly M for the headline workload; a
+    bounded sample for the larger ones (cfg2 / cfg4 would take minutes)."""
+    return m if WORKLOAD == "cfg3" else min(m, 512)
 
 
 def host_cores() -> int:
@@ -634,7 +720,7 @@ def cpu_tp_baseline(world: int, m: int, threads_total: int, c0_budget_s: float =
     os.environ["CUDA_VISIBLE_DEVICES"] = ""  # the CPU ranks never touch a GPU
     os.environ["OMP_NUM_THREADS"] = str(threads)
     try:
-        procs = [ctx.Process(target=_cpu_rank, args=(r, world, m, threads, init_file, q, c0_budget_s))
+        procs = [ctx.Process(target=_cpu_rank, args=(r, world, m, threads, init_file, q, c0_budget_s, WORKLOAD))
                  for r in range(world)]
         for p in procs:
             p.start()
@@ -666,7 +752,7 @@ def cpu_tp_baseline(world: int, m: int, threads_total: int, c0_budget_s: float =
     mc0 = res[0][2]
     return {
         "value": round(m / t8, 1), "unit": UNIT, "cores": threads * world, "kind": "port",
-        "sample": (f"M={m} tokens through the 4 W8A8 linears + SiLU*mul quant at TP={world}: {world} gloo CPU "
+        "sample": (f"M={m} tokens through {WORKLOAD}'s W8A8 linears + SiLU*mul quant at TP={world}: {world} gloo CPU "
                    f"rank(s) x {threads} threads, row-parallel partials summed by all_reduce; oracle "
                    f"(torch._int_mm on CPU); median of 3 after 1 warm-up"),
         "c0_reference_bf16": {"value": round(mc0 / tb, 1), "unit": UNIT,
@@ -747,35 +833,42 @@ def run_ours(args, rank, world, dev):
         t, _, _ = time_graph(fn, bsteps, args.warmup, flush_buf, stream)
         return round(max_over_ranks(t, world, dev) / bsteps * 1e3, 2)
 
+    # the first layer's ops, each in its own graph (an MLP-only workload has
+    # no qkv / o_proj: its gate_up reads the step input)
     qx = ops.quant_per_token(x)
-    qkv = stack.qkv.forward(x)
-    attn = qkv[:, : stack.q_cols]
-    qattn = ops.quant_per_token(attn)
-    h = stack.o_proj.forward(attn)
-    qh = ops.quant_per_token(h)
+    o_p, d_p = stack.o_proj, stack.down
+    breakdown = {"quant_x": op_us(lambda: ops.quant_per_token(x))}
+    if not MLP_ONLY:
+        qkv = stack.qkv.forward(x)
+        attn = qkv[:, : stack.q_cols]
+        qattn = ops.quant_per_token(attn)
+        h = o_p.forward(attn)
+        qh = ops.quant_per_token(h)
+        breakdown["qkv_gemm"] = op_us(lambda: ops.w8a8_gemm(qx[0], stack.qkv.weight, qx[1], stack.qkv.weight_scale))
+        breakdown["quant_attn"] = op_us(lambda: ops.quant_per_token(attn))
+        breakdown["o_proj"] = op_us(lambda: o_p.forward(ops.QuantizedActivation(*qattn)))
+        breakdown["quant_h"] = op_us(lambda: ops.quant_per_token(h))
+    else:
+        h, qh = x, qx
     gu = stack.gate_up.forward(h)
     qy = ops.silu_and_mul_quant(gu)
-    o_p, d_p = stack.o_proj, stack.down
-    breakdown = {
-        "quant_x": op_us(lambda: ops.quant_per_token(x)),
-        "qkv_gemm": op_us(lambda: ops.w8a8_gemm(qx[0], stack.qkv.weight, qx[1], stack.qkv.weight_scale)),
-        "quant_attn": op_us(lambda: ops.quant_per_token(attn)),
-        "o_proj": op_us(lambda: o_p.forward(ops.QuantizedActivation(*qattn))),
-        "quant_h": op_us(lambda: ops.quant_per_token(h)),
-        "gate_up_gemm": op_us(lambda: ops.w8a8_gemm(qh[0], stack.gate_up.weight, qh[1], stack.gate_up.weight_scale)),
-        "silu_mul_quant": op_us(lambda: ops.silu_and_mul_quant(gu)),
-        "down": op_us(lambda: d_p.forward(qy)),
-    }
+    breakdown["gate_up_gemm"] = op_us(lambda: ops.w8a8_gemm(qh[0], stack.gate_up.weight, qh[1],
+                                                            stack.gate_up.weight_scale))
+    breakdown["silu_mul_quant"] = op_us(lambda: ops.silu_and_mul_quant(gu))
+    breakdown["down"] = op_us(lambda: d_p.forward(qy))
+    ops_keys = list(breakdown)
     if world > 1:
-        breakdown["o_proj_gemm_alone"] = op_us(lambda: ops.w8a8_gemm(qattn[0], o_p.weight, qattn[1], o_p.weight_scale))
+        if not MLP_ONLY:
+            breakdown["o_proj_gemm_alone"] = op_us(lambda: ops.w8a8_gemm(qattn[0], o_p.weight, qattn[1],
+                                                                         o_p.weight_scale))
+            breakdown["o_proj_reduce_exposed"] = round(breakdown["o_proj"] - breakdown["o_proj_gemm_alone"], 2)
         breakdown["down_gemm_alone"] = op_us(lambda: ops.w8a8_gemm(qy.q, d_p.weight, qy.s, d_p.weight_scale))
-        breakdown["o_proj_reduce_exposed"] = round(breakdown["o_proj"] - breakdown["o_proj_gemm_alone"], 2)
         breakdown["down_reduce_exposed"] = round(breakdown["down"] - breakdown["down_gemm_alone"], 2)
         hb = h.clone()
         breakdown["allreduce_MxH_ours"] = op_us(lambda: comm.all_reduce(hb))
-    breakdown["sum_of_ops"] = round(sum(v for k, v in breakdown.items()
-                                        if k in ("quant_x", "qkv_gemm", "quant_attn", "o_proj", "quant_h",
-                                                 "gate_up_gemm", "silu_mul_quant", "down")), 2)
+    breakdown["sum_of_ops"] = round(sum(breakdown[k] for k in ops_keys), 2)
+    if LAYERS > 1:
+        breakdown["per_layer_step"] = round(ms_per_step * 1e3 / LAYERS, 2)
     breakdown["step"] = round(ms_per_step * 1e3, 2)
 
     # ---------------------------------------------------------------- the reference's NCCL bar (N > 1)
@@ -798,7 +891,7 @@ def run_ours(args, rank, world, dev):
             nccl_line = {
                 "tokens_per_s": round(args.m * args.steps / (tms / 1e3), 1),
                 "ms_per_step": round(tms / args.steps, 4),
-                "o_proj_us": op_us(lambda: nccl.all_reduce(
+                "o_proj_us": None if MLP_ONLY else op_us(lambda: nccl.all_reduce(
                     ops.w8a8_gemm(qattn[0], o_p.weight, qattn[1], o_p.weight_scale))),
                 "down_us": op_us(lambda: nccl.all_reduce(ops.w8a8_gemm(qy.q, d_p.weight, qy.s, d_p.weight_scale))),
                 "allreduce_MxH_us": op_us(lambda: nccl.all_reduce(hb)),
@@ -821,7 +914,9 @@ def run_ours(args, rank, world, dev):
 
     # ---------------------------------------------------------------- parity (after timing)
     parity = None
-    if not args.no_parity:
+    if MLP_ONLY:
+        parity = {"skipped": "MLP-only workload; its GEMM shapes are checked by the GPU tests"}
+    elif not args.no_parity:
         traces = collect_trace(pkg, stack, x, sample_rows(args.m), world)
         if rank == 0:
             parity = oracle_parity(traces, world, dev)
@@ -894,7 +989,7 @@ def run_ours(args, rank, world, dev):
     cpu = None
     if rank == 0 and not args.no_cpu:
         try:
-            cpu = cpu_tp_baseline(world, args.m, host_cores())
+            cpu = cpu_tp_baseline(world, cpu_tokens(args.m), host_cores())
         except Exception as e:  # noqa: BLE001 - reported in the JSON line
             cpu = {"unavailable": f"{type(e).__name__}: {e}"[:300]}
     if world > 1:
@@ -939,7 +1034,7 @@ def run_ours(args, rank, world, dev):
                 "how": "eager public layer API; every step: pinned host input copied in once (rank 0) and "
                        "broadcast to the other ranks over NVLink, replicated output copied back from rank 0; "
                        "double-buffered copy streams overlap step i+1's input and step i-1's output with step i"},
-        "gpu_launches": Stack.launches_per_step * args.steps,
+        "gpu_launches": Stack.launches_per_step() * args.steps,
         "clocks": clocks,
         "cpu_baseline": cpu,
     }
@@ -950,7 +1045,7 @@ def run_ours(args, rank, world, dev):
 def run_reference(args, rank, world):
     if rank != 0:
         return None
-    cpu = cpu_tp_baseline(world, args.m, host_cores())
+    cpu = cpu_tp_baseline(world, cpu_tokens(args.m), host_cores())
     return {
         "impl": "reference",
         "metric": METRIC,
@@ -1034,8 +1129,11 @@ def main():
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--m", type=int, default=4096)
-    ap.add_argument("--sweep", type=lambda s: [int(v) for v in s.split(",") if v], default=[1, 32, 128, 256])
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="cfg3",
+                    help="BASELINE config: cfg3 (the headline), cfg2 (Qwen3-8B MLP), cfg4 (Llama-3.1-70B 4 layers)")
+    ap.add_argument("--m", type=int, default=None, help="headline tokens (default: the workload's)")
+    ap.add_argument("--sweep", type=lambda s: [int(v) for v in s.split(",") if v], default=None,
+                    help="decode sizes (default: the workload's)")
     ap.add_argument("--no-nccl", action="store_true", help="skip the NCCL symmetric-window arm at N > 1")
     ap.add_argument("--no-parity", action="store_true", help="skip the oracle check after timing")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
@@ -1044,6 +1142,11 @@ def main():
                     help="where the raw nvidia-smi samples of the timed region are written")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
+    select_workload(args.workload)
+    if args.m is None:
+        args.m = WORKLOADS[args.workload]["m"]
+    if args.sweep is None:
+        args.sweep = list(WORKLOADS[args.workload]["sweep"])
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))

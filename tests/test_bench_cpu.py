@@ -54,8 +54,37 @@ def test_reference_arm_json_line():
     assert line["e2e"]["value"] == line["value"]
     # the same workload keys as the GPU arm's config, exactly M tokens
     assert line["config"]["M"] == 64 and line["config"]["parallelism"] == "tp1"
-    assert set(line["config"]) == {"workload", "M", "hidden", "heads", "head_dim", "intermediate", "parallelism"}
+    assert set(line["config"]) == {"workload", "M", "hidden", "heads", "head_dim", "intermediate", "layers",
+                                   "parallelism"}
     assert line["cpu_baseline"]["c0_reference_bf16"]["value"] > 0
+
+
+@pytest.mark.parametrize("workload,tp,shapes", [
+    ("cfg2", 1, {"gate_up": (24576, 4096), "down": (4096, 12288)}),
+    ("cfg4", 8, {"qkv": (1280, 8192), "o_proj": (8192, 1024), "gate_up": (7168, 8192), "down": (8192, 3584)}),
+])
+def test_workload_shard_shapes(bench, workload, tp, shapes):
+    """BASELINE config 2 (Qwen3-8B MLP) and config 4 (Llama-3.1-70B, 4 layers
+    at TP=8): the per-rank (N, K) of every linear and the step's work."""
+    try:
+        bench.select_workload(workload)
+        assert bench.local_shapes(tp) == shapes
+        ops, wbytes = bench.layer_ops(tp)
+        layers = bench.WORKLOADS[workload]["layers"]
+        assert ops == layers * sum(2 * n * k for n, k in shapes.values())
+        assert wbytes == layers * sum(n * k + 4 * n for n, k in shapes.values())
+    finally:
+        bench.select_workload("cfg3")
+
+
+def test_reference_arm_other_workload():
+    env = dict(os.environ, CUDA_VISIBLE_DEVICES="")
+    res = subprocess.run([sys.executable, "bench.py", "--impl", "reference", "--workload", "cfg2", "--m", "32"],
+                         cwd=ROOT, env=env, capture_output=True, text=True, timeout=300)
+    assert res.returncode == 0, res.stderr[-2000:]
+    line = json.loads(res.stdout.strip().splitlines()[-1])
+    assert line["config"]["hidden"] == 4096 and line["config"]["M"] == 32 and line["value"] > 0
+    assert "Qwen3-8B" in line["metric"]
 
 
 def test_cpu_baseline_two_gloo_ranks(bench):
