@@ -772,7 +772,11 @@ def run_ours(args, rank, world, dev):
     comm_kind = "none (tp1)"
     if world > 1:
         comm = D.enable_peer_mem_distributed(D.get_tp_info(), None, max_bytes=args.m * HIDDEN * 2, device=dev)
-        comm_kind = "fused into the row-parallel GEMMs (NVLink peer memory)"
+        comm.set_mode(args.comm_mode)
+        comm_kind = ("fused into the row-parallel GEMMs (NVLink peer memory; two-shot through NVSwitch multicast "
+                     "at world >= 4)" if comm.nvls else
+                     f"fused into the row-parallel GEMMs (NVLink peer memory; no NVLS: {comm.nvls_error})")
+        comm_kind += f"; mode {args.comm_mode}"
     stream = torch.cuda.Stream(dev)
     flush_buf = torch.zeros(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
     stack = Stack(pkg, world, rank, dev)
@@ -1135,6 +1139,8 @@ def main():
     ap.add_argument("--sweep", type=lambda s: [int(v) for v in s.split(",") if v], default=None,
                     help="decode sizes (default: the workload's)")
     ap.add_argument("--no-nccl", action="store_true", help="skip the NCCL symmetric-window arm at N > 1")
+    ap.add_argument("--comm-mode", type=int, default=0, choices=[0, 1, 2, 3],
+                    help="fused reduce algorithm: 0 auto, 1 one-shot, 2 two-shot peer stores, 3 two-shot NVLS")
     ap.add_argument("--no-parity", action="store_true", help="skip the oracle check after timing")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
     ap.add_argument("--pg-timeout", type=int, default=300, help="process-group timeout in seconds (N > 1)")

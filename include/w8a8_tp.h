@@ -161,9 +161,23 @@ size_t w8a8_comm_handle_bytes(void);
 int w8a8_comm_create(int rank, int world, int device, size_t max_bytes, w8a8_comm** comm,
                      void* handle_out);
 int w8a8_comm_open_peers(w8a8_comm* comm, const void* all_handles);
-/* Algorithm of w8a8_all_reduce: 0 = automatic (one-shot for world 2 or small
- * tensors, two-shot otherwise), 1 = always one-shot, 2 = always two-shot. */
+/* Algorithm: 0 = automatic (one-shot for world 2 or small tensors, two-shot
+ * otherwise; the fused GEMM's two-shot through NVLS when a multicast buffer is
+ * attached), 1 = always one-shot, 2 = always two-shot (peer stores),
+ * 3 = the fused GEMM's two-shot always through NVLS (needs the buffer). */
 int w8a8_comm_set_mode(w8a8_comm* comm, int mode);
+
+/* Attach an NVSwitch multicast (NVLS) buffer for the fused row-parallel
+ * reduce: `mc` its multicast address, `uc` this rank's unicast address of the
+ * same memory, `bytes` >= 4 x max_bytes (rounded up to 4 KiB): two halves of
+ * [partials | gathered shares].  Every rank attaches its own mapping of one
+ * multicast object (the caller allocates it, e.g. with torch's symmetric
+ * memory).  With it, each rank keeps its partial tiles local and the owner of
+ * a row share reads their sum through the switch (multimem.ld_reduce, fp32
+ * accumulation) and multicasts the result (multimem.st).  No counterpart in
+ * NCCLWrapper, whose symmetric window (M/kernel/csrc/src/pynccl.cu:74-91)
+ * lets NCCL do the same inside ncclAllReduce. */
+int w8a8_comm_attach_multicast(w8a8_comm* comm, void* mc, void* uc, size_t bytes);
 /* Bounded-wait budget of every device-side flag wait (default 10 s). */
 int w8a8_comm_set_timeout_ms(w8a8_comm* comm, int64_t timeout_ms);
 

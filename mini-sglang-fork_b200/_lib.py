@@ -65,6 +65,7 @@ SIGNATURES = {
     "w8a8_comm_create": (_c_int, [_c_int, _c_int, _c_int, _c_size, ctypes.POINTER(_c_vp), _c_vp]),
     "w8a8_comm_open_peers": (_c_int, [_c_vp, _c_vp]),
     "w8a8_comm_set_mode": (_c_int, [_c_vp, _c_int]),
+    "w8a8_comm_attach_multicast": (_c_int, [_c_vp, _c_vp, _c_vp, _c_size]),
     "w8a8_comm_set_timeout_ms": (_c_int, [_c_vp, _c_i64]),
     "w8a8_all_reduce": (_c_int, [_c_vp, _c_vp, _c_i64, _c_vp]),
     "w8a8_broadcast": (_c_int, [_c_vp, _c_vp, _c_i64, _c_int, _c_vp]),

@@ -40,7 +40,8 @@ class PeerMemCommunicator:
     """
 
     def __init__(self, rank: int, world: int, max_bytes: int, cpu_group=None,
-                 device: Optional[torch.device] = None, lib=None, timeout_ms: Optional[int] = None):
+                 device: Optional[torch.device] = None, lib=None, timeout_ms: Optional[int] = None,
+                 nvls: bool = True, device_group=None):
         self.rank = rank
         self.world = world
         self.max_bytes = int(max_bytes)
@@ -62,9 +63,47 @@ class PeerMemCommunicator:
         except BaseException:
             self.close()
             raise
+        self.nvls_error: Optional[str] = None
+        self._nv_buf = self._nv_handle = None
+        if world > 1 and nvls:
+            self._attach_multicast(device_group)
+
+    def _attach_multicast(self, group) -> None:
+        """NVSwitch multicast buffer for the fused reduce (4 x max_bytes: two
+        halves of [partials | gathered shares]), allocated and mapped by
+        torch's symmetric memory -- plumbing only; the multimem loads and
+        stores are this package's kernels.  Collective over ``group`` (the
+        default group when None).  Without multicast support the fused reduce
+        keeps its peer-store two-shot; the reason is kept in ``nvls_error``."""
+        try:
+            import torch.distributed as dist
+            import torch.distributed._symmetric_memory as symm
+
+            nbytes = 4 * ((self.max_bytes + 4095) // 4096 * 4096)
+            buf = symm.empty(nbytes, dtype=torch.uint8, device=self.device)
+            handle = symm.rendezvous(buf, group if group is not None else dist.group.WORLD)
+            mc = int(handle.multicast_ptr)
+            if not mc:
+                raise RuntimeError("no multicast mapping (NVLS unsupported here)")
+            uc = int(handle.buffer_ptrs[self.rank])
+            # the multicast address maps this allocation from its base: use it only
+            # for a handle that starts there and covers the whole buffer
+            if int(handle.offset) != 0 or uc != buf.data_ptr() or int(handle.buffer_size) < nbytes:
+                raise RuntimeError("symmetric buffer is not a whole allocation of its own")
+            _lib_check(self._lib, self._lib.w8a8_comm_attach_multicast(self._handle, mc, uc, nbytes),
+                       "comm_attach_multicast")
+            self._nv_buf, self._nv_handle = buf, handle
+        except Exception as e:  # noqa: BLE001 - reported through nvls_error
+            self.nvls_error = f"{type(e).__name__}: {e}"[:300]
+
+    @property
+    def nvls(self) -> bool:
+        """True once a multicast buffer is attached (NVLS fused reduce available)."""
+        return self._nv_buf is not None
 
     def set_mode(self, mode: int) -> None:
-        """All-reduce algorithm: 0 automatic, 1 one-shot, 2 two-shot."""
+        """Algorithm: 0 automatic, 1 one-shot, 2 two-shot (peer stores), 3 the
+        fused GEMM's two-shot through NVLS (needs the multicast buffer)."""
         _lib_check(self._lib, self._lib.w8a8_comm_set_mode(self._handle, int(mode)), "comm_set_mode")
 
     # -------------------------------------------------------------- collectives
@@ -115,6 +154,7 @@ class PeerMemCommunicator:
         if getattr(self, "_handle", None) is not None and self._handle.value:
             self._lib.w8a8_comm_destroy(self._handle)
             self._handle = ctypes.c_void_p()
+        self._nv_buf = self._nv_handle = None
 
     def __del__(self):  # pragma: no cover - best effort
         try:

@@ -52,7 +52,10 @@ struct w8a8_comm {
   char* peers[w8a8::kMaxWorld] = {nullptr};
   bool opened = false;
   long long timeout_ns = 10000000000LL;  // 10 s
-  int mode = 0;                           // 0 auto, 1 one-shot, 2 two-shot
+  int mode = 0;                           // 0 auto, 1 one-shot, 2 two-shot, 3 NVLS two-shot (fused GEMM)
+  char* nv_mc = nullptr;                  // attached multicast buffer (NVLS), or null
+  char* nv_uc = nullptr;
+  size_t nv_bytes = 0;
 };
 
 namespace w8a8 {
@@ -250,6 +253,9 @@ CommView make_view(const w8a8_comm* c, unsigned int* err) {
   v.two_shot = 0;
   v.err = err;
   v.timeout_ns = c->timeout_ns;
+  v.mc_base = c->nv_mc;
+  v.nv_local = c->nv_uc;
+  v.nvls = 0;
   return v;
 }
 
@@ -354,8 +360,25 @@ int w8a8_comm_open_peers(w8a8_comm* c, const void* all_handles) {
 
 int w8a8_comm_set_mode(w8a8_comm* c, int mode) {
   W8A8_REQUIRE(c != nullptr, W8A8_ERR_INVALID_ARG, "comm_set_mode: null comm");
-  W8A8_REQUIRE(mode >= 0 && mode <= 2, W8A8_ERR_INVALID_ARG, "comm_set_mode: mode %d not in {0, 1, 2}", mode);
+  W8A8_REQUIRE(mode >= 0 && mode <= 3, W8A8_ERR_INVALID_ARG, "comm_set_mode: mode %d not in {0, 1, 2, 3}", mode);
+  W8A8_REQUIRE(mode != 3 || c->nv_mc != nullptr, W8A8_ERR_STATE,
+               "comm_set_mode: mode 3 (NVLS) needs a multicast buffer (w8a8_comm_attach_multicast)");
   c->mode = mode;
+  return W8A8_OK;
+}
+
+int w8a8_comm_attach_multicast(w8a8_comm* c, void* mc, void* uc, size_t bytes) {
+  using namespace w8a8;
+  W8A8_REQUIRE(c != nullptr && mc != nullptr && uc != nullptr, W8A8_ERR_INVALID_ARG,
+               "comm_attach_multicast: null argument");
+  W8A8_REQUIRE(W8A8_ALIGNED16(mc) && W8A8_ALIGNED16(uc), W8A8_ERR_ALIGNMENT,
+               "comm_attach_multicast: addresses must be 16-byte aligned");
+  W8A8_REQUIRE(bytes >= 4 * c->slot_bytes, W8A8_ERR_INVALID_ARG,
+               "comm_attach_multicast: %zu bytes, need 2 halves x (partials + gather) = %zu", bytes,
+               4 * c->slot_bytes);
+  c->nv_mc = static_cast<char*>(mc);
+  c->nv_uc = static_cast<char*>(uc);
+  c->nv_bytes = bytes;
   return W8A8_OK;
 }
 
@@ -447,8 +470,14 @@ int w8a8_gemm_allreduce(w8a8_comm* c, const int8_t* A, const int8_t* B, const fl
   // output would cost more NVLink time than a second hop: two-shot for large
   // outputs at world >= 4 (tiles in the normal orientation, M > 64).
   const size_t bytes = static_cast<size_t>(M) * N * 2;
-  const bool two = c->mode == 2 || (c->mode == 0 && c->world >= 4 && M > 64 && bytes * (c->world - 1) > (4u << 20));
+  const bool big = c->world >= 4 && M > 64 && bytes * (c->world - 1) > (4u << 20);
+  const bool two = c->mode == 2 || c->mode == 3 || (c->mode == 0 && big);
   v.two_shot = (two && M > 64) ? 1 : 0;
+  // NVLS two-shot when a multicast buffer is attached: forced (mode 3), or
+  // automatic for the two-shot sizes at world >= 4, where reading the
+  // partials through the switch moves ~(1 + 1/p) x the output per rank and
+  // direction against 2 (p - 1) / p x for peer stores.
+  v.nvls = (v.two_shot && c->nv_mc != nullptr && (c->mode == 3 || (c->mode == 0 && big))) ? 1 : 0;
   return run_gemm(A, B, sa, sb, bias, C, nullptr, M, N, K, 0, 0, workspace, workspace_bytes,
                   static_cast<cudaStream_t>(stream), c->timeout_ns, &v);
 }

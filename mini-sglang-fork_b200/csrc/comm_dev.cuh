@@ -40,6 +40,14 @@ struct CommView {
   int two_shot;                   // fused GEMM reduce: 1 = two-shot, 0 = one-shot
   unsigned int* err;              // device error word
   long long timeout_ns;
+  // NVLS (NVSwitch multicast) two-shot: a buffer of 2 halves x [partials P |
+  // gather G] (slot_bytes each), bound to a multicast object on every rank.
+  // nvls = 1: partial tiles stay in this rank's P; the row share's owner reads
+  // the sum over all ranks with multimem.ld_reduce and multimem.st's it into
+  // every rank's G.
+  char* mc_base;                  // the buffer's multicast address (same on every rank's mapping)
+  char* nv_local;                 // this rank's unicast address of the same buffer
+  int nvls;
 };
 
 namespace dev {
@@ -69,6 +77,37 @@ __device__ __forceinline__ char* gather_slot(const CommView& v, int at_rank, uin
   return half_ptr(v, at_rank, epoch) + static_cast<size_t>(v.world) * v.slot_bytes;
 }
 
+// NVLS buffer regions of call `epoch` (half epoch & 1): P (partials) and G
+// (gathered shares), at a unicast or multicast base.
+__device__ __forceinline__ char* nv_partials(const CommView& v, char* base, uint32_t epoch) {
+  return base + static_cast<size_t>(epoch & 1u) * 2 * v.slot_bytes;
+}
+__device__ __forceinline__ char* nv_gather(const CommView& v, char* base, uint32_t epoch) {
+  return base + static_cast<size_t>(epoch & 1u) * 2 * v.slot_bytes + v.slot_bytes;
+}
+
+// Orders this thread's accesses through one virtual alias of a location
+// (unicast or multicast) with its accesses through the other.
+__device__ __forceinline__ void fence_proxy_alias() { asm volatile("fence.proxy.alias;" ::: "memory"); }
+
+// Sum over every rank of 8 bf16 at multicast address `mc`, reduced in the
+// switch with fp32 accumulation, rounded once to bf16.
+__device__ __forceinline__ uint4 mm_ld_reduce_bf16x8(const void* mc) {
+  uint4 r;
+  asm volatile("multimem.ld_reduce.relaxed.sys.global.add.acc::f32.v4.bf16x2 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(mc)
+               : "memory");
+  return r;
+}
+
+// Store 8 bf16 to the multicast address `mc`: every rank's copy receives them.
+__device__ __forceinline__ void mm_st_bf16x8(void* mc, const uint4& v) {
+  asm volatile("multimem.st.relaxed.sys.global.v4.bf16x2 [%0], {%1, %2, %3, %4};" ::"l"(mc), "r"(v.x), "r"(v.y),
+               "r"(v.z), "r"(v.w)
+               : "memory");
+}
+
 __device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
   asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
@@ -91,6 +130,7 @@ __device__ __forceinline__ uint32_t ld_relaxed_gpu(const uint32_t* p) {
 // (cumulatively) visible before the flag.
 __device__ __forceinline__ void signal_peers(const CommView& v, int phase, int slot, uint32_t epoch, int t) {
   if (t < v.world) {
+    if (v.nvls) fence_proxy_alias();  // the group's multimem stores precede the flag
     __threadfence_system();
     st_release_sys(flag_ptr(v.base[t], phase, slot, v.rank), epoch);
   }

@@ -207,7 +207,7 @@ int run_gemm(const int8_t* A, const int8_t* B, const float* sa, const float* sb,
 
   if (comm) {
     CommView cv = *comm;
-    if (p.swap) cv.two_shot = 0;  // weight-stationary tiles push every partial to every rank
+    if (p.swap) cv.two_shot = cv.nvls = 0;  // weight-stationary tiles push every partial to every rank
     return dispatch_variant<true>(p, tw, tn, args, cv, stream);
   }
   CommView none;

@@ -245,13 +245,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(gemm_block_threads<F
           if (r >= cur_hm) continue;
           const uint4 val = stg[stage_slot(k >> 2, k & 3)];
           const size_t off = blk + static_cast<size_t>(k) * 16;
-          if (cv.two_shot) {
+          if (cv.nvls) {
+            *reinterpret_cast<uint4*>(dev::nv_partials(cv, cv.nv_local, epoch) + off) = val;
+          } else if (cv.two_shot) {
             const int owner = min(row_owner(cur_m0 + r, cur_m0, cur_hm, cv.world), cv.world - 1);
             *reinterpret_cast<uint4*>(cv.base[owner] + my_slot + off) = val;
           } else {
             for (int d = 0; d < cv.world; ++d) *reinterpret_cast<uint4*>(cv.base[d] + my_slot + off) = val;
           }
         }
+        if (cv.nvls) dev::fence_proxy_alias();  // before the tile's ready flag (read via multicast)
         __syncwarp();
       }
     };

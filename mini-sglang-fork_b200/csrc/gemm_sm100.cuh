@@ -450,12 +450,8 @@ __device__ __forceinline__ bool signal_pump(FusedState* q, const CommView& cv, u
         asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(f), "r"(epoch) : "memory");
       }
     }
-    uint32_t old;
-    asm volatile("atom.release.cta.shared::cta.max.u32 %0, [%1], %2;"
-                 : "=r"(old)
-                 : "r"(dev::smem_u32(&q->taken)), "r"(n)
+    asm volatile("red.release.cta.shared::cta.max.u32 [%0], %1;" ::"r"(dev::smem_u32(&q->taken)), "r"(n)
                  : "memory");
-    (void)old;  // only the update matters
   }
   return closed != 0;
 }
@@ -647,6 +643,38 @@ __device__ bool fused_reduce_group(const GemmArgs& a, const CommView& cv, uint32
     if (!cv.two_shot) {
       reduce_block_any_world<BN, SWAP>(a, cv, epoch, t, m0, n0, NV, [](int v) { return v; }, g.tid, g.nthreads,
                                        false);
+    } else if (cv.nvls) {
+      // This rank's row share of tile t, summed over every rank's partial in
+      // the switch (multimem.ld_reduce), written to C and multicast into every
+      // rank's gather region; four reductions in flight per thread.
+      const int r0 = (hm * cv.rank) / cv.world, r1 = (hm * (cv.rank + 1)) / cv.world;
+      const int per_chunk = (r1 - r0) * 4;
+      const int nv = per_chunk * (BN / 32);
+      const char* mc_p = dev::nv_partials(cv, cv.mc_base, epoch) + static_cast<size_t>(t) * TILE;
+      char* mc_g = dev::nv_gather(cv, cv.mc_base, epoch) + static_cast<size_t>(t) * TILE;
+      dev::fence_proxy_alias();  // the peers' partials were written through their unicast mappings
+      for (int base = g.tid; base < nv; base += 4 * g.nthreads) {
+        uint4 sum[4];
+        int vv[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int i = base + j * g.nthreads;
+          vv[j] = (i / per_chunk) * 512 + r0 * 4 + (i % per_chunk);
+          if (i < nv) sum[j] = dev::mm_ld_reduce_bf16x8(mc_p + static_cast<size_t>(vv[j]) * 16);
+        }
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          if (base + j * g.nthreads >= nv) continue;
+          int r, col;
+          block_vec_rc<BN, SWAP>(vv[j], r, col);
+          const int m = m0 + r, n = n0 + col;
+          if (m < a.M && n < a.N) *reinterpret_cast<uint4*>(a.C + static_cast<size_t>(m) * a.ldc + n) = sum[j];
+          dev::mm_st_bf16x8(mc_g + static_cast<size_t>(vv[j]) * 16, sum[j]);
+        }
+      }
+      dev::fence_proxy_alias();  // this thread's multicast stores before the group's gathered flag
+      dev::named_bar_sync(g.bar, g.nthreads);
+      dev::signal_peers(cv, 1, t, epoch, g.tid);
     } else {
       // rows [r0, r1) of every chunk: (r1 - r0) * 4 vectors per chunk
       const int r0 = (hm * cv.rank) / cv.world, r1 = (hm * (cv.rank + 1)) / cv.world;
@@ -666,7 +694,9 @@ __device__ bool fused_reduce_group(const GemmArgs& a, const CommView& cv, uint32
     if (!group_wait(cv, 1, t, epoch, g, q, abort_flag)) return false;
     int m0, hm, n0, wn;
     tile_rect<BN, SWAP>(a, t, m0, hm, n0, wn);
-    const char* from = dev::gather_slot(cv, cv.rank, epoch) + static_cast<size_t>(t) * TILE;
+    const char* from = (cv.nvls ? dev::nv_gather(cv, cv.nv_local, epoch) : dev::gather_slot(cv, cv.rank, epoch)) +
+                       static_cast<size_t>(t) * TILE;
+    if (cv.nvls) dev::fence_proxy_alias();  // the shares arrived through the multicast mapping
     // every vector outside this rank's own row share
     const int r0 = (hm * cv.rank) / cv.world, r1 = (hm * (cv.rank + 1)) / cv.world;
     for (int base = g.tid; base < NV; base += g.nthreads * 8) {
@@ -928,13 +958,17 @@ __global__ void __launch_bounds__(gemm_block_threads<FUSED>(), 1)
           if (r >= cur_hm) continue;    // padding rows of a bottom tile are never read: not pushed
           const uint4 val = stg[stage_slot(k >> 2, k & 3)];
           const size_t off = blk + static_cast<size_t>(k) * 16;
-          if (cv.two_shot) {
+          if (cv.nvls) {
+            // NVLS: the partial stays in this rank's buffer; the owner reads it through the switch
+            *reinterpret_cast<uint4*>(dev::nv_partials(cv, cv.nv_local, epoch) + off) = val;
+          } else if (cv.two_shot) {
             const int owner = min(row_owner(cur_m0 + r, cur_m0, cur_hm, cv.world), cv.world - 1);
             *reinterpret_cast<uint4*>(cv.base[owner] + my_slot + off) = val;
           } else {
             for (int d = 0; d < cv.world; ++d) *reinterpret_cast<uint4*>(cv.base[d] + my_slot + off) = val;
           }
         }
+        if (cv.nvls) dev::fence_proxy_alias();  // before the tile's ready flag (read via multicast)
         __syncwarp();
       }
     };

@@ -199,17 +199,21 @@ _PEER_MEM_COMM: Optional["PeerMemCommunicator"] = None
 
 
 def enable_peer_mem_distributed(tp_info: DistributedInfo, tp_cpu_group, max_bytes: int,
-                                device: Optional[torch.device] = None) -> Optional["PeerMemCommunicator"]:
+                                device: Optional[torch.device] = None,
+                                device_group=None) -> Optional["PeerMemCommunicator"]:
     """Create the peer-memory communicator and register it as the all-reduce
     plugin; the W8A8 row-parallel layers then fuse their reduction into the
     GEMM.  Counterpart of ``enable_pynccl_distributed`` (M/distributed/impl.py:73-90):
-    handles are exchanged over ``tp_cpu_group`` as the NCCL unique id is."""
+    handles are exchanged over ``tp_cpu_group`` as the NCCL unique id is; the
+    NVSwitch multicast buffer (when the machine has NVLS) is set up over
+    ``device_group`` (the default group when None)."""
     global _PEER_MEM_COMM
     if tp_info.size == 1:
         return None
     from .comm import PeerMemCommunicator
 
-    comm = PeerMemCommunicator(tp_info.rank, tp_info.size, max_bytes, tp_cpu_group, device=device)
+    comm = PeerMemCommunicator(tp_info.rank, tp_info.size, max_bytes, tp_cpu_group, device=device,
+                               device_group=device_group)
     _PEER_MEM_COMM = comm
     plugin = PeerMemDistributedImpl(comm)
     DistributedCommunicator.plugins.append(plugin)

@@ -186,6 +186,46 @@ def _scn_gemm_allreduce_cfg3(pkg, O, rank, world, dev, dist):
     return True
 
 
+def _scn_gemm_allreduce_nvls(pkg, O, rank, world, dev, dist):
+    """The fused GEMM + all-reduce with the two-shot reduce through the
+    NVSwitch (mode 3: partials stay local, each row share is summed in the
+    switch by multimem.ld_reduce with fp32 accumulation and multicast back).
+    The switch's summation order is not the rank order, so the bf16 result is
+    checked within one bf16 ulp of the oracle (and the 1e-2 contract bound),
+    identical on every rank, and bit-exact on all but a sliver of elements."""
+    comm = pkg.comm.PeerMemCommunicator(rank, world, 4096 * 5120 * 2, device=dev)
+    assert comm.nvls, f"no multicast buffer: {comm.nvls_error}"
+    comm.set_mode(3)
+    cases = [(333, 4096, 256 * world, True), (1024, 5120, 512 * world, False), (2560, 5120, 128 * world, False),
+             (4096, 5120, 8192, False), (65, 2048, 128 * world, True)]
+    digests = []
+    for (m, n, kfull, bias) in cases:
+        g = torch.Generator().manual_seed(m * 11 + n)
+        x = torch.randn(m, kfull, generator=g).bfloat16()
+        w = (torch.randn(n, kfull, generator=g) * 0.02).bfloat16()
+        b = (torch.randn(n, generator=g) * 0.1).bfloat16() if bias else None
+        wq, ws = O.quant_weight_per_channel(w)
+        want = O.tp_linear("row", x, wq, ws, world, bias=b)[rank].float()
+        xs = x.chunk(world, dim=1)[rank].contiguous().to(dev)
+        wshard = O.shard_tensor(".down_proj", wq, rank, world, None).to(dev)
+        q, s = pkg.ops.quant_per_token(xs)
+        for rep in range(2):  # both halves of the buffer
+            y = comm.gemm_allreduce(q, wshard, s, ws.to(dev), None if b is None else b.to(dev))
+            torch.cuda.synchronize()
+            got = y.cpu().float()
+            diff = (got - want).abs()
+            assert torch.all(diff <= want.abs() * 2.0 ** -7 + 1e-30), (m, n, kfull, float(diff.max()))
+            torch.testing.assert_close(got, want, rtol=1e-2, atol=1e-2)
+            assert float((diff != 0).float().mean()) < 1e-3, (m, n, kfull)
+        digests.append(float(y.float().sum()))
+    everyone = [None] * world
+    dist.all_gather_object(everyone, digests)
+    assert all(d == digests for d in everyone), "ranks disagree on the reduced output"
+    assert comm.device_error() == 0
+    comm.close()
+    return True
+
+
 def _scn_broadcast(pkg, O, rank, world, dev, dist):
     """Peer-memory broadcast from every root, at sizes from one vector to
     42 MB (the bench's e2e input), twice per size (both buffer halves)."""
@@ -318,6 +358,10 @@ def test_gemm_allreduce_cfg3_shapes():
 
 def test_broadcast():
     _run("broadcast")
+
+
+def test_gemm_allreduce_nvls():
+    _run("gemm_allreduce_nvls", timeout=600)
 
 
 def test_row_parallel_layer_and_cuda_graph():

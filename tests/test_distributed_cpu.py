@@ -267,7 +267,7 @@ def _check_layers_follow_reference(pkg, ref, monkeypatch):
     created = []
 
     class FakeComm:
-        def __init__(self, rank, world, max_bytes, group, device=None):
+        def __init__(self, rank, world, max_bytes, group, device=None, device_group=None):
             created.append((rank, world))
 
         def close(self):
