@@ -2,15 +2,19 @@
 // SiLU*mul (the silu_and_mul step between gate_up and down in GatedMLP,
 // M/models/utils.py:44-50 and M/layers/activation.py:9-12 of mini-sglang).
 //
-// One CTA per row; the row is read once from HBM with 128-bit loads, reduced
-// to its absmax (warp shuffles + one shared-memory step), then quantised from
-// on-chip storage and written with 64-bit stores, so HBM traffic is exactly
-// the algorithmic 2K (or 4I) bytes in and K (+4) bytes out per row.
-//   rows of <= 1024 vectors: kept in registers (VPT vectors per thread,
-//                            <= 256 threads, many CTAs per SM);
-//   longer rows:             staged in shared memory (512 threads, up to
-//                            64 KB per CTA, >= 3 CTAs per SM), so occupancy
-//                            does not collapse on 25600-wide rows.
+// Every row is read once from HBM with 128-bit loads (or 1-D bulk copies),
+// reduced to its absmax and quantised from on-chip storage, with 64-bit int8
+// stores, so HBM traffic is exactly the algorithmic 2K (or 4I) bytes in and
+// K (+4) bytes out per row.  Paths, by shape:
+//   few rows (decode):        one row per cluster of 2..8 CTAs, the absmax
+//                             meeting in distributed shared memory;
+//   many rows <= 16384 wide   1, 2 or 4 warps per row, in registers, no
+//   (SiLU*mul: <= 8192):      CTA-wide barrier, persistent grid;
+//   many wide SiLU*mul rows:  a persistent pipeline, gate/up chunks streamed
+//                             by bulk copies into a shared-memory ring while
+//                             the product row stays in shared memory;
+//   otherwise:                one CTA per row, in registers (<= 1024 vectors)
+//                             or staged in shared memory.
 // Arithmetic convention (bit-exact with the CPU oracle):
 //   s = fp32(amax) / 127.0f (IEEE divide), q = clamp(rint_even(x / s), +-127),
 //   q = 0 for an all-zero row.
@@ -46,72 +50,89 @@ __device__ __forceinline__ float block_max(float v, float* red) {
 }
 
 // q = clamp(rint_even(fl(v / s)), -127, 127) without an IEEE divide on the
-// common path.  With Q = v/s exact, |Q| < 127.5: fl(v/s) = Q(1+d1),
-// inv = fl(1/s) = (1/s)(1+d2), r = fl(v * inv) = Q(1+d2)(1+d3), |di| <= 2^-24,
-// so |r - fl(v/s)| <= 127.5 * 3 * 2^-24 < 2.3e-5.  If rint(r) and
-// rint(fl(v/s)) differed, a half-integer would lie between them, i.e. within
-// 2.3e-5 of r; so outside a 6.1e-5 band around half-integers the cheap
-// rint(r) is exact, and inside it the quotient is taken with the IEEE divide.
+// common path.  With Q = v/s exact (|Q| < 127.5), inv = fl(1/s) = (1/s)(1+d1)
+// and p = v * inv taken UNROUNDED inside a fused multiply-add: p = Q(1+d1),
+// |p - Q| <= 127.5 * 2^-24, and |fl(Q) - Q| <= 127.5 * 2^-24, so
+// |p - fl(v/s)| <= 1.52e-5.  If rint(p) and rint(fl(v/s)) differed, a
+// half-integer would lie within 1.52e-5 of p; so outside a 6.1e-5 band
+// around half-integers rint(p) is exact, and inside it the quotient is taken
+// with the IEEE divide.
 //
-// rint(r) itself uses no conversion-unit instruction (those issue at a
-// quarter of the FP32 rate): for |r| < 2^22 the sum t = r + 1.5 * 2^23 lies in
-// [2^23, 2^24), where the float spacing is 1, so the addition rounds r to the
-// nearest integer, ties to even, and that integer is the low mantissa field:
-// rint(r) = bits(t) - bits(1.5 * 2^23).  f = r - (t - 1.5 * 2^23) = r - rint(r)
-// is exact (Sterbenz), |f| <= 0.5, and r lies in the band exactly when
-// |f| > 0.5 - 6.1e-5.
+// rint(p) itself uses no conversion-unit instruction (those issue at a
+// quarter of the FP32 rate): for |p| < 2^22 the sum p + 1.5 * 2^23 lies in
+// [2^23, 2^24), where the float spacing is 1, so t = fma(v, inv, 1.5 * 2^23)
+// rounds p to the nearest integer, ties to even, and that integer is the low
+// mantissa field of t: its low byte is the two's-complement int8 of rint(p)
+// (bits(1.5 * 2^23) has a zero low byte), which the byte permutes pick
+// directly.  -rint(p) = 1.5 * 2^23 - t exactly (Sterbenz), and
+// f = fma(v, inv, -rint(p)) = p - rint(p) with one rounding (|f| <= 0.5, error
+// <= 2^-25); p lies in the band exactly when |f| > 0.5 - 6.1e-5.
+// Three packed f32x2 operations per two values and one branch per vector of
+// eight, which sends a vector with any value in the band to the exact path,
+// kept out of line so that it costs nothing when not taken.
 // The clamp to +-127 never binds for finite inputs: |v| <= amax, so
-// |r| <= 127 (1 + 2^-23) < 127.5 and rint(r) <= 127 (likewise for fl(v/s)).
-// One branch per vector of eight sends a vector with any value in the band
-// to the exact path, which is kept out of line so that it costs nothing when
-// not taken.
+// |p| <= 127 (1 + 2^-23) < 127.5 and rint(p) <= 127 (likewise for fl(v/s)).
+// A scale below 2^-126 (a row whose absmax is below ~1.5e-36) may have an
+// infinite reciprocal: such a row takes the IEEE divide for every value.
 constexpr float kRound = 12582912.0f;  // 1.5 * 2^23
-constexpr int kRoundBits = 0x4B400000;
 constexpr float kBand = 0.5f - 6.1e-5f;
 
-__device__ __forceinline__ uint32_t pack4_s8(int a, int b, int c, int d) {
+// Row scale of the quantiser: s = fl(amax / 127) (IEEE divide), inv = fl(1/s)
+// (0 for an all-zero row, whose values are all zero and quantise to 0).
+struct RowScale {
+  float s;
+  float inv;
+  bool exact;  // s in (0, 2^-126): every value takes the IEEE divide
+};
+
+__device__ __forceinline__ RowScale row_scale(float amax) {
+  RowScale r;
+  r.s = __fdiv_rn(amax, 127.0f);
+  r.inv = r.s > 0.0f ? __frcp_rn(r.s) : 0.0f;
+  r.exact = r.s > 0.0f && r.s < 0x1p-126f;
+  return r;
+}
+
+// Low bytes of four words, packed little-endian.
+__device__ __forceinline__ uint32_t pack4_s8(uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
   return __byte_perm(__byte_perm(a, b, 0x0040), __byte_perm(c, d, 0x0040), 0x5410);
 }
 
-__device__ __noinline__ uint2 quant_vec8_exact(uint4 raw, float s, float inv) {
+// Every value through the IEEE divide (s > 0).
+__device__ __noinline__ uint2 quant_vec8_div(uint4 raw, float s) {
   const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw);
-  int q[8];
+  uint32_t q[8];
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
     const float2 v = __bfloat1622float2(h[j]);
-    const float vv[2] = {v.x, v.y};
-#pragma unroll
-    for (int e = 0; e < 2; ++e) {
-      const float r = __fmul_rn(vv[e], inv);
-      const float t = __fadd_rn(r, kRound);
-      const float f = __fsub_rn(r, __fsub_rn(t, kRound));
-      q[2 * j + e] = fabsf(f) > kBand ? __float2int_rn(__fdiv_rn(vv[e], s)) : __float_as_int(t) - kRoundBits;
-    }
+    const int a = __float2int_rn(__fdiv_rn(v.x, s)), b = __float2int_rn(__fdiv_rn(v.y, s));
+    q[2 * j] = static_cast<uint32_t>(a < -127 ? -127 : (a > 127 ? 127 : a));
+    q[2 * j + 1] = static_cast<uint32_t>(b < -127 ? -127 : (b > 127 ? 127 : b));
   }
   return make_uint2(pack4_s8(q[0], q[1], q[2], q[3]), pack4_s8(q[4], q[5], q[6], q[7]));
 }
 
-// Eight bf16 values -> eight int8 (packed little-endian in a uint2).  s == 0
-// (an all-zero row) has inv == 0, so r == 0 and every q is 0.  Two lanes at a
-// time in packed f32x2 arithmetic (each lane correctly rounded, as the scalar
-// operations are).
-__device__ __forceinline__ uint2 quant_vec8(const uint4& raw, float s, float inv) {
+// Eight bf16 values -> eight int8 (packed little-endian in a uint2).  Two
+// lanes at a time in packed f32x2 arithmetic (each lane correctly rounded, as
+// the scalar operations are).
+__device__ __forceinline__ uint2 quant_vec8(const uint4& raw, const RowScale& rs) {
+  if (rs.exact) return quant_vec8_div(raw, rs.s);
   const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw);
-  const float2 inv2 = make_float2(inv, inv);
-  const float2 rnd = make_float2(kRound, kRound), nrnd = make_float2(-kRound, -kRound);
-  int q[8];
+  const float2 inv2 = make_float2(rs.inv, rs.inv);
+  const float2 rnd = make_float2(kRound, kRound), m1 = make_float2(-1.0f, -1.0f);
+  uint32_t q[8];
   bool band = false;
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
-    const float2 r = __fmul2_rn(__bfloat1622float2(h[j]), inv2);
-    const float2 t = __fadd2_rn(r, rnd);
-    const float2 ri = __fadd2_rn(t, nrnd);
-    const float2 f = __fadd2_rn(r, make_float2(-ri.x, -ri.y));
+    const float2 v = __bfloat1622float2(h[j]);
+    const float2 t = __ffma2_rn(v, inv2, rnd);    // 1.5 * 2^23 + rint(p)
+    const float2 nr = __ffma2_rn(t, m1, rnd);     // -rint(p), exact
+    const float2 f = __ffma2_rn(v, inv2, nr);     // p - rint(p)
     band |= (fabsf(f.x) > kBand) | (fabsf(f.y) > kBand);
-    q[2 * j] = __float_as_int(t.x) - kRoundBits;
-    q[2 * j + 1] = __float_as_int(t.y) - kRoundBits;
+    q[2 * j] = __float_as_uint(t.x);
+    q[2 * j + 1] = __float_as_uint(t.y);
   }
-  if (band) return quant_vec8_exact(raw, s, inv);
+  if (band) return quant_vec8_div(raw, rs.s);
   return make_uint2(pack4_s8(q[0], q[1], q[2], q[3]), pack4_s8(q[4], q[5], q[6], q[7]));
 }
 
@@ -122,6 +143,18 @@ __device__ __forceinline__ float vec8_absmax(const uint4& raw) {
   const __nv_bfloat162 m = __hmax2(__hmax2(__habs2(h[0]), __habs2(h[1])), __hmax2(__habs2(h[2]), __habs2(h[3])));
   return fmaxf(__low2float(m), __high2float(m));
 }
+
+// Running max |x| over vectors, kept as a bf16 pair (exact: a maximum
+// involves no rounding) and widened once per row by absmax_of.
+__device__ __forceinline__ __nv_bfloat162 vec8_absmax2(const uint4& raw, __nv_bfloat162 m) {
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw);
+  m = __hmax2(m, __habs2(h[0]));
+  m = __hmax2(m, __habs2(h[1]));
+  m = __hmax2(m, __habs2(h[2]));
+  return __hmax2(m, __habs2(h[3]));
+}
+
+__device__ __forceinline__ float absmax_of(__nv_bfloat162 m) { return fmaxf(__low2float(m), __high2float(m)); }
 
 // silu(g) = g / (1 + exp(-g)) in fp32, y = bf16(silu(g) * u).  The fast
 // divide (g * rcp.approx(d)) is within a couple of fp32 ulps for
@@ -291,19 +324,18 @@ __global__ void __launch_bounds__(kRegThreads) rows_reg_kernel(const __nv_bfloat
     }
   }
   amax = block_max(amax, red);
-  const float s = __fdiv_rn(amax, 127.0f);
-  const float inv = s > 0.0f ? __frcp_rn(s) : 0.0f;
+  const RowScale rs = row_scale(amax);
   uint2* qr = reinterpret_cast<uint2*>(q + row * static_cast<int64_t>(width));
   uint4* yr = y_out ? reinterpret_cast<uint4*>(y_out + row * static_cast<int64_t>(width)) : nullptr;
 #pragma unroll
   for (int i = 0; i < VPT; ++i) {
     const int vi = threadIdx.x + i * blockDim.x;
     if (vi < nvec) {
-      qr[vi] = quant_vec8(buf[i], s, inv);
+      qr[vi] = quant_vec8(buf[i], rs);
       if (SILU && yr) yr[vi] = buf[i];
     }
   }
-  if (threadIdx.x == 0) scale[row] = s;
+  if (threadIdx.x == 0) scale[row] = rs.s;
 }
 
 // Shared-memory path: the row (or the SiLU*mul product) is staged on chip.
@@ -343,114 +375,247 @@ __global__ void __launch_bounds__(kSmemThreads) rows_smem_kernel(const __nv_bflo
     amax = fmaxf(amax, vec8_absmax(v));
   }
   amax = block_max(amax, red);  // its __syncthreads also publishes `stage`
-  const float s = __fdiv_rn(amax, 127.0f);
-  const float inv = s > 0.0f ? __frcp_rn(s) : 0.0f;
+  const RowScale rs = row_scale(amax);
   uint2* qr = reinterpret_cast<uint2*>(q + row * static_cast<int64_t>(width));
   uint4* yr = y_out ? reinterpret_cast<uint4*>(y_out + row * static_cast<int64_t>(width)) : nullptr;
   for (int i = threadIdx.x; i < nvec; i += kSmemThreads) {
     const uint4 v = stage[i];
-    qr[i] = quant_vec8(v, s, inv);
+    qr[i] = quant_vec8(v, rs);
     if (SILU && yr) yr[i] = v;
   }
-  if (threadIdx.x == 0) scale[row] = s;
+  if (threadIdx.x == 0) scale[row] = rs.s;
 }
 
-// Staged path (the plain quantiser, many rows of at most 24 KB): persistent
-// CTAs, CTA b taking rows b, b + G, b + 2G, ...  Thread 0 keeps DEPTH whole
-// rows in flight with 1-D bulk copies (cp.async.bulk, global -> shared
-// memory, completing on one mbarrier per stage); every thread then reads its
-// VPT vectors of the current row from shared memory, and as soon as the
-// block's absmax reduction shows that the row has been read, thread 0 reuses
-// the stage for the row DEPTH ahead.  The loads of later rows therefore stay
-// in flight while a row is reduced and quantised, which the one-row-per-CTA
-// path cannot do (its load phase drains before each reduction).
-// Waits on the stage barriers are bounded; on expiry the kernel records the
-// error, waits (bounded) for its copies still in flight and returns.
-constexpr int kStagedMaxRowBytes = 24 * 1024;
-constexpr int kStagedSmemBytes = 48 * 1024;
+// Warp-group path (many rows of at most 16384 values; SiLU*mul rows of at
+// most 8192): G warps (G = 1, 2 or 4) own a row, lane t of the group
+// (t < 32 G) holding vectors t + 32 G j, j < VPT, in registers, so every
+// load is a coalesced 128-bit access and all of a lane's loads are in flight
+// together.  The row's absmax is a warp-shuffle reduction plus, for G > 1,
+// one exchange through shared memory under a named barrier of the group's
+// own warps: no CTA-wide barrier, so rows never wait for one another.  The
+// grid is persistent (as many CTAs as are resident at once), group g taking
+// rows g, g + groups, ...
+constexpr int kWarpThreads = 128;  // 4 warps: groups of G = 1, 2 or 4 (at most 2 groups take a barrier)
+#ifndef W8A8_WARP_MAX_VPT
+#define W8A8_WARP_MAX_VPT 16  // plain rows: vectors per lane before G doubles
+#endif
+#ifndef W8A8_WARP_MAX_VPT_SILU
+#define W8A8_WARP_MAX_VPT_SILU 8  // SiLU*mul rows also hold the gate and up loads
+#endif
 
-constexpr int kStagedMaxThreads = 512;  // nvec / 4 threads: <= 384 for 24 KB rows
+template <int VPT, int G, bool SILU>
+__global__ void __launch_bounds__(kWarpThreads) rows_warp_kernel(const __nv_bfloat16* __restrict__ in, int64_t ld,
+                                                                 int8_t* __restrict__ q, float* __restrict__ scale,
+                                                                 __nv_bfloat16* __restrict__ y_out, int64_t M,
+                                                                 int width) {
+  constexpr int kGroups = kWarpThreads / 32 / G;
+  __shared__ float part[2][kWarpThreads / 32];  // per-warp maxima, by row parity
+  w8a8::dev::griddep_launch();  // early trigger, as in rows_reg_kernel
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int grp = warp / G;
+  const int t = (warp % G) * 32 + lane;
+  const int nvec = width >> 3;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * kGroups;
+  w8a8::dev::griddep_wait();  // the rows are the previous kernel's output
+  int it = 0;
+  for (int64_t row = static_cast<int64_t>(blockIdx.x) * kGroups + grp; row < M; row += stride, ++it) {
+    const RowSrc<SILU> src(in, row, ld, width);
+    uint4 v[VPT];
+    __nv_bfloat162 m2 = __float2bfloat162_rn(0.0f);
+    if constexpr (SILU) {
+      uint4 u[VPT];
+#pragma unroll
+      for (int j = 0; j < VPT; ++j) {
+        const int vi = t + j * 32 * G;
+        if (vi < nvec) src.fetch(vi, v[j], u[j]);
+      }
+#pragma unroll
+      for (int j = 0; j < VPT; ++j) {
+        const int vi = t + j * 32 * G;
+        if (vi < nvec) {
+          v[j] = silu_mul_vec8(v[j], u[j]);
+          m2 = vec8_absmax2(v[j], m2);
+        }
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < VPT; ++j) {
+        const int vi = t + j * 32 * G;
+        if (vi < nvec) {
+          uint4 unused;
+          src.fetch(vi, v[j], unused);
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < VPT; ++j)
+        if (t + j * 32 * G < nvec) m2 = vec8_absmax2(v[j], m2);
+    }
+    float amax = warp_max(absmax_of(m2));
+    if constexpr (G > 1) {
+      float* p = &part[it & 1][grp * G];
+      if (lane == 0) p[warp % G] = amax;
+      // constant barrier ids (one per group of the CTA)
+      if (kGroups == 1 || grp == 0)
+        w8a8::dev::named_bar_sync(1, 32 * G);
+      else
+        w8a8::dev::named_bar_sync(2, 32 * G);
+#pragma unroll
+      for (int k = 0; k < G; ++k) amax = fmaxf(amax, p[k]);
+    }
+    const RowScale rs = row_scale(amax);
+    uint2* qr = reinterpret_cast<uint2*>(q + row * static_cast<int64_t>(width));
+    uint4* yr = SILU && y_out ? reinterpret_cast<uint4*>(y_out + row * static_cast<int64_t>(width)) : nullptr;
+#pragma unroll
+    for (int j = 0; j < VPT; ++j) {
+      const int vi = t + j * 32 * G;
+      if (vi < nvec) {
+        qr[vi] = quant_vec8(v[j], rs);
+        if (SILU && yr) yr[vi] = v[j];
+      }
+    }
+    if (t == 0) scale[row] = rs.s;
+  }
+}
 
-template <int VPT>
-__global__ void __launch_bounds__(kStagedMaxThreads) rows_staged_kernel(const __nv_bfloat16* __restrict__ in, int64_t ld,
-                                                                  int8_t* __restrict__ q, float* __restrict__ scale,
-                                                                  int64_t M, int width, int depth, unsigned int* err,
-                                                                  long long timeout_ns) {
-  extern __shared__ __align__(128) uint4 rows_smem[];
-  __shared__ float red[32];
-  __shared__ uint64_t full[8];
+// SiLU*mul pipeline (many wide gate_up rows): persistent CTAs, one per SM.
+// A producer warp streams each row's gate and up halves in chunks of
+// kPipeChunk vectors into a ring of shared-memory stages with 1-D bulk copies
+// (cp.async.bulk, completing on a `full` mbarrier per stage) and reuses a
+// stage once every consumer warp has arrived on its `empty` mbarrier.  CONS
+// consumer threads turn each chunk into y = bf16(silu(g) * u), keep y in a
+// row buffer in shared memory and fold it into a running absmax; at the end
+// of the row one named barrier of the consumers reduces the absmax and each
+// consumer quantises the vectors it computed itself (vector i belongs to
+// thread i mod CONS in both phases, so the row buffer needs no barrier of its
+// own).  The producer meanwhile keeps loading the next row, so HBM reads do
+// not stop during the reduction and the quantisation.
+// Waits are bounded; on expiry the kernel records the error, every role
+// leaves its loop, and the producer waits (bounded) for its copies in flight.
+constexpr int kPipeChunk = 512;                // vectors (16 B) of gate, and of up, per stage
+constexpr int kPipeStageBytes = 2 * kPipeChunk * 16;
+constexpr int kPipeMaxStages = 8;
+constexpr int kPipeSmemLimit = 220 * 1024;
+
+template <int CONS>
+__global__ void __launch_bounds__(CONS + 32, 1) silu_pipe_kernel(const __nv_bfloat16* __restrict__ in, int64_t ld,
+                                                                 int8_t* __restrict__ q, float* __restrict__ scale,
+                                                                 __nv_bfloat16* __restrict__ y_out, int64_t M,
+                                                                 int width, int stages, unsigned int* err,
+                                                                 long long timeout_ns) {
+  constexpr int kConsWarps = CONS / 32;
+  constexpr int kVpc = kPipeChunk / CONS;  // vectors per consumer thread per chunk
+  extern __shared__ __align__(128) uint4 pipe_smem[];
+  __shared__ uint64_t full[kPipeMaxStages], empty[kPipeMaxStages];
+  __shared__ float red[2][kConsWarps];
   __shared__ int abort_flag;
   w8a8::dev::griddep_launch();  // early trigger, as in rows_reg_kernel
   const int nvec = width >> 3;
-  const uint32_t row_bytes = static_cast<uint32_t>(width) * 2u;
-  const uint32_t stage_vecs = (row_bytes + 127u) / 128u * 8u;  // stages 128-byte aligned
+  const int nchunk = (nvec + kPipeChunk - 1) / kPipeChunk;
+  uint4* ring = pipe_smem;
+  uint4* yrow = pipe_smem + static_cast<size_t>(stages) * 2 * kPipeChunk;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t G = gridDim.x;
-  const int64_t nrows = (M - blockIdx.x + G - 1) / G;  // rows of this CTA
   if (threadIdx.x == 0) {
-    for (int i = 0; i < depth; ++i) w8a8::dev::mbar_init(w8a8::dev::smem_u32(&full[i]), 1);
+    for (int i = 0; i < stages; ++i) {
+      w8a8::dev::mbar_init(w8a8::dev::smem_u32(&full[i]), 1);
+      w8a8::dev::mbar_init(w8a8::dev::smem_u32(&empty[i]), kConsWarps);
+    }
     abort_flag = 0;
     w8a8::dev::fence_mbar_init();
   }
   __syncthreads();
-  w8a8::dev::griddep_wait();  // the rows are the previous kernel's output
-  const uint64_t policy = w8a8::dev::policy_evict_first();
-  auto issue = [&](int64_t i) {  // row i of this CTA into stage i % depth
-    const int st = static_cast<int>(i % depth);
-    const uint32_t bar = w8a8::dev::smem_u32(&full[st]);
-    w8a8::dev::mbar_expect_tx(bar, row_bytes);
-    w8a8::dev::bulk_load_1d(w8a8::dev::smem_u32(rows_smem + st * stage_vecs), in + (blockIdx.x + i * G) * ld,
-                            row_bytes, bar, policy);
-  };
-  if (threadIdx.x == 0)
-    for (int64_t i = 0; i < depth && i < nrows; ++i) issue(i);
-  int64_t issued = nrows < depth ? nrows : depth;
-  for (int64_t i = 0; i < nrows; ++i) {
-    const int st = static_cast<int>(i % depth);
-    const uint32_t parity = static_cast<uint32_t>((i / depth) & 1);
-    // One thread waits for the stage (the others idle at the barrier instead
-    // of spinning through issue slots), then every thread tests the completed
-    // phase once, which gives it the acquire of the bulk copy's bytes.
-    bool ok = true;
-    if (threadIdx.x == 0)
-      ok = w8a8::dev::mbar_wait(w8a8::dev::smem_u32(&full[st]), parity, &abort_flag, err, w8a8::kErrGemmWait,
-                                timeout_ns);
-    if (__syncthreads_or(!ok)) break;
-    (void)w8a8::dev::mbar_test(w8a8::dev::smem_u32(&full[st]), parity);
-    const uint4* row = rows_smem + st * stage_vecs;
-    uint4 buf[VPT];
-    float amax = 0.0f;
-#pragma unroll
-    for (int j = 0; j < VPT; ++j) {
-      const int vi = threadIdx.x + j * blockDim.x;
-      if (vi < nvec) {
-        buf[j] = row[vi];
-        amax = fmaxf(amax, vec8_absmax(buf[j]));
+  w8a8::dev::griddep_wait();  // gate_up is the previous kernel's output
+  if (warp == kConsWarps) {
+    // ------------------------------------------------------------- producer
+    if (lane == 0) {
+      const uint64_t policy = w8a8::dev::policy_evict_first();
+      uint32_t k = 0;
+      bool ok = true;
+      for (int64_t row = blockIdx.x; ok && row < M; row += G) {
+        const __nv_bfloat16* src = in + row * ld;
+        for (int c = 0; c < nchunk; ++c, ++k) {
+          const int st = static_cast<int>(k % static_cast<uint32_t>(stages));
+          const uint32_t ph = (k / static_cast<uint32_t>(stages)) & 1u;
+          if (k >= static_cast<uint32_t>(stages) &&
+              !w8a8::dev::mbar_wait(w8a8::dev::smem_u32(&empty[st]), ph ^ 1u, &abort_flag, err, w8a8::kErrGemmWait,
+                                    timeout_ns)) {
+            ok = false;
+            break;
+          }
+          const int n = nvec - c * kPipeChunk < kPipeChunk ? nvec - c * kPipeChunk : kPipeChunk;
+          const uint32_t bytes = static_cast<uint32_t>(n) * 16u;
+          const uint32_t bar = w8a8::dev::smem_u32(&full[st]);
+          w8a8::dev::mbar_expect_tx(bar, 2u * bytes);
+          uint4* dst = ring + static_cast<size_t>(st) * 2 * kPipeChunk;
+          w8a8::dev::bulk_load_1d(w8a8::dev::smem_u32(dst), src + static_cast<int64_t>(c) * kPipeChunk * 8, bytes,
+                                  bar, policy);
+          w8a8::dev::bulk_load_1d(w8a8::dev::smem_u32(dst + kPipeChunk),
+                                  src + width + static_cast<int64_t>(c) * kPipeChunk * 8, bytes, bar, policy);
+        }
+      }
+      // Copies may still be landing (after an abort, they may have no
+      // consumer): wait (bounded) for the last copy issued into every stage
+      // before the CTA's shared memory can be released.
+      const uint32_t first = k > static_cast<uint32_t>(stages) ? k - static_cast<uint32_t>(stages) : 0u;
+      for (uint32_t i = first; i < k; ++i) {
+        const int st = static_cast<int>(i % static_cast<uint32_t>(stages));
+        if (!w8a8::dev::mbar_wait_drain(w8a8::dev::smem_u32(&full[st]), (i / static_cast<uint32_t>(stages)) & 1u,
+                                        timeout_ns) && err)
+          atomicOr(err, w8a8::kErrGemmDrain);
       }
     }
-    amax = block_max(amax, red);  // its barrier also means every thread has read the stage
-    if (threadIdx.x == 0 && issued < nrows) issue(issued);
-    ++issued;
-    const float sc = __fdiv_rn(amax, 127.0f);
-    const float inv = sc > 0.0f ? __frcp_rn(sc) : 0.0f;
-    const int64_t r = blockIdx.x + i * G;
-    uint2* qr = reinterpret_cast<uint2*>(q + r * static_cast<int64_t>(width));
-#pragma unroll
-    for (int j = 0; j < VPT; ++j) {
-      const int vi = threadIdx.x + j * blockDim.x;
-      if (vi < nvec) qr[vi] = quant_vec8(buf[j], sc, inv);
-    }
-    if (threadIdx.x == 0) scale[r] = sc;
-    __syncthreads();  // `red` is reused by the next row's reduction
+    return;
   }
-  // After an abort, copies may still be landing: wait (bounded) for every
-  // issued stage before the CTA's shared memory is released.
-  if (threadIdx.x == 0 && abort_flag) {
-    const int64_t last = issued < nrows ? issued : nrows;
-    for (int64_t i = last - depth < 0 ? 0 : last - depth; i < last; ++i) {
-      if (!w8a8::dev::mbar_wait_drain(w8a8::dev::smem_u32(&full[i % depth]), static_cast<uint32_t>((i / depth) & 1),
-                                      timeout_ns) && err)
-        atomicOr(err, w8a8::kErrGemmDrain);
+  // --------------------------------------------------------------- consumers
+  const int t = threadIdx.x;
+  uint32_t k = 0;
+  int it = 0;
+  for (int64_t row = blockIdx.x; row < M; row += G, ++it) {
+    __nv_bfloat162 m2 = __float2bfloat162_rn(0.0f);
+    bool ok = true;
+    for (int c = 0; c < nchunk; ++c, ++k) {
+      const int st = static_cast<int>(k % static_cast<uint32_t>(stages));
+      const uint32_t ph = (k / static_cast<uint32_t>(stages)) & 1u;
+      // lane 0 waits for the stage and tells its warp (the warp stays
+      // converged, also on a timeout); every lane then tests the completed
+      // phase once, which gives it the acquire of the copied bytes
+      bool got = true;
+      if (lane == 0)
+        got = w8a8::dev::mbar_wait(w8a8::dev::smem_u32(&full[st]), ph, &abort_flag, err, w8a8::kErrGemmWait,
+                                   timeout_ns);
+      if (!__shfl_sync(0xffffffffu, got, 0)) {
+        ok = false;
+        break;
+      }
+      (void)w8a8::dev::mbar_test(w8a8::dev::smem_u32(&full[st]), ph);
+      const uint4* gs = ring + static_cast<size_t>(st) * 2 * kPipeChunk;
+#pragma unroll
+      for (int j = 0; j < kVpc; ++j) {
+        const int i = t + j * CONS;
+        const int vi = c * kPipeChunk + i;
+        if (vi < nvec) {
+          const uint4 y = silu_mul_vec8(gs[i], gs[kPipeChunk + i]);
+          yrow[vi] = y;
+          m2 = vec8_absmax2(y, m2);
+        }
+      }
+      __syncwarp();
+      if (lane == 0) w8a8::dev::mbar_arrive(w8a8::dev::smem_u32(&empty[st]));
     }
+    float amax = warp_max(absmax_of(m2));
+    if (lane == 0) red[it & 1][warp] = amax;
+    if (w8a8::dev::named_bar_or(1, CONS, !ok)) break;  // an abort anywhere ends every consumer here
+#pragma unroll
+    for (int w = 0; w < kConsWarps; ++w) amax = fmaxf(amax, red[it & 1][w]);
+    const RowScale rs = row_scale(amax);
+    uint2* qr = reinterpret_cast<uint2*>(q + row * static_cast<int64_t>(width));
+    uint4* yr = y_out ? reinterpret_cast<uint4*>(y_out + row * static_cast<int64_t>(width)) : nullptr;
+    for (int vi = t; vi < nvec; vi += CONS) {
+      const uint4 y = yrow[vi];
+      qr[vi] = quant_vec8(y, rs);
+      if (yr) yr[vi] = y;
+    }
+    if (t == 0) scale[row] = rs.s;
   }
 }
 
@@ -510,19 +675,18 @@ __global__ void __launch_bounds__(kRegThreads) rows_cluster_kernel(const __nv_bf
   }
   amax = block_max(amax, red);
   amax = cluster_max(amax, &share_max);
-  const float s = __fdiv_rn(amax, 127.0f);
-  const float inv = s > 0.0f ? __frcp_rn(s) : 0.0f;
+  const RowScale rs = row_scale(amax);
   uint2* qr = reinterpret_cast<uint2*>(q + row * static_cast<int64_t>(width));
   uint4* yr = y_out ? reinterpret_cast<uint4*>(y_out + row * static_cast<int64_t>(width)) : nullptr;
 #pragma unroll
   for (int i = 0; i < VPT; ++i) {
     const int vi = lo + threadIdx.x + i * kRegThreads;
     if (vi < hi) {
-      qr[vi] = quant_vec8(buf[i], s, inv);
+      qr[vi] = quant_vec8(buf[i], rs);
       if (SILU && yr) yr[vi] = buf[i];
     }
   }
-  if (c == 0 && threadIdx.x == 0) scale[row] = s;
+  if (c == 0 && threadIdx.x == 0) scale[row] = rs.s;
   w8a8::dev::cluster_sync();  // no CTA leaves while a peer may still read its share_max
 }
 
@@ -623,18 +787,17 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_quant_kernel(
     amax = fmaxf(amax, vec8_absmax(ya[i]));
   }
   amax = block_max(amax, red);
-  const float s = __fdiv_rn(amax, 127.0f);
-  const float inv = s > 0.0f ? __frcp_rn(s) : 0.0f;
+  const RowScale rs = row_scale(amax);
   uint2* qr = reinterpret_cast<uint2*>(q + row * static_cast<int64_t>(width));
   uint4* yr = y_out ? reinterpret_cast<uint4*>(y_out + row * static_cast<int64_t>(width)) : nullptr;
 #pragma unroll
   for (int i = 0; i < VPT; ++i) {
     const int vi = threadIdx.x + i * blockDim.x;
     if (vi >= nvec) continue;
-    qr[vi] = quant_vec8(ya[i], s, inv);
+    qr[vi] = quant_vec8(ya[i], rs);
     if (yr) yr[vi] = ya[i];
   }
-  if (threadIdx.x == 0) scale[row] = s;
+  if (threadIdx.x == 0) scale[row] = rs.s;
 }
 
 template <bool ADD>
@@ -687,23 +850,94 @@ cudaError_t launch_cluster_rows(const __nv_bfloat16* in, int64_t ld, int8_t* q, 
   return cudaLaunchKernelEx(&cfg, rows_cluster_kernel<VPT, SILU>, in, ld, q, scale, y, width);
 }
 
-// Staged path launch: VPT = 4 vectors per thread (threads = nvec / 4
-// rounded up to a warp), DEPTH rows in flight within 48 KB of shared memory,
-// as many persistent CTAs as fit on the SMs (by threads and by shared memory).
-int launch_staged_rows(const __nv_bfloat16* in, int64_t ld, int8_t* q, float* scale, int64_t M, int width,
-                       int nsm, cudaStream_t s) {
+// Resident CTAs per SM of a kernel at a given block size and dynamic shared
+// memory, queried once per device and kernel instance.
+template <typename Kernel>
+int resident_ctas(Kernel kernel, int threads, size_t smem) {
+  static int cached[64] = {0};
+  const int dev = w8a8::current_device();
+  if (dev < 0 || dev >= 64) return 1;
+  if (cached[dev] == 0) {
+    int n = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kernel, threads, smem) != cudaSuccess || n < 1) n = 1;
+    cached[dev] = n;
+  }
+  return cached[dev];
+}
+
+template <int VPT, int G, bool SILU>
+cudaError_t launch_warp_rows(const __nv_bfloat16* in, int64_t ld, int8_t* q, float* scale, __nv_bfloat16* y,
+                             int64_t M, int width, int nsm, cudaStream_t s) {
+  constexpr int kGroups = kWarpThreads / 32 / G;
+  const int per_sm = resident_ctas(rows_warp_kernel<VPT, G, SILU>, kWarpThreads, 0);
+  int64_t grid = (M + kGroups - 1) / kGroups;
+  const int64_t cap = static_cast<int64_t>(nsm) * per_sm;
+  if (grid > cap) grid = cap;
+  return w8a8::launch_pdl(rows_warp_kernel<VPT, G, SILU>, dim3(static_cast<unsigned>(grid)), dim3(kWarpThreads), 0,
+                          s, in, ld, q, scale, y, M, width);
+}
+
+// Vectors per lane rounded up to an instantiated count (plain rows: 2, 4, 8,
+// 10, 12, 16; SiLU*mul rows: 2, 4, 6, 8).
+template <int G, bool SILU>
+cudaError_t launch_warp_rows_vpt(int vpt, const __nv_bfloat16* in, int64_t ld, int8_t* q, float* scale,
+                                 __nv_bfloat16* y, int64_t M, int width, int nsm, cudaStream_t s) {
+  if constexpr (SILU) {
+    if (vpt <= 2) return launch_warp_rows<2, G, SILU>(in, ld, q, scale, y, M, width, nsm, s);
+    if (vpt <= 4) return launch_warp_rows<4, G, SILU>(in, ld, q, scale, y, M, width, nsm, s);
+    if (vpt <= 6) return launch_warp_rows<6, G, SILU>(in, ld, q, scale, y, M, width, nsm, s);
+    return launch_warp_rows<8, G, SILU>(in, ld, q, scale, y, M, width, nsm, s);
+  } else {
+    if (vpt <= 2) return launch_warp_rows<2, G, SILU>(in, ld, q, scale, y, M, width, nsm, s);
+    if (vpt <= 4) return launch_warp_rows<4, G, SILU>(in, ld, q, scale, y, M, width, nsm, s);
+    if (vpt <= 8) return launch_warp_rows<8, G, SILU>(in, ld, q, scale, y, M, width, nsm, s);
+    if (vpt <= 10) return launch_warp_rows<10, G, SILU>(in, ld, q, scale, y, M, width, nsm, s);
+    if (vpt <= 12) return launch_warp_rows<12, G, SILU>(in, ld, q, scale, y, M, width, nsm, s);
+    return launch_warp_rows<16, G, SILU>(in, ld, q, scale, y, M, width, nsm, s);
+  }
+}
+
+// Warps per row for the warp-group path: the fewest (1, 2 or 4) that keep a
+// lane's vectors within the target; 0 when the row is too wide for 4 warps.
+template <bool SILU>
+int warp_group_size(int nvec) {
+  const int target = SILU ? W8A8_WARP_MAX_VPT_SILU : W8A8_WARP_MAX_VPT;
+  const int limit = SILU ? 8 : 16;
+  for (int g = 1; g <= 4; g *= 2)
+    if ((nvec + 32 * g - 1) / (32 * g) <= target) return g;
+  return (nvec + 127) / 128 <= limit ? 4 : 0;
+}
+
+template <bool SILU>
+int launch_warp_group(const __nv_bfloat16* in, int64_t ld, int8_t* q, float* scale, __nv_bfloat16* y, int64_t M,
+                      int width, int g, int nsm, cudaStream_t s) {
   const int nvec = width / 8;
-  const int threads = ((nvec + 3) / 4 + 31) / 32 * 32;
-  const int stage_bytes = (width * 2 + 127) / 128 * 128;
-  int depth = kStagedSmemBytes / stage_bytes;
-  depth = depth < 2 ? 2 : (depth > 8 ? 8 : depth);
-  const int smem = depth * stage_bytes;
-  int per_sm = 2048 / threads;
-  const int by_smem = (227 * 1024) / (smem + 1024 + 512);
-  per_sm = per_sm < by_smem ? per_sm : by_smem;
-  per_sm = per_sm < 1 ? 1 : (per_sm > 16 ? 16 : per_sm);
-  int64_t grid = static_cast<int64_t>(nsm) * per_sm;
-  if (grid > M) grid = M;
+  const int vpt = (nvec + 32 * g - 1) / (32 * g);
+  switch (g) {
+    case 1: W8A8_CUDA_TRY((launch_warp_rows_vpt<1, SILU>(vpt, in, ld, q, scale, y, M, width, nsm, s))); break;
+    case 2: W8A8_CUDA_TRY((launch_warp_rows_vpt<2, SILU>(vpt, in, ld, q, scale, y, M, width, nsm, s))); break;
+    default: W8A8_CUDA_TRY((launch_warp_rows_vpt<4, SILU>(vpt, in, ld, q, scale, y, M, width, nsm, s))); break;
+  }
+  return W8A8_OK;
+}
+
+#ifndef W8A8_PIPE_CONS
+#define W8A8_PIPE_CONS 256  // consumer threads of the SiLU*mul pipeline (256 or 512)
+#endif
+
+// Stages of the SiLU*mul pipeline for rows of nvec output vectors (0 = the
+// row buffer leaves room for fewer than two stages).
+inline int silu_pipe_stages(int nvec) {
+  const int room = kPipeSmemLimit - nvec * 16;
+  int st = room / kPipeStageBytes;
+  return st < 2 ? 0 : (st > kPipeMaxStages ? kPipeMaxStages : st);
+}
+
+int launch_silu_pipe(const __nv_bfloat16* in, int64_t ld, int8_t* q, float* scale, __nv_bfloat16* y, int64_t M,
+                     int width, int nsm, cudaStream_t s) {
+  const int nvec = width / 8;
+  const int stages = silu_pipe_stages(nvec);
+  const size_t smem = static_cast<size_t>(stages) * kPipeStageBytes + static_cast<size_t>(nvec) * 16;
   unsigned int* err = w8a8::device_error_word();
   if (!err) return W8A8_ERR_CUDA;
   static std::mutex mu;
@@ -713,13 +947,14 @@ int launch_staged_rows(const __nv_bfloat16* in, int64_t ld, int8_t* q, float* sc
   {
     std::lock_guard<std::mutex> lk(mu);
     if (!configured[dev]) {
-      W8A8_CUDA_TRY(cudaFuncSetAttribute(rows_staged_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         kStagedSmemBytes));
+      W8A8_CUDA_TRY(cudaFuncSetAttribute(silu_pipe_kernel<W8A8_PIPE_CONS>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, kPipeSmemLimit));
       configured[dev] = true;
     }
   }
-  W8A8_CUDA_TRY(w8a8::launch_pdl(rows_staged_kernel<4>, dim3(static_cast<unsigned>(grid)), dim3(threads),
-                                 static_cast<size_t>(smem), s, in, ld, q, scale, M, width, depth, err,
+  const int64_t grid = M < nsm ? M : nsm;
+  W8A8_CUDA_TRY(w8a8::launch_pdl(silu_pipe_kernel<W8A8_PIPE_CONS>, dim3(static_cast<unsigned>(grid)),
+                                 dim3(W8A8_PIPE_CONS + 32), smem, s, in, ld, q, scale, y, M, width, stages, err,
                                  w8a8::kDefaultGemmTimeoutNs));
   return W8A8_OK;
 }
@@ -732,10 +967,14 @@ int launch_rows(const __nv_bfloat16* in, int64_t ld, int8_t* q, float* scale, __
   int nsm = w8a8::sm_count();
   if (nsm <= 0) nsm = 148;
   const int csize = row_cluster_size(M, nvec, nsm);
-  // many rows of the plain quantiser: the bulk-copy staged persistent kernel
-  if (!SILU && csize == 0 && width * 2 <= kStagedMaxRowBytes && nvec >= 64 &&
-      (reinterpret_cast<uintptr_t>(in) & 15u) == 0 && ld % 8 == 0)
-    return launch_staged_rows(in, ld, q, scale, M, width, nsm, s);
+  const bool aligned = (reinterpret_cast<uintptr_t>(in) & 15u) == 0 && ld % 8 == 0;
+  if (csize == 0 && aligned) {
+    // many rows: warp groups per row (plain rows, narrow SiLU*mul rows), or
+    // the bulk-copy pipeline for wide SiLU*mul rows
+    const int g = warp_group_size<SILU>(nvec);
+    if (g > 0) return launch_warp_group<SILU>(in, ld, q, scale, y, M, width, g, nsm, s);
+    if (SILU && silu_pipe_stages(nvec) > 0) return launch_silu_pipe(in, ld, q, scale, y, M, width, nsm, s);
+  }
   if (csize > 0) {
     const int per = (nvec + csize - 1) / csize;
     const int vpt = per <= kRegThreads ? 1 : (per <= 2 * kRegThreads ? 2 : 4);

@@ -183,11 +183,13 @@ def test_silu_mul_quant_cluster_rows(pkg, oracle, cuda_dev, m, i):
     assert torch.equal(qa2.q.cpu(), qa.q.cpu()) and torch.equal(qa2.s.cpu(), qa.s.cpu())
 
 
-# Many rows of at most 24 KB: the persistent kernel that keeps several rows in
-# flight with bulk copies into shared memory (rows per CTA > pipeline depth,
-# ragged last wave, strided rows as in the q slice of a qkv output).
+# Many rows of at most 16384 values: the persistent warp-group kernel (1, 2
+# or 4 warps per row held in registers; rows per group > 1, ragged last wave,
+# rows that do not fill every lane, strided rows as in the q slice of a qkv
+# output).
 STAGED_SHAPES = [(296, 5120, 5120), (4096, 5120, 5120), (4096, 8192, 10240), (1000, 12288, 12288),
-                 (777, 512, 520), (3000, 2048, 2048), (513, 1024, 1536)]
+                 (777, 512, 520), (3000, 2048, 2048), (513, 1024, 1536), (400, 16384, 16384), (350, 40, 40),
+                 (9000, 3584, 3584)]
 
 
 @pytest.mark.parametrize("m,k,ld", STAGED_SHAPES)
@@ -215,3 +217,82 @@ def test_quant_half_integer_ties(pkg, oracle, cuda_dev):
         q, s = pkg.ops.quant_per_token(xb.to(cuda_dev))
         q_ref, s_ref = oracle.quant_per_token(xb)
         assert torch.equal(s.cpu(), s_ref) and torch.equal(q.cpu(), q_ref), m
+
+
+# Many SiLU*mul rows: narrow rows (at most 8192 outputs) in the warp-group
+# kernel, wide rows in the bulk-copy pipeline (chunks of 512 vectors, the last
+# one ragged for I = 25600, rows per CTA above the ring depth).
+SILU_MANY = [(296, 25600), (700, 12800), (300, 12288), (4096, 3200), (500, 6400), (777, 1000), (1200, 8192),
+             (2000, 25600)]
+
+
+@pytest.mark.parametrize("m,i", SILU_MANY)
+def test_silu_mul_quant_many_rows(pkg, oracle, cuda_dev, m, i):
+    gu = _x(m, 2 * i + 8, seed=m * 5 + i, scale=2.0)[:, : 2 * i]  # strided rows
+    gu[m // 3, i - 1] = 30.0  # a large product at a row's last element
+    gu[m // 3, 2 * i - 1] = 4.0
+    gu[m - 1, i:] = 0  # all-zero product row
+    gd = gu.to(cuda_dev)
+    qa, y = pkg.ops.silu_and_mul_quant(gd, with_bf16=True)
+    y_ref = oracle.silu_and_mul(gu.contiguous())
+    yc = y.cpu()
+    diff = (yc.float() - y_ref.float()).abs()
+    assert torch.all(diff <= y_ref.float().abs() * 2.0 ** -7 + 1e-30), float(diff.max())
+    assert (yc != y_ref).float().mean().item() < 1e-3
+    q_ref, s_ref = oracle.quant_per_token(yc)
+    assert torch.equal(qa.s.cpu(), s_ref) and torch.equal(qa.q.cpu(), q_ref)
+    assert float(qa.s[m - 1]) == 0.0
+    qa2 = pkg.ops.silu_and_mul_quant(gd)
+    assert torch.equal(qa2.q.cpu(), qa.q.cpu()) and torch.equal(qa2.s.cpu(), qa.s.cpu())
+
+
+def _all_bf16_upto(amax: float) -> torch.Tensor:
+    """Every finite bf16 value v with |v| <= amax (both signs), amax first."""
+    bits = torch.arange(0, 0x7F80, dtype=torch.int32).to(torch.int16).view(torch.bfloat16)
+    a = torch.tensor(amax).bfloat16()
+    pos = bits[bits.float() <= a.float()]
+    return torch.cat([a.reshape(1), pos, -pos])
+
+
+@pytest.mark.parametrize("many", [False, True])
+def test_quant_every_bf16_value(pkg, oracle, cuda_dev, many):
+    """For absmax values across the whole exponent range (subnormal scales
+    included: 1/s is infinite below s = 2^-128), every bf16 value that can
+    share a row with that absmax is quantised bit-exactly.  Rows of 16384
+    values, each led by its absmax: 18 rows reach the cluster kernel, the
+    same rows repeated to >= 296 the warp-group kernel."""
+    width = 16384
+    rows = []
+    for amax in (1.0, 3.140625, 127.0, 1e-20, 2.0e-36, 1.2e-38, 5.0e-39, 1.0e-39, 9.2e-41, 3.0e38):
+        v = _all_bf16_upto(amax)
+        n = (v.numel() + width - 2) // (width - 1)
+        pad = torch.zeros(n * (width - 1) - (v.numel() - 1), dtype=torch.bfloat16)
+        body = torch.cat([v[1:], pad]).reshape(n, width - 1)
+        rows.append(torch.cat([v[:1].expand(n, 1), body], dim=1))
+    x = torch.cat(rows)
+    if many:
+        x = x.repeat((296 + x.shape[0] - 1) // x.shape[0], 1)
+    q, s = pkg.ops.quant_per_token(x.to(cuda_dev))
+    q_ref, s_ref = oracle.quant_per_token(x)
+    assert torch.equal(s.cpu(), s_ref)
+    bad = (q.cpu() != q_ref).nonzero()
+    assert bad.numel() == 0, (bad[:5].tolist(), x[bad[0, 0], bad[0, 1]].item() if bad.numel() else None)
+
+
+def test_quant_subnormal_scale_rows(pkg, oracle, cuda_dev):
+    """Rows whose scale is subnormal (absmax below ~1.5e-36): through the
+    warp-group, cluster and register paths, and from the fused SiLU*mul."""
+    for m, k in ((400, 5120), (3, 5120), (2, 256)):
+        x = _x(m, k, seed=m + k)
+        for r, amax in enumerate((1.0e-38, 9.2e-41, 3.0e-39)):
+            if r < m:
+                x[r] = (x[r].float() / x[r].float().abs().max() * amax).bfloat16()
+        q, s = pkg.ops.quant_per_token(x.to(cuda_dev))
+        q_ref, s_ref = oracle.quant_per_token(x)
+        assert torch.equal(s.cpu(), s_ref) and torch.equal(q.cpu(), q_ref)
+        assert int(q[0].abs().max()) == 127
+    gu = _x(300, 2 * 3200, seed=5)
+    gu[:, 3200:] = (gu[:, 3200:].float() * 1e-38).bfloat16()
+    qa, y = pkg.ops.silu_and_mul_quant(gu.to(cuda_dev), with_bf16=True)
+    q_ref, s_ref = oracle.quant_per_token(y.cpu())
+    assert torch.equal(qa.s.cpu(), s_ref) and torch.equal(qa.q.cpu(), q_ref)
