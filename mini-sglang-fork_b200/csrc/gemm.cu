@@ -107,7 +107,7 @@ int launch_pair_variant(const GemmPlan& p, const CUtensorMap& ta, const CUtensor
       configured[dev] = true;
     }
   }
-  W8A8_CUDA_TRY(launch_pdl(kern, dim3(p.grid), dim3(gemm_block_threads<FUSED>()), kSmem, stream, ta, tb,
+  W8A8_CUDA_TRY(launch_pdl(kern, dim3(p.grid), dim3(gemm2_block_threads<FUSED>()), kSmem, stream, ta, tb,
                            args, cv));
   return W8A8_OK;
 }

@@ -40,19 +40,34 @@ struct Gemm2Traits {
   static constexpr int kAccCols = 256;
   static constexpr int kTmemCols = 512;
   static constexpr int kBarrierBytes = 256;
-  static constexpr int kStagingBytes = 4 * 2048;
   static constexpr int kTileOutBytes = 128 * kBN * 2;
-  // the staging buffer serves both modes (the epilogue's row-contiguous
-  // stores); the hand-over state only the fused one
+  // the staging buffers (2 KB per epilogue warp) serve both modes (the
+  // epilogue's row-contiguous stores); the hand-over state only the fused one
+  static constexpr int staging_bytes(bool fused) { return (fused ? 4 : 8) * 2048; }
   static constexpr int kScaleBytes = 2 * 2 * kBN * 4;  // double-buffered scales and bias of the tile (fp32)
-  static constexpr int kSmemBytesPlain = 1024 + STAGES * kStageBytes + kBarrierBytes + kStagingBytes + kScaleBytes;
-  static constexpr int kSmemBytes = kSmemBytesPlain + kSignalBytes;
+  static constexpr int kSmemBytesPlain =
+      1024 + STAGES * kStageBytes + kBarrierBytes + staging_bytes(false) + kScaleBytes;
+  static constexpr int kSmemBytes =
+      1024 + STAGES * kStageBytes + kBarrierBytes + staging_bytes(true) + kScaleBytes + kSignalBytes;
   static constexpr int smem_bytes(bool fused) { return fused ? kSmemBytes : kSmemBytesPlain; }
   static constexpr uint32_t kIdesc = dev::idesc_i8(256, 256);
   // (the launch checks the footprint of the mode it launches: a 7-stage ring
   // fits only without the fused-mode buffers)
   static_assert(kSmemBytesPlain <= 227 * 1024, "shared memory");
 };
+
+// Epilogue warps (warps 2, 3, ...): four in fused mode, one per TMEM lane
+// quarter (warps 6-7 reduce there); eight in plain mode, two per lane quarter,
+// each converting half of the block's 256 accumulator columns, which halves
+// the per-block epilogue that sets the time of short-K GEMMs.
+template <bool FUSED>
+constexpr int gemm2_epi_warps() {
+  return FUSED ? 4 : 8;
+}
+template <bool FUSED>
+constexpr int gemm2_block_threads() {
+  return FUSED ? gemm_block_threads<true>() : 32 * (2 + gemm2_epi_warps<false>());
+}
 
 // Pair p -> (pw, tn): 256-row block index and 256-column block index.
 __device__ __forceinline__ void pair_coords(const GemmArgs& a, int pairs_w, int p, int& pw, int& tn) {
@@ -71,10 +86,13 @@ __device__ __forceinline__ int tile_index(const GemmArgs& a, int tw, int tn) {
 }
 
 template <int STAGES, bool FUSED>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(gemm_block_threads<FUSED>(), 1)
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(gemm2_block_threads<FUSED>(), 1)
     w8a8_gemm2_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
                       const GemmArgs args, const CommView cv) {
   using T = Gemm2Traits<STAGES>;
+  constexpr int kEpi = gemm2_epi_warps<FUSED>();
+  constexpr int kEpiThreads = 32 * kEpi;
+  constexpr int kChunksPerWarp = 8 * 4 / kEpi;  // 32-column chunks of the 256 per warp
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* s_a = smem;
@@ -89,8 +107,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(gemm_block_threads<F
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   volatile uint32_t* epoch_slot = reinterpret_cast<volatile uint32_t*>(abort_flag + 2);
   uint8_t* staging = reinterpret_cast<uint8_t*>(bars) + T::kBarrierBytes;
-  float* scale_stage = reinterpret_cast<float*>(staging + T::kStagingBytes);  // [2][256] sb, then [2][256] bias
-  FusedState* sigq = reinterpret_cast<FusedState*>(staging + T::kStagingBytes + T::kScaleBytes);
+  float* scale_stage = reinterpret_cast<float*>(staging + T::staging_bytes(FUSED));  // [2][256] sb, [2][256] bias
+  FusedState* sigq = reinterpret_cast<FusedState*>(staging + T::staging_bytes(FUSED) + T::kScaleBytes);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -108,7 +126,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(gemm_block_threads<F
     }
     for (int s = 0; s < 2; ++s) {
       dev::mbar_init(dev::smem_u32(acc_full + s), 1);
-      dev::mbar_init(dev::smem_u32(acc_empty + s), 256);  // 128 epilogue threads of each CTA
+      dev::mbar_init(dev::smem_u32(acc_empty + s), 2 * kEpiThreads);  // the epilogue threads of both CTAs
     }
     dev::mbar_init(dev::smem_u32(drain), 1);
     *abort_flag = 0;
@@ -224,13 +242,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(gemm_block_threads<F
         if (args.err) atomicOr(args.err, kErrGemmDrain);
       }
     }
-  } else if (warp < kGemmWarps) {
+  } else if (warp < 2 + kEpi) {
     // ------------------------------------------------------------ epilogue
     dev::griddep_wait();
     if constexpr (FUSED) epoch = dev::ld_relaxed_gpu(dev::ctrl_ptr(cv.base[cv.rank])) + 1u;
     const size_t my_slot = kHeaderBytes + static_cast<size_t>(epoch & 1u) * cv.half_bytes +
                            static_cast<size_t>(cv.rank) * cv.slot_bytes;
-    uint4* stg = reinterpret_cast<uint4*>(staging + (warp & 3) * 2048);
+    uint4* stg = reinterpret_cast<uint4*>(staging + (warp - 2) * 2048);
     int cur_m0 = 0, cur_hm = 1, cur_n0 = 0, cur_tile = 0;
     auto emit16 = [&](int, int n, const uint4& val) { stg[stage_slot(lane, (n & 31) >> 3)] = val; };
     auto push_chunk = [&](int c) {
@@ -258,7 +276,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(gemm_block_threads<F
         __syncwarp();
       }
     };
-    const int quarter = warp & 3;
+    const int quarter = warp & 3;                        // TMEM lane quarter (warp id mod 4)
+    const int c0 = ((warp - 2) / 4) * kChunksPerWarp;    // first of this warp's column chunks
     const int row_in_tile = quarter * 32 + lane;
     const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
     const int et = threadIdx.x - 64;
@@ -289,22 +308,23 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(gemm_block_threads<F
       ++blk;
       const bool ok = dev::mbar_wait(dev::smem_u32(acc_full + acc), acc_phase, abort_flag, args.err, kErrGemmWait,
                                      tmo);
-      if (dev::named_bar_or(1, 128, !ok)) {
+      if (dev::named_bar_or(1, kEpiThreads, !ok)) {
         aborted = true;
         break;
       }
       dev::tc_fence_after();
       const uint32_t t_acc = tmem_base + lane_base + static_cast<uint32_t>(acc * T::kAccCols);
       uint32_t vn[32];
-      dev::tmem_ld32(t_acc, vn);  // chunk c + 1 loads while chunk c is processed
+      dev::tmem_ld32(t_acc + c0 * 32, vn);  // chunk c + 1 loads while chunk c is processed
 #pragma unroll 1
-      for (int c = 0; c < 8; ++c) {
+      for (int c = c0; c < c0 + kChunksPerWarp; ++c) {
         uint32_t v[32];
         dev::tmem_wait_ld(vn);
 #pragma unroll
         for (int q = 0; q < 32; ++q) v[q] = vn[q];
-        if (c < 7) dev::tmem_ld32(t_acc + (c + 1) * 32, vn);
-        if (c == 7) {
+        const bool last = c == c0 + kChunksPerWarp - 1;
+        if (!last) dev::tmem_ld32(t_acc + (c + 1) * 32, vn);
+        if (last) {
           dev::tc_fence_before();
           const uint32_t bar = dev::smem_u32(acc_empty + acc);
           if (half == 0) {
@@ -325,7 +345,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(gemm_block_threads<F
       if constexpr (FUSED) {
         if (real) {
           // every epilogue thread's pushes of the tile precede the hand-over
-          dev::named_bar_sync(1, 128);
+          dev::named_bar_sync(1, kEpiThreads);
           if (et == 0 && !signal_handover(sigq, sig_n, tile, args.err, tmo)) *abort_flag = 1;
         }
       }
