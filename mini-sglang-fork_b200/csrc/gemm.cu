@@ -118,6 +118,8 @@ int dispatch_variant(const GemmPlan& p, const CUtensorMap& tw, const CUtensorMap
   switch (p.variant) {
     case 1: return launch_variant<256, 4, false, FUSED>(p, tw, tn, args, cv, stream);
     case 2: return launch_variant<128, 6, false, FUSED>(p, tw, tn, args, cv, stream);
+    // (a 5-stage decode ring, small enough for the next decode GEMM's CTA to
+    // become resident beside this one, measured slower per decode step)
     case 3: return launch_variant<16, 10, true, FUSED>(p, tw, tn, args, cv, stream);
     case 4: return launch_variant<32, 9, true, FUSED>(p, tw, tn, args, cv, stream);
     case 5: return launch_variant<64, 8, true, FUSED>(p, tw, tn, args, cv, stream);

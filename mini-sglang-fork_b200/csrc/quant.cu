@@ -8,13 +8,10 @@
 // K (+4) bytes out per row.  Paths, by shape:
 //   few rows (decode):        one row per cluster of 2..8 CTAs, the absmax
 //                             meeting in distributed shared memory;
-//   many rows <= 16384 wide   1, 2 or 4 warps per row, in registers, no
-//   (SiLU*mul: <= 8192):      CTA-wide barrier, persistent grid;
-//   many wide SiLU*mul rows:  a persistent pipeline, gate/up chunks streamed
-//                             by bulk copies into a shared-memory ring while
-//                             the product row stays in shared memory;
-//   otherwise:                one CTA per row, in registers (<= 1024 vectors)
-//                             or staged in shared memory.
+//   many plain rows          1, 2 or 4 warps per row in registers, no
+//   (<= 16384 wide):          CTA-wide barrier, persistent grid;
+//   otherwise (SiLU*mul       one CTA per row, in registers (<= 1024 vectors)
+//   rows among them):         or staged in shared memory.
 // Arithmetic convention (bit-exact with the CPU oracle):
 //   s = fp32(amax) / 127.0f (IEEE divide), q = clamp(rint_even(x / s), +-127),
 //   q = 0 for an all-zero row.
@@ -112,16 +109,16 @@ __device__ __noinline__ uint2 quant_vec8_div(uint4 raw, float s) {
   return make_uint2(pack4_s8(q[0], q[1], q[2], q[3]), pack4_s8(q[4], q[5], q[6], q[7]));
 }
 
-// Eight bf16 values -> eight int8 (packed little-endian in a uint2).  Two
-// lanes at a time in packed f32x2 arithmetic (each lane correctly rounded, as
-// the scalar operations are).
-__device__ __forceinline__ uint2 quant_vec8(const uint4& raw, const RowScale& rs) {
-  if (rs.exact) return quant_vec8_div(raw, rs.s);
+// Eight bf16 values -> eight int8 (packed little-endian in a uint2), without
+// a branch: `band` is set when a value lies in the band (the result must then
+// be replaced by quant_vec8_div's).  Two lanes at a time in packed f32x2
+// arithmetic (each lane correctly rounded, as the scalar operations are).
+__device__ __forceinline__ uint2 quant_vec8_fast(const uint4& raw, float inv, bool& band) {
   const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw);
-  const float2 inv2 = make_float2(rs.inv, rs.inv);
+  const float2 inv2 = make_float2(inv, inv);
   const float2 rnd = make_float2(kRound, kRound), m1 = make_float2(-1.0f, -1.0f);
   uint32_t q[8];
-  bool band = false;
+  band = false;
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
     const float2 v = __bfloat1622float2(h[j]);
@@ -132,8 +129,14 @@ __device__ __forceinline__ uint2 quant_vec8(const uint4& raw, const RowScale& rs
     q[2 * j] = __float_as_uint(t.x);
     q[2 * j + 1] = __float_as_uint(t.y);
   }
-  if (band) return quant_vec8_div(raw, rs.s);
   return make_uint2(pack4_s8(q[0], q[1], q[2], q[3]), pack4_s8(q[4], q[5], q[6], q[7]));
+}
+
+__device__ __forceinline__ uint2 quant_vec8(const uint4& raw, const RowScale& rs) {
+  if (rs.exact) return quant_vec8_div(raw, rs.s);
+  bool band;
+  const uint2 r = quant_vec8_fast(raw, rs.inv, band);
+  return band ? quant_vec8_div(raw, rs.s) : r;
 }
 
 // max |x| over eight bf16 values, compared as bf16 pairs (exact: a maximum
@@ -174,10 +177,13 @@ __device__ __forceinline__ float rcp_approx(float x) {
   return y;
 }
 
-// 2^x with the MUFU ex2 unit (relative error ~2^-22 over the range used here).
+// 2^x with the MUFU ex2 unit (relative error ~2^-22 over the range used
+// here), subnormal inputs and results flushed to zero: d = 1 + 2^x rounds to
+// 1 for any 2^x below 2^-24 and for any |x| below 2^-24, so the flush never
+// changes d.
 __device__ __forceinline__ float ex2_approx(float x) {
   float y;
-  asm("ex2.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
 }
 
@@ -212,24 +218,28 @@ __device__ __noinline__ uint4 silu_mul_vec8_exact(uint4 graw, uint4 uraw) {
 // ~1e-7 relative error, and in all ~1e-6 at |g| = 20, far below the bf16
 // rounding step (2^-8) -- the fused product differs from the CPU's in the last
 // bf16 bit on a small fraction of elements, never by more.  Then the fast
-// divide, and the two multiplies as packed f32x2 arithmetic.
+// divide, and the two multiplies as packed f32x2 arithmetic.  The fast divide
+// is safe when every gate value of the vector is >= -87: then
+// -g log2 e <= 125.52 and d < 2^126; the vector's minimum gate is taken on the
+// bf16 pairs (three min instructions and one compare per eight values).
 __device__ __forceinline__ uint4 silu_mul_vec8(const uint4& graw, const uint4& uraw) {
   const __nv_bfloat162* g = reinterpret_cast<const __nv_bfloat162*>(&graw);
   const __nv_bfloat162* u = reinterpret_cast<const __nv_bfloat162*>(&uraw);
   uint4 out;
   __nv_bfloat162* o = reinterpret_cast<__nv_bfloat162*>(&out);
-  bool huge = false;
+  const __nv_bfloat162 gmin = __hmin2(__hmin2(g[0], g[1]), __hmin2(g[2], g[3]));
+  // (a NaN gate drops out of the minimum; both paths give NaN for it)
+  const bool safe = __hbge2(gmin, __float2bfloat162_rn(-87.0f));
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
     const float2 gf = __bfloat1622float2(g[j]);
     const float2 uf = __bfloat1622float2(u[j]);
     const float2 a = __fmul2_rn(gf, make_float2(kNegLog2e, kNegLog2e));
     const float2 d = __fadd2_rn(make_float2(ex2_approx(a.x), ex2_approx(a.y)), make_float2(1.0f, 1.0f));
-    huge |= (d.x > 0x1p126f) | (d.y > 0x1p126f);
     const float2 y = __fmul2_rn(__fmul2_rn(gf, make_float2(rcp_approx(d.x), rcp_approx(d.y))), uf);
     o[j] = __floats2bfloat162_rn(y.x, y.y);
   }
-  if (huge) return silu_mul_vec8_exact(graw, uraw);
+  if (!safe) return silu_mul_vec8_exact(graw, uraw);
   return out;
 }
 
@@ -340,7 +350,7 @@ __global__ void __launch_bounds__(kRegThreads) rows_reg_kernel(const __nv_bfloat
 
 // Shared-memory path: the row (or the SiLU*mul product) is staged on chip.
 template <bool SILU>
-__global__ void __launch_bounds__(kSmemThreads) rows_smem_kernel(const __nv_bfloat16* __restrict__ in, int64_t ld,
+__global__ void __launch_bounds__(kSmemThreads, 2) rows_smem_kernel(const __nv_bfloat16* __restrict__ in, int64_t ld,
                                                                  int8_t* __restrict__ q, float* __restrict__ scale,
                                                                  __nv_bfloat16* __restrict__ y_out, int width) {
   extern __shared__ uint4 stage[];
@@ -386,28 +396,25 @@ __global__ void __launch_bounds__(kSmemThreads) rows_smem_kernel(const __nv_bflo
   if (threadIdx.x == 0) scale[row] = rs.s;
 }
 
-// Warp-group path (many rows of at most 16384 values; SiLU*mul rows of at
-// most 8192): G warps (G = 1, 2 or 4) own a row, lane t of the group
-// (t < 32 G) holding vectors t + 32 G j, j < VPT, in registers, so every
-// load is a coalesced 128-bit access and all of a lane's loads are in flight
-// together.  The row's absmax is a warp-shuffle reduction plus, for G > 1,
-// one exchange through shared memory under a named barrier of the group's
-// own warps: no CTA-wide barrier, so rows never wait for one another.  The
-// grid is persistent (as many CTAs as are resident at once), group g taking
-// rows g, g + groups, ...
+// Warp-group path (the plain quantiser, many rows of at most 16384 values):
+// G warps (G = 1, 2 or 4) own a row, lane t of the group (t < 32 G) holding
+// vectors t + 32 G j, j < VPT, in registers, so every load is a coalesced
+// 128-bit access and all of a lane's loads are in flight together.  Each
+// group loops over rows g, g + groups, ... (persistent grid; a second row
+// buffer in registers, to load the next row while one is computed, measured
+// slower: the extra registers cost more resident groups than the overlap
+// gains).  The row's absmax is a warp-shuffle reduction plus,
+// for G > 1, one exchange through shared memory under a named barrier of the
+// group's own warps: no CTA-wide barrier, so rows never wait for one another.
 constexpr int kWarpThreads = 128;  // 4 warps: groups of G = 1, 2 or 4 (at most 2 groups take a barrier)
 #ifndef W8A8_WARP_MAX_VPT
-#define W8A8_WARP_MAX_VPT 16  // plain rows: vectors per lane before G doubles
-#endif
-#ifndef W8A8_WARP_MAX_VPT_SILU
-#define W8A8_WARP_MAX_VPT_SILU 8  // SiLU*mul rows also hold the gate and up loads
+#define W8A8_WARP_MAX_VPT 10  // vectors per lane before G doubles
 #endif
 
-template <int VPT, int G, bool SILU>
+template <int VPT, int G>
 __global__ void __launch_bounds__(kWarpThreads) rows_warp_kernel(const __nv_bfloat16* __restrict__ in, int64_t ld,
                                                                  int8_t* __restrict__ q, float* __restrict__ scale,
-                                                                 __nv_bfloat16* __restrict__ y_out, int64_t M,
-                                                                 int width) {
+                                                                 int64_t M, int width) {
   constexpr int kGroups = kWarpThreads / 32 / G;
   __shared__ float part[2][kWarpThreads / 32];  // per-warp maxima, by row parity
   w8a8::dev::griddep_launch();  // early trigger, as in rows_reg_kernel
@@ -416,40 +423,23 @@ __global__ void __launch_bounds__(kWarpThreads) rows_warp_kernel(const __nv_bflo
   const int t = (warp % G) * 32 + lane;
   const int nvec = width >> 3;
   const int64_t stride = static_cast<int64_t>(gridDim.x) * kGroups;
+  auto load = [&](int64_t r, uint4 (&dst)[VPT]) {
+    const uint4* src = reinterpret_cast<const uint4*>(in + r * ld);
+#pragma unroll
+    for (int j = 0; j < VPT; ++j) {
+      const int vi = t + j * 32 * G;
+      dst[j] = vi < nvec ? __ldcs(src + vi) : make_uint4(0u, 0u, 0u, 0u);
+    }
+  };
   w8a8::dev::griddep_wait();  // the rows are the previous kernel's output
   int it = 0;
   for (int64_t row = static_cast<int64_t>(blockIdx.x) * kGroups + grp; row < M; row += stride, ++it) {
-    const RowSrc<SILU> src(in, row, ld, width);
     uint4 v[VPT];
+    load(row, v);
     __nv_bfloat162 m2 = __float2bfloat162_rn(0.0f);
-    if constexpr (SILU) {
-      uint4 u[VPT];
 #pragma unroll
-      for (int j = 0; j < VPT; ++j) {
-        const int vi = t + j * 32 * G;
-        if (vi < nvec) src.fetch(vi, v[j], u[j]);
-      }
-#pragma unroll
-      for (int j = 0; j < VPT; ++j) {
-        const int vi = t + j * 32 * G;
-        if (vi < nvec) {
-          v[j] = silu_mul_vec8(v[j], u[j]);
-          m2 = vec8_absmax2(v[j], m2);
-        }
-      }
-    } else {
-#pragma unroll
-      for (int j = 0; j < VPT; ++j) {
-        const int vi = t + j * 32 * G;
-        if (vi < nvec) {
-          uint4 unused;
-          src.fetch(vi, v[j], unused);
-        }
-      }
-#pragma unroll
-      for (int j = 0; j < VPT; ++j)
-        if (t + j * 32 * G < nvec) m2 = vec8_absmax2(v[j], m2);
-    }
+    for (int j = 0; j < VPT; ++j)
+      if (t + j * 32 * G < nvec) m2 = vec8_absmax2(v[j], m2);
     float amax = warp_max(absmax_of(m2));
     if constexpr (G > 1) {
       float* p = &part[it & 1][grp * G];
@@ -464,156 +454,10 @@ __global__ void __launch_bounds__(kWarpThreads) rows_warp_kernel(const __nv_bflo
     }
     const RowScale rs = row_scale(amax);
     uint2* qr = reinterpret_cast<uint2*>(q + row * static_cast<int64_t>(width));
-    uint4* yr = SILU && y_out ? reinterpret_cast<uint4*>(y_out + row * static_cast<int64_t>(width)) : nullptr;
 #pragma unroll
     for (int j = 0; j < VPT; ++j) {
       const int vi = t + j * 32 * G;
-      if (vi < nvec) {
-        qr[vi] = quant_vec8(v[j], rs);
-        if (SILU && yr) yr[vi] = v[j];
-      }
-    }
-    if (t == 0) scale[row] = rs.s;
-  }
-}
-
-// SiLU*mul pipeline (many wide gate_up rows): persistent CTAs, one per SM.
-// A producer warp streams each row's gate and up halves in chunks of
-// kPipeChunk vectors into a ring of shared-memory stages with 1-D bulk copies
-// (cp.async.bulk, completing on a `full` mbarrier per stage) and reuses a
-// stage once every consumer warp has arrived on its `empty` mbarrier.  CONS
-// consumer threads turn each chunk into y = bf16(silu(g) * u), keep y in a
-// row buffer in shared memory and fold it into a running absmax; at the end
-// of the row one named barrier of the consumers reduces the absmax and each
-// consumer quantises the vectors it computed itself (vector i belongs to
-// thread i mod CONS in both phases, so the row buffer needs no barrier of its
-// own).  The producer meanwhile keeps loading the next row, so HBM reads do
-// not stop during the reduction and the quantisation.
-// Waits are bounded; on expiry the kernel records the error, every role
-// leaves its loop, and the producer waits (bounded) for its copies in flight.
-constexpr int kPipeChunk = 512;                // vectors (16 B) of gate, and of up, per stage
-constexpr int kPipeStageBytes = 2 * kPipeChunk * 16;
-constexpr int kPipeMaxStages = 8;
-constexpr int kPipeSmemLimit = 220 * 1024;
-
-template <int CONS>
-__global__ void __launch_bounds__(CONS + 32, 1) silu_pipe_kernel(const __nv_bfloat16* __restrict__ in, int64_t ld,
-                                                                 int8_t* __restrict__ q, float* __restrict__ scale,
-                                                                 __nv_bfloat16* __restrict__ y_out, int64_t M,
-                                                                 int width, int stages, unsigned int* err,
-                                                                 long long timeout_ns) {
-  constexpr int kConsWarps = CONS / 32;
-  constexpr int kVpc = kPipeChunk / CONS;  // vectors per consumer thread per chunk
-  extern __shared__ __align__(128) uint4 pipe_smem[];
-  __shared__ uint64_t full[kPipeMaxStages], empty[kPipeMaxStages];
-  __shared__ float red[2][kConsWarps];
-  __shared__ int abort_flag;
-  w8a8::dev::griddep_launch();  // early trigger, as in rows_reg_kernel
-  const int nvec = width >> 3;
-  const int nchunk = (nvec + kPipeChunk - 1) / kPipeChunk;
-  uint4* ring = pipe_smem;
-  uint4* yrow = pipe_smem + static_cast<size_t>(stages) * 2 * kPipeChunk;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t G = gridDim.x;
-  if (threadIdx.x == 0) {
-    for (int i = 0; i < stages; ++i) {
-      w8a8::dev::mbar_init(w8a8::dev::smem_u32(&full[i]), 1);
-      w8a8::dev::mbar_init(w8a8::dev::smem_u32(&empty[i]), kConsWarps);
-    }
-    abort_flag = 0;
-    w8a8::dev::fence_mbar_init();
-  }
-  __syncthreads();
-  w8a8::dev::griddep_wait();  // gate_up is the previous kernel's output
-  if (warp == kConsWarps) {
-    // ------------------------------------------------------------- producer
-    if (lane == 0) {
-      const uint64_t policy = w8a8::dev::policy_evict_first();
-      uint32_t k = 0;
-      bool ok = true;
-      for (int64_t row = blockIdx.x; ok && row < M; row += G) {
-        const __nv_bfloat16* src = in + row * ld;
-        for (int c = 0; c < nchunk; ++c, ++k) {
-          const int st = static_cast<int>(k % static_cast<uint32_t>(stages));
-          const uint32_t ph = (k / static_cast<uint32_t>(stages)) & 1u;
-          if (k >= static_cast<uint32_t>(stages) &&
-              !w8a8::dev::mbar_wait(w8a8::dev::smem_u32(&empty[st]), ph ^ 1u, &abort_flag, err, w8a8::kErrGemmWait,
-                                    timeout_ns)) {
-            ok = false;
-            break;
-          }
-          const int n = nvec - c * kPipeChunk < kPipeChunk ? nvec - c * kPipeChunk : kPipeChunk;
-          const uint32_t bytes = static_cast<uint32_t>(n) * 16u;
-          const uint32_t bar = w8a8::dev::smem_u32(&full[st]);
-          w8a8::dev::mbar_expect_tx(bar, 2u * bytes);
-          uint4* dst = ring + static_cast<size_t>(st) * 2 * kPipeChunk;
-          w8a8::dev::bulk_load_1d(w8a8::dev::smem_u32(dst), src + static_cast<int64_t>(c) * kPipeChunk * 8, bytes,
-                                  bar, policy);
-          w8a8::dev::bulk_load_1d(w8a8::dev::smem_u32(dst + kPipeChunk),
-                                  src + width + static_cast<int64_t>(c) * kPipeChunk * 8, bytes, bar, policy);
-        }
-      }
-      // Copies may still be landing (after an abort, they may have no
-      // consumer): wait (bounded) for the last copy issued into every stage
-      // before the CTA's shared memory can be released.
-      const uint32_t first = k > static_cast<uint32_t>(stages) ? k - static_cast<uint32_t>(stages) : 0u;
-      for (uint32_t i = first; i < k; ++i) {
-        const int st = static_cast<int>(i % static_cast<uint32_t>(stages));
-        if (!w8a8::dev::mbar_wait_drain(w8a8::dev::smem_u32(&full[st]), (i / static_cast<uint32_t>(stages)) & 1u,
-                                        timeout_ns) && err)
-          atomicOr(err, w8a8::kErrGemmDrain);
-      }
-    }
-    return;
-  }
-  // --------------------------------------------------------------- consumers
-  const int t = threadIdx.x;
-  uint32_t k = 0;
-  int it = 0;
-  for (int64_t row = blockIdx.x; row < M; row += G, ++it) {
-    __nv_bfloat162 m2 = __float2bfloat162_rn(0.0f);
-    bool ok = true;
-    for (int c = 0; c < nchunk; ++c, ++k) {
-      const int st = static_cast<int>(k % static_cast<uint32_t>(stages));
-      const uint32_t ph = (k / static_cast<uint32_t>(stages)) & 1u;
-      // lane 0 waits for the stage and tells its warp (the warp stays
-      // converged, also on a timeout); every lane then tests the completed
-      // phase once, which gives it the acquire of the copied bytes
-      bool got = true;
-      if (lane == 0)
-        got = w8a8::dev::mbar_wait(w8a8::dev::smem_u32(&full[st]), ph, &abort_flag, err, w8a8::kErrGemmWait,
-                                   timeout_ns);
-      if (!__shfl_sync(0xffffffffu, got, 0)) {
-        ok = false;
-        break;
-      }
-      (void)w8a8::dev::mbar_test(w8a8::dev::smem_u32(&full[st]), ph);
-      const uint4* gs = ring + static_cast<size_t>(st) * 2 * kPipeChunk;
-#pragma unroll
-      for (int j = 0; j < kVpc; ++j) {
-        const int i = t + j * CONS;
-        const int vi = c * kPipeChunk + i;
-        if (vi < nvec) {
-          const uint4 y = silu_mul_vec8(gs[i], gs[kPipeChunk + i]);
-          yrow[vi] = y;
-          m2 = vec8_absmax2(y, m2);
-        }
-      }
-      __syncwarp();
-      if (lane == 0) w8a8::dev::mbar_arrive(w8a8::dev::smem_u32(&empty[st]));
-    }
-    float amax = warp_max(absmax_of(m2));
-    if (lane == 0) red[it & 1][warp] = amax;
-    if (w8a8::dev::named_bar_or(1, CONS, !ok)) break;  // an abort anywhere ends every consumer here
-#pragma unroll
-    for (int w = 0; w < kConsWarps; ++w) amax = fmaxf(amax, red[it & 1][w]);
-    const RowScale rs = row_scale(amax);
-    uint2* qr = reinterpret_cast<uint2*>(q + row * static_cast<int64_t>(width));
-    uint4* yr = y_out ? reinterpret_cast<uint4*>(y_out + row * static_cast<int64_t>(width)) : nullptr;
-    for (int vi = t; vi < nvec; vi += CONS) {
-      const uint4 y = yrow[vi];
-      qr[vi] = quant_vec8(y, rs);
-      if (yr) yr[vi] = y;
+      if (vi < nvec) qr[vi] = quant_vec8(v[j], rs);
     }
     if (t == 0) scale[row] = rs.s;
   }
@@ -865,97 +709,48 @@ int resident_ctas(Kernel kernel, int threads, size_t smem) {
   return cached[dev];
 }
 
-template <int VPT, int G, bool SILU>
-cudaError_t launch_warp_rows(const __nv_bfloat16* in, int64_t ld, int8_t* q, float* scale, __nv_bfloat16* y,
-                             int64_t M, int width, int nsm, cudaStream_t s) {
+template <int VPT, int G>
+cudaError_t launch_warp_rows(const __nv_bfloat16* in, int64_t ld, int8_t* q, float* scale, int64_t M, int width,
+                             int nsm, cudaStream_t s) {
   constexpr int kGroups = kWarpThreads / 32 / G;
-  const int per_sm = resident_ctas(rows_warp_kernel<VPT, G, SILU>, kWarpThreads, 0);
+  const int per_sm = resident_ctas(rows_warp_kernel<VPT, G>, kWarpThreads, 0);
   int64_t grid = (M + kGroups - 1) / kGroups;
   const int64_t cap = static_cast<int64_t>(nsm) * per_sm;
   if (grid > cap) grid = cap;
-  return w8a8::launch_pdl(rows_warp_kernel<VPT, G, SILU>, dim3(static_cast<unsigned>(grid)), dim3(kWarpThreads), 0,
-                          s, in, ld, q, scale, y, M, width);
+  return w8a8::launch_pdl(rows_warp_kernel<VPT, G>, dim3(static_cast<unsigned>(grid)), dim3(kWarpThreads), 0, s,
+                          in, ld, q, scale, M, width);
 }
 
-// Vectors per lane rounded up to an instantiated count (plain rows: 2, 4, 8,
-// 10, 12, 16; SiLU*mul rows: 2, 4, 6, 8).
-template <int G, bool SILU>
-cudaError_t launch_warp_rows_vpt(int vpt, const __nv_bfloat16* in, int64_t ld, int8_t* q, float* scale,
-                                 __nv_bfloat16* y, int64_t M, int width, int nsm, cudaStream_t s) {
-  if constexpr (SILU) {
-    if (vpt <= 2) return launch_warp_rows<2, G, SILU>(in, ld, q, scale, y, M, width, nsm, s);
-    if (vpt <= 4) return launch_warp_rows<4, G, SILU>(in, ld, q, scale, y, M, width, nsm, s);
-    if (vpt <= 6) return launch_warp_rows<6, G, SILU>(in, ld, q, scale, y, M, width, nsm, s);
-    return launch_warp_rows<8, G, SILU>(in, ld, q, scale, y, M, width, nsm, s);
-  } else {
-    if (vpt <= 2) return launch_warp_rows<2, G, SILU>(in, ld, q, scale, y, M, width, nsm, s);
-    if (vpt <= 4) return launch_warp_rows<4, G, SILU>(in, ld, q, scale, y, M, width, nsm, s);
-    if (vpt <= 8) return launch_warp_rows<8, G, SILU>(in, ld, q, scale, y, M, width, nsm, s);
-    if (vpt <= 10) return launch_warp_rows<10, G, SILU>(in, ld, q, scale, y, M, width, nsm, s);
-    if (vpt <= 12) return launch_warp_rows<12, G, SILU>(in, ld, q, scale, y, M, width, nsm, s);
-    return launch_warp_rows<16, G, SILU>(in, ld, q, scale, y, M, width, nsm, s);
-  }
+// Vectors per lane rounded up to an instantiated count (2, 4, 6, 8, 10, 12, 16).
+template <int G>
+cudaError_t launch_warp_rows_vpt(int vpt, const __nv_bfloat16* in, int64_t ld, int8_t* q, float* scale, int64_t M,
+                                 int width, int nsm, cudaStream_t s) {
+  if (vpt <= 2) return launch_warp_rows<2, G>(in, ld, q, scale, M, width, nsm, s);
+  if (vpt <= 4) return launch_warp_rows<4, G>(in, ld, q, scale, M, width, nsm, s);
+  if (vpt <= 6) return launch_warp_rows<6, G>(in, ld, q, scale, M, width, nsm, s);
+  if (vpt <= 8) return launch_warp_rows<8, G>(in, ld, q, scale, M, width, nsm, s);
+  if (vpt <= 10) return launch_warp_rows<10, G>(in, ld, q, scale, M, width, nsm, s);
+  if (vpt <= 12) return launch_warp_rows<12, G>(in, ld, q, scale, M, width, nsm, s);
+  return launch_warp_rows<16, G>(in, ld, q, scale, M, width, nsm, s);
 }
 
 // Warps per row for the warp-group path: the fewest (1, 2 or 4) that keep a
 // lane's vectors within the target; 0 when the row is too wide for 4 warps.
-template <bool SILU>
-int warp_group_size(int nvec) {
-  const int target = SILU ? W8A8_WARP_MAX_VPT_SILU : W8A8_WARP_MAX_VPT;
-  const int limit = SILU ? 8 : 16;
+inline int warp_group_size(int nvec) {
   for (int g = 1; g <= 4; g *= 2)
-    if ((nvec + 32 * g - 1) / (32 * g) <= target) return g;
-  return (nvec + 127) / 128 <= limit ? 4 : 0;
+    if ((nvec + 32 * g - 1) / (32 * g) <= W8A8_WARP_MAX_VPT) return g;
+  return (nvec + 127) / 128 <= 16 ? 4 : 0;
 }
 
-template <bool SILU>
-int launch_warp_group(const __nv_bfloat16* in, int64_t ld, int8_t* q, float* scale, __nv_bfloat16* y, int64_t M,
-                      int width, int g, int nsm, cudaStream_t s) {
+int launch_warp_group(const __nv_bfloat16* in, int64_t ld, int8_t* q, float* scale, int64_t M, int width, int g,
+                      int nsm, cudaStream_t s) {
   const int nvec = width / 8;
   const int vpt = (nvec + 32 * g - 1) / (32 * g);
   switch (g) {
-    case 1: W8A8_CUDA_TRY((launch_warp_rows_vpt<1, SILU>(vpt, in, ld, q, scale, y, M, width, nsm, s))); break;
-    case 2: W8A8_CUDA_TRY((launch_warp_rows_vpt<2, SILU>(vpt, in, ld, q, scale, y, M, width, nsm, s))); break;
-    default: W8A8_CUDA_TRY((launch_warp_rows_vpt<4, SILU>(vpt, in, ld, q, scale, y, M, width, nsm, s))); break;
+    case 1: W8A8_CUDA_TRY(launch_warp_rows_vpt<1>(vpt, in, ld, q, scale, M, width, nsm, s)); break;
+    case 2: W8A8_CUDA_TRY(launch_warp_rows_vpt<2>(vpt, in, ld, q, scale, M, width, nsm, s)); break;
+    default: W8A8_CUDA_TRY(launch_warp_rows_vpt<4>(vpt, in, ld, q, scale, M, width, nsm, s)); break;
   }
-  return W8A8_OK;
-}
-
-#ifndef W8A8_PIPE_CONS
-#define W8A8_PIPE_CONS 256  // consumer threads of the SiLU*mul pipeline (256 or 512)
-#endif
-
-// Stages of the SiLU*mul pipeline for rows of nvec output vectors (0 = the
-// row buffer leaves room for fewer than two stages).
-inline int silu_pipe_stages(int nvec) {
-  const int room = kPipeSmemLimit - nvec * 16;
-  int st = room / kPipeStageBytes;
-  return st < 2 ? 0 : (st > kPipeMaxStages ? kPipeMaxStages : st);
-}
-
-int launch_silu_pipe(const __nv_bfloat16* in, int64_t ld, int8_t* q, float* scale, __nv_bfloat16* y, int64_t M,
-                     int width, int nsm, cudaStream_t s) {
-  const int nvec = width / 8;
-  const int stages = silu_pipe_stages(nvec);
-  const size_t smem = static_cast<size_t>(stages) * kPipeStageBytes + static_cast<size_t>(nvec) * 16;
-  unsigned int* err = w8a8::device_error_word();
-  if (!err) return W8A8_ERR_CUDA;
-  static std::mutex mu;
-  static bool configured[64] = {false};
-  const int dev = w8a8::current_device();
-  W8A8_REQUIRE(dev >= 0 && dev < 64, W8A8_ERR_CUDA, "no current device");
-  {
-    std::lock_guard<std::mutex> lk(mu);
-    if (!configured[dev]) {
-      W8A8_CUDA_TRY(cudaFuncSetAttribute(silu_pipe_kernel<W8A8_PIPE_CONS>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, kPipeSmemLimit));
-      configured[dev] = true;
-    }
-  }
-  const int64_t grid = M < nsm ? M : nsm;
-  W8A8_CUDA_TRY(w8a8::launch_pdl(silu_pipe_kernel<W8A8_PIPE_CONS>, dim3(static_cast<unsigned>(grid)),
-                                 dim3(W8A8_PIPE_CONS + 32), smem, s, in, ld, q, scale, y, M, width, stages, err,
-                                 w8a8::kDefaultGemmTimeoutNs));
   return W8A8_OK;
 }
 
@@ -968,12 +763,10 @@ int launch_rows(const __nv_bfloat16* in, int64_t ld, int8_t* q, float* scale, __
   if (nsm <= 0) nsm = 148;
   const int csize = row_cluster_size(M, nvec, nsm);
   const bool aligned = (reinterpret_cast<uintptr_t>(in) & 15u) == 0 && ld % 8 == 0;
-  if (csize == 0 && aligned) {
-    // many rows: warp groups per row (plain rows, narrow SiLU*mul rows), or
-    // the bulk-copy pipeline for wide SiLU*mul rows
-    const int g = warp_group_size<SILU>(nvec);
-    if (g > 0) return launch_warp_group<SILU>(in, ld, q, scale, y, M, width, g, nsm, s);
-    if (SILU && silu_pipe_stages(nvec) > 0) return launch_silu_pipe(in, ld, q, scale, y, M, width, nsm, s);
+  if (!SILU && csize == 0 && aligned) {
+    // many plain rows: warp groups per row
+    const int g = warp_group_size(nvec);
+    if (g > 0) return launch_warp_group(in, ld, q, scale, M, width, g, nsm, s);
   }
   if (csize > 0) {
     const int per = (nvec + csize - 1) / csize;

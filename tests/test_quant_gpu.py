@@ -219,9 +219,9 @@ def test_quant_half_integer_ties(pkg, oracle, cuda_dev):
         assert torch.equal(s.cpu(), s_ref) and torch.equal(q.cpu(), q_ref), m
 
 
-# Many SiLU*mul rows: narrow rows (at most 8192 outputs) in the warp-group
-# kernel, wide rows in the bulk-copy pipeline (chunks of 512 vectors, the last
-# one ragged for I = 25600, rows per CTA above the ring depth).
+# Many SiLU*mul rows (one CTA per row: in registers up to 8192 outputs, staged
+# in shared memory beyond), strided, with an all-zero product row and the
+# absmax at a row's last element.
 SILU_MANY = [(296, 25600), (700, 12800), (300, 12288), (4096, 3200), (500, 6400), (777, 1000), (1200, 8192),
              (2000, 25600)]
 
