@@ -113,10 +113,13 @@ struct GemmTraits {
   // both modes in the normal orientation (the epilogue transposes each chunk
   // through it so that stores are row-contiguous); weight-stationary tiles
   // store token rows directly, so a plain swap launch has no staging.
-  // double-buffered weight scales and bias of the tile's BN columns (fp32)
-  static constexpr int kScaleBytes = SWAP ? 0 : 2 * 2 * BN * 4;
+  // double-buffered scales of the tile's BN columns (fp32): weight scales and
+  // bias (normal orientation), token scales (weight-stationary)
+  static constexpr int kScaleBytes = SWAP ? 2 * BN * 4 : 2 * 2 * BN * 4;
+  // offset of the scales: a plain weight-stationary launch has no staging
+  static constexpr int scale_offset(bool fused) { return (SWAP && !fused) ? 0 : kStagingBytes; }
   static constexpr int kSmemBytesPlain =
-      1024 + STAGES * kStageBytes + kBarrierBytes + (SWAP ? 0 : kStagingBytes + kScaleBytes);
+      1024 + STAGES * kStageBytes + kBarrierBytes + (SWAP ? 0 : kStagingBytes) + kScaleBytes;
   static constexpr int kSmemBytes =
       1024 + STAGES * kStageBytes + kBarrierBytes + kStagingBytes + kScaleBytes + kSignalBytes;
   static constexpr int smem_bytes(bool fused) { return fused ? kSmemBytes : kSmemBytesPlain; }
@@ -184,82 +187,25 @@ __device__ __forceinline__ float dequant1(int32_t acc, float sa, float sb) {
   return __fmul_rn(__fmul_rn(__int2float_rn(acc), sa), sb);
 }
 
-// Dequantise CH accumulators of one TMEM row and hand the bf16 values to the
-// emitters: emit16(m, n, 8 packed values) / emit2(m, n, 1 value).
-//   normal: row = token m, the values are channels col0..col0+CH-1.
-//   swap:   row = channel n, the values are tokens col0..col0+CH-1.
-template <bool SWAP, int CH, class Emit16, class Emit2>
-__device__ __forceinline__ void store_chunk(const GemmArgs& a, int row, int col0, const uint32_t (&v)[32],
-                                            Emit16&& emit16, Emit2&& emit2) {
-  if (!SWAP) {
-    const int m = row;
-    if (m >= a.M) return;
-    const float sam = __ldg(a.sa + m);
+// Weight-stationary dequantisation of CH accumulators of TMEM row `n` (a
+// weight row): the values are tokens col0..col0+CH-1, with the row's scale
+// and bias from registers and the tokens' scales from shared memory, staged
+// before the accumulator wait (no global load after it).
+template <int CH, class Emit2>
+__device__ __forceinline__ void store_chunk_swap(const GemmArgs& a, int n, int col0, float sbn, float bnv,
+                                                 const float* sas, const uint32_t (&v)[32], Emit2&& emit2) {
+  if (n >= a.N) return;
 #pragma unroll
-    for (int g = 0; g < CH / 8; ++g) {
-      const int n = col0 + g * 8;
-      if (n >= a.N) break;  // N % 16 == 0: granules are either fully in or out
-      // the granule's eight weight scales (and bias values): two 16-byte loads
-      // (one for the bias), the same addresses in every lane of the warp
-      float sb[8], bs[8];
-      if (a.vec_scales) {
-        const float4 s0 = __ldg(reinterpret_cast<const float4*>(a.sb + n));
-        const float4 s1 = __ldg(reinterpret_cast<const float4*>(a.sb + n + 4));
-        sb[0] = s0.x; sb[1] = s0.y; sb[2] = s0.z; sb[3] = s0.w;
-        sb[4] = s1.x; sb[5] = s1.y; sb[6] = s1.z; sb[7] = s1.w;
-        if (a.bias) {
-          const uint4 braw = __ldg(reinterpret_cast<const uint4*>(a.bias + n));
-          const __nv_bfloat162* bh = reinterpret_cast<const __nv_bfloat162*>(&braw);
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const float2 f = __bfloat1622float2(bh[e]);
-            bs[2 * e] = f.x;
-            bs[2 * e + 1] = f.y;
-          }
-        }
-      } else {
-#pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          sb[e] = __ldg(a.sb + n + e);
-          if (a.bias) bs[e] = __bfloat162float(a.bias[n + e]);
-        }
-      }
-      uint4 pk;
-      __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&pk);
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const int c0 = g * 8 + 2 * j;
-        float y0 = dequant1(static_cast<int32_t>(v[c0]), sam, sb[2 * j]);
-        float y1 = dequant1(static_cast<int32_t>(v[c0 + 1]), sam, sb[2 * j + 1]);
-        if (a.bias) {
-          y0 = __fadd_rn(y0, bs[2 * j]);
-          y1 = __fadd_rn(y1, bs[2 * j + 1]);
-        }
-        h[j] = __floats2bfloat162_rn(y0, y1);
-      }
-      emit16(m, n, pk);
-      if (a.c_i32) {
-        int4* dst = reinterpret_cast<int4*>(a.c_i32 + static_cast<int64_t>(m) * a.N + n);
-        dst[0] = make_int4(v[g * 8 + 0], v[g * 8 + 1], v[g * 8 + 2], v[g * 8 + 3]);
-        dst[1] = make_int4(v[g * 8 + 4], v[g * 8 + 5], v[g * 8 + 6], v[g * 8 + 7]);
-      }
-    }
-  } else {
-    const int n = row;
-    if (n >= a.N) return;
-    const float sbn = __ldg(a.sb + n);
-    const float bn = a.bias ? __bfloat162float(a.bias[n]) : 0.0f;
-#pragma unroll
-    for (int j = 0; j < CH; ++j) {
-      const int m = col0 + j;
-      if (m >= a.M) break;
-      float y = dequant1(static_cast<int32_t>(v[j]), __ldg(a.sa + m), sbn);
-      if (a.bias) y = __fadd_rn(y, bn);
-      emit2(m, n, __float2bfloat16_rn(y));
-      if (a.c_i32) a.c_i32[static_cast<int64_t>(m) * a.N + n] = static_cast<int32_t>(v[j]);
-    }
+  for (int j = 0; j < CH; ++j) {
+    const int m = col0 + j;
+    if (m >= a.M) break;
+    float y = dequant1(static_cast<int32_t>(v[j]), sas[j], sbn);
+    if (a.bias) y = __fadd_rn(y, bnv);
+    emit2(m, n, __float2bfloat16_rn(y));
+    if (a.c_i32) a.c_i32[static_cast<int64_t>(m) * a.N + n] = static_cast<int32_t>(v[j]);
   }
 }
+
 
 // Per-warp staging of one 32-row x 32-column bf16 chunk of the output tile
 // (2 KB): row r (the lane that computed it), 16-byte piece g (8 columns) at
@@ -742,7 +688,8 @@ __global__ void __launch_bounds__(gemm_block_threads<FUSED>(), 1)
   volatile int* last_flag = abort_flag + 1;
   volatile uint32_t* epoch_slot = reinterpret_cast<volatile uint32_t*>(last_flag + 1);
   uint8_t* staging = reinterpret_cast<uint8_t*>(bars) + T::kBarrierBytes;  // 16-byte aligned
-  float* scale_stage = reinterpret_cast<float*>(staging + T::kStagingBytes);  // [2][BN] sb, then [2][BN] bias
+  // [2][BN] sb, then [2][BN] bias (normal orientation); [2][BN] sa (weight-stationary)
+  float* scale_stage = reinterpret_cast<float*>(staging + T::scale_offset(FUSED));
   FusedState* sigq = reinterpret_cast<FusedState*>(staging + T::kStagingBytes + T::kScaleBytes);
 
   const int warp = threadIdx.x >> 5;
@@ -1007,7 +954,21 @@ __global__ void __launch_bounds__(gemm_block_threads<FUSED>(), 1)
       float* sbs = scale_stage + (frag & 1u) * BN;
       float* bss = scale_stage + 2 * BN + (frag & 1u) * BN;
       float sam = 0.0f;
-      if constexpr (!SWAP) sam = stage_tile_scales(args, tn * BN, BN, et, true, row, sbs, bss);
+      // weight-stationary: this thread's weight-row scale and bias in
+      // registers, the tile's token scales staged in shared memory (sbs)
+      float sbn = 0.0f, bnv = 0.0f;
+      if constexpr (!SWAP) {
+        sam = stage_tile_scales(args, tn * BN, BN, et, true, row, sbs, bss);
+      } else {
+        if (et < BN) {
+          const int m = tn * BN + et;
+          sbs[et] = m < args.M ? __ldg(args.sa + m) : 0.0f;
+        }
+        if (row < args.N) {
+          sbn = __ldg(args.sb + row);
+          if (args.bias) bnv = __bfloat162float(args.bias[row]);
+        }
+      }
       ++frag;
       const bool ok = dev::mbar_wait(dev::smem_u32(acc_full + acc), acc_phase, abort_flag, args.err,
                                      kErrGemmWait, tmo);
@@ -1023,7 +984,7 @@ __global__ void __launch_bounds__(gemm_block_threads<FUSED>(), 1)
           store_chunk_smem(args, row, tn * BN + c * T::kChunk, sam, sbs + c * T::kChunk, bss + c * T::kChunk, v,
                            emit16);
         } else {
-          store_chunk<SWAP, T::kChunk>(args, row, tn * BN + c * T::kChunk, v, emit16, emit2);
+          store_chunk_swap<T::kChunk>(args, row, tn * BN + c * T::kChunk, sbn, bnv, sbs + c * T::kChunk, v, emit2);
         }
       };
       bool wrote_tile = true;
@@ -1048,61 +1009,89 @@ __global__ void __launch_bounds__(gemm_block_threads<FUSED>(), 1)
           out_chunk(tw, tn, c);
         }
       } else {
-        // Partial fragment: park the int32 values in this CTA's slot.  Slot
-        // layout [chunk][warp][column group j][lane][4 columns]: a thread
-        // moves its chunk as kChunk/4 16-byte stores / loads, and each warp
-        // instruction covers 512 contiguous bytes.
+        // Partial fragment of a tile cut between CTAs c_first..c_last.  The
+        // tile's owner is c_first: it holds the tile's first k-blocks at the
+        // END of its stream-K range, so it is the last to finish the tile,
+        // while every other CTA holds the tile as its FIRST fragment (or as
+        // its whole range) and never waits for anything.  A non-owner parks its
+        // int32 values in its slot (layout [chunk][warp][column group j][lane]
+        // [4 columns]: a thread moves its chunk as kChunk/4 16-byte stores, each
+        // warp instruction covers 512 contiguous bytes) and counts itself in
+        // the tile's counter; the owner waits (bounded) for the count, adds the
+        // slots to its own values, still in TMEM, and writes the tile.  The
+        // owner thus never parks its own share nor takes the counter atomic:
+        // its tail after the last MMA is one counter read and one batch of
+        // slot loads.
         const long long tile_begin = static_cast<long long>(tile) * args.kblocks;
-        const int slot = 2 * blockIdx.x + (my_begin < tile_begin ? 1 : 0);
-        int4* wslot = reinterpret_cast<int4*>(args.ws + static_cast<int64_t>(slot) * (T::kBM * BN));
-        constexpr int kVec = T::kChunk / 4;
-#pragma unroll 1
-        for (int c = 0; c < T::kChunks; ++c) {
-          uint32_t v[32];
-          dev::tmem_ld<T::kChunk>(t_acc + c * T::kChunk, v);
-          dev::tmem_wait_ld(v);
-          int4* p = wslot + ((c * 4 + quarter) * kVec) * 32 + lane;
-#pragma unroll
-          for (int j = 0; j < kVec; ++j)
-            __stcg(p + j * 32, make_int4(static_cast<int>(v[4 * j]), static_cast<int>(v[4 * j + 1]),
-                                    static_cast<int>(v[4 * j + 2]), static_cast<int>(v[4 * j + 3])));
-        }
-        __threadfence();
-        dev::named_bar_sync(1, 128);
         const int c_first = sk_owner(args, tile_begin);
         const int c_last = sk_owner(args, tile_begin + args.kblocks - 1);
-        if (et == 0) {
-          const uint32_t prev = atomicAdd(args.counters + tile, 1u);
-          *last_flag = (prev == static_cast<uint32_t>(c_last - c_first)) ? 1 : 0;
-        }
-        dev::named_bar_sync(1, 128);
-        wrote_tile = *last_flag != 0;
-        if (!wrote_tile) {
-          dev::tc_fence_before();
-          dev::mbar_arrive(dev::smem_u32(acc_empty + acc));
-        } else {
-          // Last arriver: its own share is still in TMEM (the accumulator is
-          // released only after this fix-up); add the other CTAs' slots.
-          __threadfence();
+        const int me = static_cast<int>(blockIdx.x);
+        constexpr int kVec = T::kChunk / 4;
+        if (me != c_first) {
+          const int slot = 2 * me + (my_begin < tile_begin ? 1 : 0);
+          int4* wslot = reinterpret_cast<int4*>(args.ws + static_cast<int64_t>(slot) * (T::kBM * BN));
 #pragma unroll 1
           for (int c = 0; c < T::kChunks; ++c) {
             uint32_t v[32];
             dev::tmem_ld<T::kChunk>(t_acc + c * T::kChunk, v);
             dev::tmem_wait_ld(v);
-            for (int cta = c_first; cta <= c_last; ++cta) {
-              if (cta == static_cast<int>(blockIdx.x)) continue;
-              const int s = 2 * cta + (sk_begin(args, cta) < tile_begin ? 1 : 0);
-              const int4* p = reinterpret_cast<const int4*>(args.ws + static_cast<int64_t>(s) * (T::kBM * BN)) +
-                              ((c * 4 + quarter) * kVec) * 32 + lane;
-              int4 q[kVec];
+            int4* p = wslot + ((c * 4 + quarter) * kVec) * 32 + lane;
 #pragma unroll
-              for (int j = 0; j < kVec; ++j) q[j] = __ldcg(p + j * 32);
+            for (int j = 0; j < kVec; ++j)
+              __stcg(p + j * 32, make_int4(static_cast<int>(v[4 * j]), static_cast<int>(v[4 * j + 1]),
+                                      static_cast<int>(v[4 * j + 2]), static_cast<int>(v[4 * j + 3])));
+          }
+          dev::tc_fence_before();
+          dev::mbar_arrive(dev::smem_u32(acc_empty + acc));
+          // one fence after the barrier orders every epilogue thread's slot
+          // stores (ordered before it by the barrier) before the count
+          dev::named_bar_sync(1, 128);
+          if (et == 0) {
+            __threadfence();
+            atomicAdd(args.counters + tile, 1u);
+          }
+          wrote_tile = false;
+        } else {
+          bool counted = true;
+          if (et == 0)
+            counted = dev::wait_counter(args.counters + tile, static_cast<uint32_t>(c_last - c_first), abort_flag,
+                                        args.err, kErrGemmWait, tmo);
+          if (dev::named_bar_or(1, 128, !counted)) {
+            aborted = true;
+            break;
+          }
+          __threadfence();
+          // The slots' loads are issued in batches of kBatch CTAs, all in
+          // flight together (a tile of a decode GEMM spans up to ~5 CTAs).
+          constexpr int kBatch = kVec <= 4 ? 4 : 2;
+#pragma unroll 1
+          for (int c = 0; c < T::kChunks; ++c) {
+            uint32_t v[32];
+            dev::tmem_ld<T::kChunk>(t_acc + c * T::kChunk, v);
+            dev::tmem_wait_ld(v);
+#pragma unroll 1
+            for (int cta0 = c_first + 1; cta0 <= c_last; cta0 += kBatch) {
+              int4 q[kBatch][kVec];
 #pragma unroll
-              for (int j = 0; j < kVec; ++j) {  // two's-complement sums, as int32
-                v[4 * j] += static_cast<uint32_t>(q[j].x);
-                v[4 * j + 1] += static_cast<uint32_t>(q[j].y);
-                v[4 * j + 2] += static_cast<uint32_t>(q[j].z);
-                v[4 * j + 3] += static_cast<uint32_t>(q[j].w);
+              for (int b = 0; b < kBatch; ++b) {
+                const int cta = cta0 + b;
+                if (cta > c_last) continue;
+                const int s = 2 * cta + (sk_begin(args, cta) < tile_begin ? 1 : 0);
+                const int4* p = reinterpret_cast<const int4*>(args.ws + static_cast<int64_t>(s) * (T::kBM * BN)) +
+                                ((c * 4 + quarter) * kVec) * 32 + lane;
+#pragma unroll
+                for (int j = 0; j < kVec; ++j) q[b][j] = __ldcg(p + j * 32);
+              }
+#pragma unroll
+              for (int b = 0; b < kBatch; ++b) {
+                if (cta0 + b > c_last) continue;
+#pragma unroll
+                for (int j = 0; j < kVec; ++j) {  // two's-complement sums, as int32
+                  v[4 * j] += static_cast<uint32_t>(q[b][j].x);
+                  v[4 * j + 1] += static_cast<uint32_t>(q[b][j].y);
+                  v[4 * j + 2] += static_cast<uint32_t>(q[b][j].z);
+                  v[4 * j + 3] += static_cast<uint32_t>(q[b][j].w);
+                }
               }
             }
             if (c == T::kChunks - 1) {
@@ -1114,8 +1103,6 @@ __global__ void __launch_bounds__(gemm_block_threads<FUSED>(), 1)
           }
           if (et == 0) args.counters[tile] = 0u;
         }
-        // last_flag is rewritten by the next fragment: keep every reader ahead of it
-        dev::named_bar_sync(1, 128);
       }
       if constexpr (FUSED) {
         if (wrote_tile) {

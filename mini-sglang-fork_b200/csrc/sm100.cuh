@@ -369,6 +369,34 @@ __device__ __forceinline__ uint32_t ld_acquire_cta(const uint32_t* p) {
   return v;
 }
 
+// Acquire load of a global word at GPU scope.
+__device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Bounded wait until the global counter *p reaches `target` (acquire).  On
+// expiry, or once another role of the CTA has aborted, raises the abort flag
+// and the error word and returns false.
+__device__ __forceinline__ bool wait_counter(const uint32_t* p, uint32_t target, volatile int* abort_flag,
+                                             unsigned int* err_word, unsigned int err_bit, long long timeout_ns) {
+  if (ld_acquire_gpu(p) >= target) return true;
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t it = 1;; ++it) {
+    if (ld_acquire_gpu(p) >= target) return true;
+    if ((it & 63u) == 0) {
+      if (*abort_flag) return false;
+      if (globaltimer_ns() - t0 > static_cast<uint64_t>(timeout_ns)) {
+        *abort_flag = 1;
+        if (err_word) atomicOr(err_word, err_bit);
+        return false;
+      }
+    }
+    if (it > 16) __nanosleep(64);
+  }
+}
+
 // -------------------------------------------------------- named barriers
 __device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
