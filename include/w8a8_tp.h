@@ -162,9 +162,9 @@ int w8a8_comm_create(int rank, int world, int device, size_t max_bytes, w8a8_com
                      void* handle_out);
 int w8a8_comm_open_peers(w8a8_comm* comm, const void* all_handles);
 /* Algorithm: 0 = automatic (one-shot for world 2 or small tensors, two-shot
- * otherwise; the fused GEMM's two-shot through NVLS when a multicast buffer is
- * attached), 1 = always one-shot, 2 = always two-shot (peer stores),
- * 3 = the fused GEMM's two-shot always through NVLS (needs the buffer). */
+ * with peer stores otherwise), 1 = always one-shot, 2 = always two-shot (peer
+ * stores), 3 = the fused GEMM's two-shot through NVLS (needs the multicast
+ * buffer; opt-in: measured slower than peer stores at world 2). */
 int w8a8_comm_set_mode(w8a8_comm* comm, int mode);
 
 /* Attach an NVSwitch multicast (NVLS) buffer for the fused row-parallel

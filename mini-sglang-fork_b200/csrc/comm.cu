@@ -473,11 +473,13 @@ int w8a8_gemm_allreduce(w8a8_comm* c, const int8_t* A, const int8_t* B, const fl
   const bool big = c->world >= 4 && M > 64 && bytes * (c->world - 1) > (4u << 20);
   const bool two = c->mode == 2 || c->mode == 3 || (c->mode == 0 && big);
   v.two_shot = (two && M > 64) ? 1 : 0;
-  // NVLS two-shot when a multicast buffer is attached: forced (mode 3), or
-  // automatic for the two-shot sizes at world >= 4, where reading the
-  // partials through the switch moves ~(1 + 1/p) x the output per rank and
-  // direction against 2 (p - 1) / p x for peer stores.
-  v.nvls = (v.two_shot && c->nv_mc != nullptr && (c->mode == 3 || (c->mode == 0 && big))) ? 1 : 0;
+  // NVLS two-shot only when asked for (mode 3, with a multicast buffer
+  // attached).  It moves ~(1 + 1/p) x the output per rank and direction
+  // against 2 (p - 1) / p x for peer stores, but measured at world 2 its
+  // switch-reduced loads (few in flight per thread, each a round trip through
+  // the switch) left the reduce ~4x longer than the peer-store path, so the
+  // automatic mode keeps peer stores.
+  v.nvls = (v.two_shot && c->nv_mc != nullptr && c->mode == 3) ? 1 : 0;
   return run_gemm(A, B, sa, sb, bias, C, nullptr, M, N, K, 0, 0, workspace, workspace_bytes,
                   static_cast<cudaStream_t>(stream), c->timeout_ns, &v);
 }

@@ -1056,11 +1056,12 @@ __global__ void __launch_bounds__(gemm_block_threads<FUSED>(), 1)
           if (et == 0)
             counted = dev::wait_counter(args.counters + tile, static_cast<uint32_t>(c_last - c_first), abort_flag,
                                         args.err, kErrGemmWait, tmo);
+          // et == 0's acquire of the count, then the barrier, order every
+          // epilogue thread's slot loads (L2, .cg) after the other CTAs' stores
           if (dev::named_bar_or(1, 128, !counted)) {
             aborted = true;
             break;
           }
-          __threadfence();
           // The slots' loads are issued in batches of kBatch CTAs, all in
           // flight together (a tile of a decode GEMM spans up to ~5 CTAs).
           constexpr int kBatch = kVec <= 4 ? 4 : 2;
