@@ -592,24 +592,26 @@ __device__ bool fused_reduce_group(const GemmArgs& a, const CommView& cv, uint32
     } else if (cv.nvls) {
       // This rank's row share of tile t, summed over every rank's partial in
       // the switch (multimem.ld_reduce), written to C and multicast into every
-      // rank's gather region; four reductions in flight per thread.
+      // rank's gather region; kInFlight reductions in flight per thread (each
+      // is a round trip through the switch).
       const int r0 = (hm * cv.rank) / cv.world, r1 = (hm * (cv.rank + 1)) / cv.world;
       const int per_chunk = (r1 - r0) * 4;
       const int nv = per_chunk * (BN / 32);
       const char* mc_p = dev::nv_partials(cv, cv.mc_base, epoch) + static_cast<size_t>(t) * TILE;
       char* mc_g = dev::nv_gather(cv, cv.mc_base, epoch) + static_cast<size_t>(t) * TILE;
       dev::fence_proxy_alias();  // the peers' partials were written through their unicast mappings
-      for (int base = g.tid; base < nv; base += 4 * g.nthreads) {
-        uint4 sum[4];
-        int vv[4];
+      constexpr int kInFlight = 8;
+      for (int base = g.tid; base < nv; base += kInFlight * g.nthreads) {
+        uint4 sum[kInFlight];
+        int vv[kInFlight];
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
+        for (int j = 0; j < kInFlight; ++j) {
           const int i = base + j * g.nthreads;
           vv[j] = (i / per_chunk) * 512 + r0 * 4 + (i % per_chunk);
           if (i < nv) sum[j] = dev::mm_ld_reduce_bf16x8(mc_p + static_cast<size_t>(vv[j]) * 16);
         }
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
+        for (int j = 0; j < kInFlight; ++j) {
           if (base + j * g.nthreads >= nv) continue;
           int r, col;
           block_vec_rc<BN, SWAP>(vv[j], r, col);
