@@ -29,6 +29,7 @@ Prints one JSON line on rank 0.
 from __future__ import annotations
 
 import argparse
+import copy
 import ctypes
 import importlib
 import json
@@ -165,6 +166,23 @@ def checkpoint_items(dev: torch.device):
             yield f"model.layers.{layer}.{module}.{name}.weight", full_weight(name, dev, layer)
 
 
+DECODE_CHAIN = 8  # decode steps per graph replay in the sweep
+
+
+def clone_layers(layers):
+    """Copies of a stack's layers with their own weight storage (same values)."""
+    out = []
+    for lay in layers:
+        new = {}
+        for name, layer in lay.items():
+            c = copy.copy(layer)
+            c.weight = layer.weight.clone()
+            c.weight_scale = layer.weight_scale.clone()
+            new[name] = c
+        out.append(new)
+    return out
+
+
 # --------------------------------------------------------------------------- clocks
 class ClockSampler:
     """nvidia-smi sampling of SM clock and throttle reasons during the timed region."""
@@ -271,11 +289,13 @@ class Stack:
         if not MLP_ONLY:
             qkv = lay["qkv"].forward(x)
             x = lay["o_proj"].forward(qkv[:, : self.q_cols])
-        gu = lay["gate_up"].forward(x)
-        return lay["down"].forward(self.pkg.ops.silu_and_mul_quant(gu))
+        return lay["down"].forward(lay["gate_up"].forward_silu_quant(x))
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
-        for lay in self.layers:
+        return self.forward_layers(self.layers, x)
+
+    def forward_layers(self, layers, x: torch.Tensor) -> torch.Tensor:
+        for lay in layers:
             x = self._layer(lay, x)
         return x
 
@@ -286,8 +306,8 @@ class Stack:
         t["qkv"] = self.qkv.forward(x)
         t["attn"] = t["qkv"][:, : self.q_cols]
         t["h"] = self.o_proj.forward(t["attn"])
-        t["gu"] = self.gate_up.forward(t["h"])
-        qa = self.pkg.ops.silu_and_mul_quant(t["gu"])
+        t["gu"] = self.gate_up.forward(t["h"])  # the gate_up GEMM alone, checked on its own
+        qa = self.gate_up.forward_silu_quant(t["h"])  # the timed path (SiLU in the GEMM's epilogue)
         t["q"], t["s"] = qa.q, qa.s
         t["out"] = self.down.forward(qa)
         return t
@@ -301,8 +321,7 @@ class Stack:
                 qkv = lay["qkv"].forward(x)
                 qa = lay["o_proj"]._quantize_input(qkv[:, : self.q_cols])
                 x = nccl.all_reduce(ops.w8a8_gemm(qa.q, lay["o_proj"].weight, qa.s, lay["o_proj"].weight_scale))
-            gu = lay["gate_up"].forward(x)
-            y = ops.silu_and_mul_quant(gu)
+            y = lay["gate_up"].forward_silu_quant(x)
             x = nccl.all_reduce(ops.w8a8_gemm(y.q, lay["down"].weight, y.s, lay["down"].weight_scale))
         return x
 
@@ -448,13 +467,14 @@ def max_over_ranks(v: float, world: int, dev) -> float:
     return float(t.item())
 
 
-def _read_traffic(m: int, n: int, k: int):
+def _read_traffic(m: int, n: int, k: int, silu: bool = False):
     """Per-launch DRAM bytes of the dominant kernel, from the committed ncu
-    summary of the gate_up GEMM at M=4096, N=51200, K=5120 (TP=1).  At TP=N
-    the launch has N/TP output columns; its traffic (weight rows read, output
-    columns written) scales with N, so the captured figure is scaled by
-    n / 51200.  None for another M or K."""
-    p = os.path.join(ROOT, "profiles", "gemm_gate_up_m4096_tp1_ncu.txt")
+    summary of the gate_up GEMM at M=4096, N=51200, K=5120 (TP=1) -- with the
+    SiLU*mul epilogue or plain.  At TP=N the launch has N/TP output columns;
+    its traffic (weight rows read, output columns written) scales with N, so
+    the captured figure is scaled by n / 51200.  None for another M or K."""
+    name = "gemm_gate_up_silu_m4096_tp1_ncu.txt" if silu else "gemm_gate_up_m4096_tp1_ncu.txt"
+    p = os.path.join(ROOT, "profiles", name)
     if m != 4096 or k != HIDDEN:
         return None
     try:
@@ -797,24 +817,48 @@ def run_ours(args, rank, world, dev):
         value = args.m * args.steps / (total_ms / 1e3)
 
         # ------------------------------------------------------------ decode sweep
+        # A model's layers run back to back inside one CUDA graph, so the
+        # graph's launch cost is spread over all of them: each replay runs
+        # DECODE_CHAIN consecutive steps, each through its own copy of the
+        # layers (own weight storage: no step finds another's weights in L2),
+        # and the time per step is the replay's time / DECODE_CHAIN.
         sweep = {}
         ops_tok, wbytes = layer_ops(world)
+        chain = [stack.layers] + [clone_layers(stack.layers) for _ in range(DECODE_CHAIN - 1)]
+
+        def decode_chain(xm):
+            for layers in chain:
+                xm = stack.forward_layers(layers, xm)
+            return xm
+
         for m in args.sweep:
             xm = torch.randn(m, HIDDEN, device=dev, generator=gx).bfloat16()
-            tms, _, _ = time_graph(lambda: stack.forward(xm), max(20, args.steps), args.warmup, flush_buf, stream)
+            reps = max(10, args.steps // 2)
+            tms, _, _ = time_graph(lambda: decode_chain(xm), reps, args.warmup, flush_buf, stream)
             tms = max_over_ranks(tms, world, dev)
-            us = tms / max(20, args.steps) * 1e3
+            us = tms / (reps * DECODE_CHAIN) * 1e3
             t_hbm = wbytes / (peaks["hbm_gbs"] * 1e9) * 1e6
             sweep[str(m)] = {"tokens_per_s": round(m / (us * 1e-6), 1), "us_per_step": round(us, 2),
-                             "weight_stream_frac_of_hbm": round(t_hbm / us, 3)}
+                             "weight_stream_frac_of_hbm": round(t_hbm / us, 3),
+                             "steps_per_graph": DECODE_CHAIN}
+        del chain
 
         # ------------------------------------------------------------ roofline: dominant kernel
         n_gu, k_gu = local_shapes(world)["gate_up"]
         qa = stack.gate_up._quantize_input(x)
         gemm_out = torch.empty(args.m, n_gu, dtype=torch.bfloat16, device=dev)
-        gemm_ms = time_kernel_events(
+        plain_ms = time_kernel_events(
             lambda: ops.w8a8_gemm(qa.q, stack.gate_up.weight, qa.s, stack.gate_up.weight_scale, out=gemm_out),
             max(10, args.steps // 2), flush_buf, stream)
+        # the step's gate_up kernel: the GEMM with SiLU*mul in its epilogue
+        # where the fusion applies (y [M, N/2] written instead of [M, N])
+        silu_step = ops.gemm_silu(qa.q, stack.gate_up.weight, qa.s, stack.gate_up.weight_scale) is not None
+        if silu_step:
+            gemm_ms = time_kernel_events(
+                lambda: ops.gemm_silu(qa.q, stack.gate_up.weight, qa.s, stack.gate_up.weight_scale),
+                max(10, args.steps // 2), flush_buf, stream)
+        else:
+            gemm_ms = plain_ms
         alg_ops = 2.0 * args.m * n_gu * k_gu
         achieved_tops = alg_ops / (gemm_ms * 1e-3) / 1e12
         peak_probe = int8_peak(pkg, stream)
@@ -854,13 +898,20 @@ def run_ours(args, rank, world, dev):
         breakdown["quant_h"] = op_us(lambda: ops.quant_per_token(h))
     else:
         h, qh = x, qx
-    gu = stack.gate_up.forward(h)
-    qy = ops.silu_and_mul_quant(gu)
-    breakdown["gate_up_gemm"] = op_us(lambda: ops.w8a8_gemm(qh[0], stack.gate_up.weight, qh[1],
-                                                            stack.gate_up.weight_scale))
-    breakdown["silu_mul_quant"] = op_us(lambda: ops.silu_and_mul_quant(gu))
+    qah = ops.QuantizedActivation(*qh)
+    qy = stack.gate_up.forward_silu_quant(qah)
+    # the step's gate_up: the GEMM with SiLU*mul in its epilogue + the
+    # quantiser of its product (or, below the fusion's range, the GEMM and the
+    # fused SiLU*mul quantiser)
+    breakdown["gate_up_silu_quant"] = op_us(lambda: stack.gate_up.forward_silu_quant(qah))
     breakdown["down"] = op_us(lambda: d_p.forward(qy))
     ops_keys = list(breakdown)
+    # for comparison (not in the step): the two-step path it replaces
+    gu = stack.gate_up.forward(qah)
+    breakdown["two_step_gate_up_gemm"] = op_us(lambda: ops.w8a8_gemm(qh[0], stack.gate_up.weight, qh[1],
+                                                                     stack.gate_up.weight_scale))
+    breakdown["two_step_silu_mul_quant"] = op_us(lambda: ops.silu_and_mul_quant(gu))
+    del gu
     if world > 1:
         if not MLP_ONLY:
             breakdown["o_proj_gemm_alone"] = op_us(lambda: ops.w8a8_gemm(qattn[0], o_p.weight, qattn[1],
@@ -999,7 +1050,7 @@ def run_ours(args, rank, world, dev):
     if world > 1:
         torch.distributed.barrier()
 
-    traffic = _read_traffic(args.m, n_gu, k_gu)
+    traffic = _read_traffic(args.m, n_gu, k_gu, silu=silu_step)
     line = {
         "metric": METRIC,
         "value": round(value, 1),
@@ -1015,7 +1066,9 @@ def run_ours(args, rank, world, dev):
         "data": "synthetic: seeded N(0,1) bf16 activations; synthetic N(0,0.02) bf16 checkpoint quantised per "
                 "channel and sharded by the package's loader",
         "config": dict(workload_config(world, args.m), allreduce=comm_kind, l2=L2_NOTE),
-        "roofline": {"kernel": f"w8a8_gemm gate_up M={args.m} N={n_gu} K={k_gu}", "bound": "tensor",
+        "roofline": {"kernel": (f"w8a8_gemm_silu gate_up + SiLU*mul epilogue M={args.m} N={n_gu} K={k_gu}"
+                                if silu_step else f"w8a8_gemm gate_up M={args.m} N={n_gu} K={k_gu}"),
+                     "bound": "tensor",
                      "achieved": round(achieved_tops, 1), "peak": round(peak_tops, 1), "unit": "TOP/s (int8)",
                      "frac": round(achieved_tops / peak_tops, 4),
                      "peak_source": "measured in this run: MMA-only tcgen05 kind::i8 loop from resident shared "
@@ -1023,11 +1076,14 @@ def run_ours(args, rank, world, dev):
                      "frac_of_2x_bf16": round(achieved_tops / (2.0 * peaks["bf16_tflops"]), 4),
                      "frac_of_nominal_int8_4500": round(achieved_tops / INT8_NOMINAL_TOPS, 4),
                      "launch_ms": round(gemm_ms, 4), "traffic": traffic,
-                     "algorithmic_bytes": args.m * k_gu + n_gu * k_gu + 2 * args.m * n_gu + 4 * args.m + 4 * n_gu},
+                     "algorithmic_bytes": (args.m * k_gu + n_gu * k_gu + (args.m * n_gu if silu_step else
+                                                                           2 * args.m * n_gu)
+                                           + (8 if silu_step else 4) * args.m + 4 * n_gu)},
         "yardsticks": {"torch_int_mm_tops_same_shape": None if int_mm_tops is None else round(int_mm_tops, 1),
                        "torch_int_mm_ms_same_shape": None if int_mm_ms is None else round(int_mm_ms, 4),
                        "cublas_bf16_linear_ms_same_shape": round(bf16_ms, 4),
-                       "ours_gemm_ms_same_shape": round(gemm_ms, 4)},
+                       "ours_gemm_ms_same_shape": round(gemm_ms, 4),
+                       "ours_plain_gemm_ms_same_shape": round(plain_ms, 4)},
         "breakdown_us": breakdown,
         "nccl_baseline": nccl_line,
         "parity": parity,
@@ -1076,7 +1132,9 @@ def run_reference(args, rank, world):
 def run_gemm_only(args, dev):
     """Profiling entry for single GEMM shapes (``--gemm MxNxK,...``): int8
     operands drawn on the device (no other kernel of ours runs), then two
-    launches of the auto-planned GEMM per shape, in the order given."""
+    launches of the auto-planned GEMM per shape, in the order given (with
+    ``--silu``: the GEMM with the SiLU*mul epilogue, N = 2I, and the quantiser
+    of its product)."""
     pkg = _pkg()
     pkg.ops.gemm_workspace(dev)
     g = torch.Generator(device=dev).manual_seed(0)
@@ -1091,7 +1149,10 @@ def run_gemm_only(args, dev):
     torch.cuda.synchronize()
     for a, w, sa, sw, out in shapes:
         for _ in range(2):
-            pkg.ops.w8a8_gemm(a, w, sa, sw, out=out)
+            if args.silu:
+                assert pkg.ops.gate_up_silu_quant(a, w, sa, sw) is not None, "shape outside the SiLU epilogue's range"
+            else:
+                pkg.ops.w8a8_gemm(a, w, sa, sw, out=out)
     torch.cuda.synchronize()
     assert pkg.ops.device_error() == 0
     print(json.dumps({"gemm_only": True, "shapes": args.gemm,
@@ -1129,6 +1190,8 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--kernel-only", action="store_true", help="profiling entry (see run_kernel_only)")
     ap.add_argument("--gemm", default="", help="profiling entry: GEMM shapes MxNxK,... (see run_gemm_only)")
+    ap.add_argument("--silu", action="store_true",
+                    help="with --gemm: the GEMM with the SiLU*mul epilogue and the quantiser of its product")
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)

@@ -75,6 +75,15 @@ int w8a8_quant_per_token(const void* x, int64_t ldx, int8_t* q, float* scale,
 int w8a8_silu_mul_quant(const void* gate_up, int64_t ld, int8_t* q, float* scale,
                         void* y_out, int64_t M, int64_t I, void* stream);
 
+/* The per-token quantiser for rows whose absmax is already known: amax[M]
+ * holds max |y| of each row as float bits (as w8a8_gemm_silu leaves it);
+ * scale = amax/127 and q follow w8a8_quant_per_token's rule exactly.  The
+ * second half of the gate_up + SiLU*mul + quantiser fusion (the reference's
+ * gate_up F.linear and silu_and_mul, M/models/utils.py:44-50).  Needs
+ * K % 8 == 0, ldy % 8 == 0, 16-byte aligned y and q. */
+int w8a8_quant_rows_amax(const void* y, int64_t ldy, const uint32_t* amax, int8_t* q,
+                         float* scale, int64_t M, int64_t K, void* stream);
+
 /* RMSNorm fused with the per-token quantiser: the input side of qkv and
  * gate_up.  Replaces RMSNorm.forward / RMSNormFused.forward
  * (M/layers/norm.py:8-38) followed by the quantiser.  x[M, K] bf16 (row stride
@@ -105,6 +114,19 @@ size_t w8a8_gemm_workspace_size(int64_t M, int64_t N, int64_t K);
 int w8a8_gemm(const int8_t* A, const int8_t* B, const float* sa, const float* sb,
               const void* bias, void* C, int32_t* c_i32, int64_t M, int64_t N, int64_t K,
               void* workspace, size_t workspace_bytes, void* stream);
+
+/* gate_up GEMM with the SiLU*mul in its epilogue: B = [gate (I rows); up
+ * (I rows)] int8 [2I, K] (the merged gate_up weight of
+ * LinearColParallelMerged, M/layers/linear.py:56-71), bias [2I] or null;
+ * Y[M, I] bf16 receives y = bf16(silu(g) * u), g and u the bf16 values
+ * w8a8_gemm would write, and amax[M] (uint32, zeroed by the caller) the
+ * float bits of every row's max |y| -- the gate_up linear and silu_and_mul
+ * of GatedMLP (M/models/utils.py:44-50) without the [M, 2I] tensor in HBM.
+ * Runs on the 2-SM pair kernel: M > 128 and 2I % 256 == 0, else
+ * W8A8_ERR_UNSUPPORTED (take w8a8_gemm + w8a8_silu_mul_quant then). */
+int w8a8_gemm_silu(const int8_t* A, const int8_t* B, const float* sa, const float* sb,
+                   const void* bias, void* Y, uint32_t* amax, int64_t M, int64_t N2, int64_t K,
+                   void* workspace, size_t workspace_bytes, void* stream);
 
 /* Same as w8a8_gemm with an explicit configuration (for tests and tuning):
  * variant 0 = auto, 1 = 128x256 tiles, 2 = 128x128 tiles, 3..6 =

@@ -49,11 +49,14 @@ SIGNATURES = {
     "w8a8_device_error": (_c_int, [ctypes.POINTER(_c_int), _c_int]),
     "w8a8_quant_per_token": (_c_int, [_c_vp, _c_i64, _c_vp, _c_vp, _c_i64, _c_i64, _c_vp]),
     "w8a8_silu_mul_quant": (_c_int, [_c_vp, _c_i64, _c_vp, _c_vp, _c_vp, _c_i64, _c_i64, _c_vp]),
+    "w8a8_quant_rows_amax": (_c_int, [_c_vp, _c_i64, _c_vp, _c_vp, _c_vp, _c_i64, _c_i64, _c_vp]),
     "w8a8_rmsnorm_quant": (_c_int, [_c_vp, _c_i64, _c_vp, _c_i64, _c_vp, ctypes.c_float, _c_vp, _c_vp,
                                     _c_vp, _c_vp, _c_i64, _c_i64, _c_vp]),
     "w8a8_gemm_workspace_size": (_c_size, [_c_i64, _c_i64, _c_i64]),
     "w8a8_gemm": (_c_int, [_c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp,
                            _c_i64, _c_i64, _c_i64, _c_vp, _c_size, _c_vp]),
+    "w8a8_gemm_silu": (_c_int, [_c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp,
+                                _c_i64, _c_i64, _c_i64, _c_vp, _c_size, _c_vp]),
     "w8a8_gemm_config": (_c_int, [_c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp,
                                   _c_i64, _c_i64, _c_i64, _c_int, _c_int, _c_vp, _c_size, _c_vp]),
     "w8a8_gemm_static_scratch": (_c_int, [_c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp,

@@ -131,7 +131,8 @@ int dispatch_variant(const GemmPlan& p, const CUtensorMap& tw, const CUtensorMap
 
 int run_gemm(const int8_t* A, const int8_t* B, const float* sa, const float* sb, const void* bias, void* C,
              int32_t* c_i32, int64_t M, int64_t N, int64_t K, int variant, int ctas, void* workspace,
-             size_t workspace_bytes, cudaStream_t stream, long long timeout_ns, const CommView* comm) {
+             size_t workspace_bytes, cudaStream_t stream, long long timeout_ns, const CommView* comm,
+             uint32_t* silu_amax) {
   W8A8_REQUIRE(M >= 0 && N >= 0 && K >= 0, W8A8_ERR_INVALID_ARG, "gemm: negative shape");
   if (M == 0) return W8A8_OK;  // empty batch: nothing to compute (its tensors may be null)
   int rc = validate_gemm_args(A, B, sa, sb, C, M, N, K);
@@ -143,6 +144,21 @@ int run_gemm(const int8_t* A, const int8_t* B, const float* sa, const float* sb,
   GemmPlan p;
   rc = plan_gemm(M, N, K, variant, ctas, workspace_bytes, sm_count(), &p);
   W8A8_REQUIRE(rc == 0, W8A8_ERR_INVALID_ARG, "gemm: %s", plan_error(rc));
+  if (silu_amax) {
+    W8A8_REQUIRE(comm == nullptr && c_i32 == nullptr, W8A8_ERR_INVALID_ARG,
+                 "gemm_silu: no int32 output and no fused reduce with the SiLU epilogue");
+    W8A8_REQUIRE(N % 256 == 0, W8A8_ERR_UNSUPPORTED, "gemm_silu: 2I = %lld must be a multiple of 256",
+                 (long long)N);
+    W8A8_REQUIRE(W8A8_ALIGNED16(silu_amax), W8A8_ERR_ALIGNMENT, "gemm_silu: amax must be 16-byte aligned");
+    // the SiLU epilogue lives in the 2-SM pair kernel: take its plan whenever
+    // the pairs have whole 256-row blocks to work on
+    if (p.variant != 7 && M > 128) {
+      GemmPlan q;
+      if (plan_gemm(M, N, K, 7, ctas, workspace_bytes, sm_count(), &q) == 0) p = q;
+    }
+    W8A8_REQUIRE(p.variant == 7, W8A8_ERR_UNSUPPORTED,
+                 "gemm_silu: M=%lld is below the 2-SM pair plan's range (needs M > 128)", (long long)M);
+  }
   if (comm) {
     W8A8_REQUIRE(p.num_tiles <= kMaxSlots, W8A8_ERR_UNSUPPORTED,
                  "gemm_allreduce: %d output tiles exceed the %d flag slots", p.num_tiles, kMaxSlots);
@@ -206,6 +222,11 @@ int run_gemm(const int8_t* A, const int8_t* B, const float* sa, const float* sb,
   args.units = p.units;
   args.wide_fast = p.wide_fast;
   args.vec_scales = ((reinterpret_cast<uintptr_t>(sb) & 15u) == 0 && (reinterpret_cast<uintptr_t>(bias) & 15u) == 0) ? 1 : 0;
+  if (silu_amax) {
+    args.silu_i = static_cast<int>(N / 2);
+    args.amax = silu_amax;
+    args.ldc = static_cast<int>(N / 2);
+  }
 
   if (comm) {
     CommView cv = *comm;
@@ -253,6 +274,15 @@ int w8a8_gemm(const int8_t* A, const int8_t* B, const float* sa, const float* sb
               void* stream) {
   return w8a8::run_gemm(A, B, sa, sb, bias, C, c_i32, M, N, K, 0, 0, workspace, workspace_bytes,
                         static_cast<cudaStream_t>(stream), w8a8::kDefaultGemmTimeoutNs, nullptr);
+}
+
+int w8a8_gemm_silu(const int8_t* A, const int8_t* B, const float* sa, const float* sb, const void* bias, void* Y,
+                   uint32_t* amax, int64_t M, int64_t N2, int64_t K, void* workspace, size_t workspace_bytes,
+                   void* stream) {
+  W8A8_REQUIRE(amax != nullptr || M == 0, W8A8_ERR_INVALID_ARG, "gemm_silu: amax is null");
+  if (M == 0) return W8A8_OK;
+  return w8a8::run_gemm(A, B, sa, sb, bias, Y, nullptr, M, N2, K, 0, 0, workspace, workspace_bytes,
+                        static_cast<cudaStream_t>(stream), w8a8::kDefaultGemmTimeoutNs, nullptr, amax);
 }
 
 int w8a8_gemm_config(const int8_t* A, const int8_t* B, const float* sa, const float* sb, const void* bias,

@@ -27,6 +27,7 @@
 #pragma once
 
 #include "gemm_sm100.cuh"
+#include "silu.cuh"
 
 namespace w8a8 {
 
@@ -170,8 +171,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(gemm2_block_threads<
           if (half == 0) dev::mbar_expect_tx(dev::smem_u32(full + stage), 2 * T::kStageBytes);
           dev::tma_load_2d_pair(dev::smem_u32(s_a + stage * T::kTileABytes), &tm_a, leader_full, kb * T::kBK,
                                 tw * 128);
+          // B rows of this CTA's half: the block's next 128 weight rows, or
+          // (SiLU epilogue) the block's 128 gate rows / their 128 up rows
+          const int b_row = args.silu_i ? tn * 128 + static_cast<int>(half) * args.silu_i
+                                        : tn * 256 + static_cast<int>(half) * 128;
           dev::tma_load_2d_pair(dev::smem_u32(s_b + stage * T::kTileBBytes), &tm_b, leader_full, kb * T::kBK,
-                                tn * 256 + static_cast<int>(half) * 128);
+                                b_row);
           issued_mask |= 1u << stage;
           issued_phase = (issued_phase & ~(1u << stage)) | (phase << stage);
           if (++stage == STAGES) {
@@ -304,7 +309,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(gemm2_block_threads<
       // the barrier below publishes them (see the single-CTA kernel)
       float* sbs = scale_stage + (blk & 1u) * 256;
       float* bss = scale_stage + 512 + (blk & 1u) * 256;
-      const float sam = stage_tile_scales(args, tn * 256, 256, et, real, row, sbs, bss);
+      const float sam = args.silu_i ? stage_tile_scales_silu(args, tn, et, real, row, sbs, bss)
+                                    : stage_tile_scales(args, tn * 256, 256, et, real, row, sbs, bss);
       ++blk;
       const bool ok = dev::mbar_wait(dev::smem_u32(acc_full + acc), acc_phase, abort_flag, args.err, kErrGemmWait,
                                      tmo);
@@ -314,6 +320,54 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(gemm2_block_threads<
       }
       dev::tc_fence_after();
       const uint32_t t_acc = tmem_base + lane_base + static_cast<uint32_t>(acc * T::kAccCols);
+      if constexpr (!FUSED) {
+        if (args.silu_i) {
+          // SiLU epilogue: accumulator columns [0, 128) are the block's gate
+          // features, [128, 256) their up features.  This warp takes features
+          // [64 hh, 64 hh + 64) in two 32-feature chunks: gate and up chunk
+          // dequantised to bf16 as the plain epilogue would write them, then
+          // y = bf16(silu(g) * u) (the fused quantiser's arithmetic), staged and
+          // written to C = y [M, I]; the row's max |y| goes to amax.
+          const int hh = (warp - 2) >> 2;
+          __nv_bfloat162 m2 = __float2bfloat162_rn(0.0f);
+#pragma unroll 1
+          for (int j = 0; j < 2; ++j) {
+            const int fc = hh * 64 + j * 32;
+            uint32_t vg[32], vu[32];
+            dev::tmem_ld32(t_acc + fc, vg);
+            dev::tmem_ld32(t_acc + 128 + fc, vu);
+            dev::tmem_wait_ld(vg);
+            dev::tmem_wait_ld(vu);
+            if (j == 1) {
+              dev::tc_fence_before();
+              const uint32_t bar = dev::smem_u32(acc_empty + acc);
+              if (half == 0) {
+                dev::mbar_arrive(bar);
+              } else {
+                dev::mbar_arrive_cluster(dev::mapa(bar, 0));
+              }
+            }
+            if (real) {
+              uint4 pg[4], pu[4];
+              dequant_pack32(args, sam, sbs + fc, bss + fc, vg, pg);
+              dequant_pack32(args, sam, sbs + 128 + fc, bss + 128 + fc, vu, pu);
+#pragma unroll
+              for (int i = 0; i < 4; ++i) {
+                const uint4 y = act::silu_mul_vec8(pg[i], pu[i]);
+                if (row < args.M) m2 = act::vec8_absmax2(y, m2);
+                stg[stage_slot(lane, i)] = y;
+              }
+              store_staged_chunk(args, stg, lane, tw * 128 + quarter * 32, tn * 128 + fc, args.silu_i);
+            }
+          }
+          if (real && row < args.M) atomicMax(args.amax + row, __float_as_uint(act::absmax_of(m2)));
+          if (++acc == 2) {
+            acc = 0;
+            acc_phase ^= 1u;
+          }
+          continue;
+        }
+      }
       uint32_t vn[32];
       dev::tmem_ld32(t_acc + c0 * 32, vn);  // chunk c + 1 loads while chunk c is processed
 #pragma unroll 1

@@ -88,6 +88,11 @@ struct GemmArgs {
   int sk_ctas;                // CTAs sharing the stream-K part: min(G, units), >= 1
   int wide_fast;              // raster: 1 = consecutive tiles walk the 128-row side
   int vec_scales;             // 1: sb (and bias) are 16-byte aligned, read 8 columns per load
+  // gate_up + SiLU epilogue (pair kernel, plain mode): silu_i = I > 0 when the
+  // weight is [gate (I rows); up (I rows)] and C receives y = bf16(silu(g) * u)
+  // [M, I] (ldc = I); amax[m] collects max |y| of row m as float bits.
+  int silu_i;
+  uint32_t* amax;
 };
 
 // Shared memory of the fused epilogue and reduction state (FusedState, below).
@@ -216,17 +221,67 @@ __device__ __forceinline__ void store_chunk_swap(const GemmArgs& a, int n, int c
 __device__ __forceinline__ int stage_slot(int r, int g) { return r * 4 + (g ^ ((r >> 1) & 3)); }
 
 // Write a staged chunk (rows m_base.., columns n0..n0+31) to C with
-// row-contiguous 16-byte stores; rows >= M and columns >= N are skipped.
+// row-contiguous 16-byte stores; rows >= M and columns >= n_limit are skipped.
 __device__ __forceinline__ void store_staged_chunk(const GemmArgs& a, const uint4* stg, int lane, int m_base,
-                                                   int n0) {
+                                                   int n0, int n_limit) {
   __syncwarp();
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
     const int r = j * 8 + (lane >> 2), g = lane & 3;
     const int m = m_base + r, n = n0 + g * 8;
-    if (m < a.M && n < a.N) *reinterpret_cast<uint4*>(a.C + static_cast<size_t>(m) * a.ldc + n) = stg[stage_slot(r, g)];
+    if (m < a.M && n < n_limit)
+      *reinterpret_cast<uint4*>(a.C + static_cast<size_t>(m) * a.ldc + n) = stg[stage_slot(r, g)];
   }
   __syncwarp();  // the next chunk may overwrite the staging buffer
+}
+__device__ __forceinline__ void store_staged_chunk(const GemmArgs& a, const uint4* stg, int lane, int m_base,
+                                                   int n0) {
+  store_staged_chunk(a, stg, lane, m_base, n0, a.N);
+}
+
+// The dequantised bf16 values of one 32-column chunk of row m, packed eight
+// to a uint4 -- the same arithmetic as store_chunk_smem.
+__device__ __forceinline__ void dequant_pack32(const GemmArgs& a, float sam, const float* sbs, const float* bss,
+                                               const uint32_t (&v)[32], uint4 (&out)[4]) {
+#pragma unroll
+  for (int g = 0; g < 4; ++g) {
+    const float4 s0 = reinterpret_cast<const float4*>(sbs)[g * 2];
+    const float4 s1 = reinterpret_cast<const float4*>(sbs)[g * 2 + 1];
+    const float sb[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+    __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&out[g]);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      float y0 = dequant1(static_cast<int32_t>(v[g * 8 + 2 * j]), sam, sb[2 * j]);
+      float y1 = dequant1(static_cast<int32_t>(v[g * 8 + 2 * j + 1]), sam, sb[2 * j + 1]);
+      if (a.bias) {
+        y0 = __fadd_rn(y0, bss[g * 8 + 2 * j]);
+        y1 = __fadd_rn(y1, bss[g * 8 + 2 * j + 1]);
+      }
+      h[j] = __floats2bfloat162_rn(y0, y1);
+    }
+  }
+}
+
+// SiLU epilogue: stage the scales (and bias) of a block's 128 gate columns
+// (tn * 128 ..) at [0, 128) and of the matching up columns (I + tn * 128 ..)
+// at [128, 256), the order of the block's accumulator columns; thread t takes
+// columns 2t and 2t + 1.  Returns row m's activation scale (0 past M).
+__device__ __forceinline__ float stage_tile_scales_silu(const GemmArgs& a, int tn, int t, bool real, int m,
+                                                        float* sbs, float* bss) {
+  if (t < 128) {
+    const int c = 2 * t;
+    const int n = c < 128 ? tn * 128 + c : a.silu_i + tn * 128 + (c - 128);
+    float2 sv = make_float2(0.0f, 0.0f), bv = make_float2(0.0f, 0.0f);
+    if (real) {
+      sv = make_float2(__ldg(a.sb + n), __ldg(a.sb + n + 1));
+      if (a.bias) bv = make_float2(__bfloat162float(a.bias[n]), __bfloat162float(a.bias[n + 1]));
+    }
+    sbs[c] = sv.x;
+    sbs[c + 1] = sv.y;
+    bss[c] = bv.x;
+    bss[c + 1] = bv.y;
+  }
+  return (real && m < a.M) ? __ldg(a.sa + m) : 0.0f;
 }
 
 // Normal orientation, with the tile's weight scales (and bias) staged in

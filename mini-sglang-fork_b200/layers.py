@@ -122,6 +122,18 @@ class LinearColParallelMerged(_LinearTPImpl):
         tp_output_sizes = [div_even(size, tp_info.size) for size in output_sizes]
         super().__init__(input_size, sum(output_sizes), input_size, sum(tp_output_sizes), has_bias)
 
+    def forward_silu_quant(self, x: Union[torch.Tensor, QuantizedActivation]) -> QuantizedActivation:
+        """For a [gate; up] merge (GatedMLP's gate_up_proj): the quantised
+        ``silu(gate) * up`` that ``silu_and_mul_quant(self.forward(x))`` gives,
+        bit for bit, with the SiLU*mul in the GEMM's epilogue when the shape
+        allows (ops.gate_up_silu_quant) so the [M, 2I] output is never
+        written; otherwise in those two steps."""
+        qa = self._quantize_input(x)
+        fused = ops.gate_up_silu_quant(qa.q, self.weight, qa.s, self.weight_scale, self.bias)
+        if fused is not None:
+            return fused
+        return ops.silu_and_mul_quant(ops.w8a8_gemm(qa.q, self.weight, qa.s, self.weight_scale, self.bias))
+
 
 class LinearQKVMerged(_LinearTPImpl):
     """Column-parallel q|k|v over heads, kv replicated when kv_heads < tp
@@ -194,8 +206,9 @@ class RMSNormFusedQuant(BaseOP):
 
 class GatedMLP(BaseOP):
     """W8A8 ``GatedMLP`` (M/models/utils.py:25-50): gate_up (column-parallel)
-    -> fused SiLU*mul + per-token quant -> down (row-parallel + all-reduce).
-    The bf16 product of SiLU*mul never touches HBM."""
+    with SiLU*mul in its epilogue -> per-token quant -> down (row-parallel +
+    all-reduce).  The [M, 2I] gate_up output never touches HBM (below the
+    fusion's shape range: gate_up, then the fused SiLU*mul quantiser)."""
 
     def __init__(self, hidden_size: int, intermediate_size: int):
         self.gate_up_proj = LinearColParallelMerged(hidden_size, [intermediate_size, intermediate_size],
@@ -203,8 +216,6 @@ class GatedMLP(BaseOP):
         self.down_proj = LinearRowParallel(intermediate_size, hidden_size, has_bias=False)
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
-        gate_up = self.gate_up_proj.forward(x)
+        y = self.gate_up_proj.forward_silu_quant(x)
         del x
-        y = silu_and_mul_quant(gate_up)
-        del gate_up
         return self.down_proj.forward(y)

@@ -18,6 +18,9 @@ __all__ = [
     "silu_and_mul_quant",
     "silu_and_mul",
     "w8a8_gemm",
+    "gate_up_silu_quant",
+    "gemm_silu",
+    "quant_rows_amax",
     "gemm_plan",
     "gemm_workspace",
     "device_error",
@@ -177,13 +180,15 @@ def gemm_plan(m: int, n: int, k: int, variant: int = 0, ctas: int = 0,
 
 def check_gemm_operands(name: str, aq: torch.Tensor, wq: torch.Tensor, sa: torch.Tensor, sw: torch.Tensor,
                         bias: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None,
-                        out_i32: Optional[torch.Tensor] = None) -> Tuple[int, int, int, torch.Tensor]:
+                        out_i32: Optional[torch.Tensor] = None,
+                        alloc_out: bool = True) -> Tuple[int, int, int, Optional[torch.Tensor]]:
     """Host-side validation shared by every GEMM entry (plain and fused): all
     tensors on one CUDA device, int8 2-D operands with matching K, fp32 scale
     vectors of exactly M and N elements, bf16 bias [N], bf16 out [M, N]
     (allocated when None), int32 out_i32 [M, N].  A bad operand raises here,
     before any pointer reaches a kernel (a host pointer or a short scale
-    vector would otherwise be read by the GPU).  Returns (M, N, K, out)."""
+    vector would otherwise be read by the GPU).  Returns (M, N, K, out); out
+    stays None with ``alloc_out=False``."""
     if aq.dtype != torch.int8 or wq.dtype != torch.int8 or aq.dim() != 2 or wq.dim() != 2:
         raise _lib.W8A8Error(_lib.ERR_INVALID_ARG, f"{name}: 2-D int8 operands required")
     if not (aq.is_contiguous() and wq.is_contiguous() and sa.is_contiguous() and sw.is_contiguous()):
@@ -207,7 +212,7 @@ def check_gemm_operands(name: str, aq: torch.Tensor, wq: torch.Tensor, sa: torch
     devs = {t.device for t in (aq, wq, sa, sw, bias, out, out_i32) if t is not None}
     if len(devs) != 1:
         raise _lib.W8A8Error(_lib.ERR_INVALID_ARG, f"{name}: operands on several devices {sorted(map(str, devs))}")
-    if out is None:
+    if out is None and alloc_out:
         out = torch.empty(m, n, dtype=torch.bfloat16, device=aq.device)
     return m, n, k, out
 
@@ -229,6 +234,61 @@ def w8a8_gemm(aq: torch.Tensor, wq: torch.Tensor, sa: torch.Tensor, sw: torch.Te
                               m, n, k, variant, ctas, _ptr(ws), ws.numel(), _stream(aq))
     _lib.check(st, "w8a8_gemm")
     return out
+
+
+def gemm_silu(aq: torch.Tensor, wq: torch.Tensor, sa: torch.Tensor, sw: torch.Tensor,
+              bias: Optional[torch.Tensor] = None) -> Optional[Tuple[torch.Tensor, torch.Tensor]]:
+    """The gate_up GEMM with SiLU*mul in its epilogue: ``wq [2I, K]`` is the
+    merged [gate; up] weight; returns ``(y, amax)`` with ``y = bf16(silu(g) *
+    u)`` ``[M, I]`` (g, u the bf16 values :func:`w8a8_gemm` would write) and
+    ``amax [M]`` int32 holding the float bits of every row's max |y|.  None
+    where the fusion does not apply (M <= 128 or 2I % 256 != 0: the 2-SM pair
+    kernel carries the SiLU epilogue)."""
+    m, n2, k, _ = check_gemm_operands("gemm_silu", aq, wq, sa, sw, bias, alloc_out=False)
+    if m <= 128 or n2 % 256:
+        return None
+    dev = aq.device
+    y = torch.empty(m, n2 // 2, dtype=torch.bfloat16, device=dev)
+    amax = torch.zeros(m, dtype=torch.int32, device=dev)  # raised atomically by the epilogue
+    ws = gemm_workspace(dev)
+    lib = _lib.load()
+    st = lib.w8a8_gemm_silu(_ptr(aq), _ptr(wq), _ptr(sa), _ptr(sw), _ptr(bias), _ptr(y), _ptr(amax),
+                            m, n2, k, _ptr(ws), ws.numel(), _stream(aq))
+    if st == _lib.ERR_UNSUPPORTED:
+        return None
+    _lib.check(st, "gemm_silu")
+    return y, amax
+
+
+def quant_rows_amax(y: torch.Tensor, amax: torch.Tensor) -> QuantizedActivation:
+    """Per-token quantisation of ``y [M, K]`` bf16 whose row absmax is already
+    known (``amax [M]``, float bits as :func:`gemm_silu` leaves them); the same
+    rule as :func:`quant_per_token`."""
+    _require_cuda("quant_rows_amax", y, amax)
+    if y.dtype != torch.bfloat16 or y.dim() != 2 or y.stride(1) != 1 or amax.numel() != y.shape[0]:
+        raise _lib.W8A8Error(_lib.ERR_INVALID_ARG, "quant_rows_amax: y must be 2-D bf16, amax [M]")
+    m, k = y.shape
+    q = torch.empty(m, k, dtype=torch.int8, device=y.device)
+    s = torch.empty(m, dtype=torch.float32, device=y.device)
+    lib = _lib.load()
+    _lib.check(lib.w8a8_quant_rows_amax(_ptr(y), y.stride(0), _ptr(amax), _ptr(q), _ptr(s), m, k, _stream(y)),
+               "quant_rows_amax")
+    return QuantizedActivation(q, s)
+
+
+def gate_up_silu_quant(aq: torch.Tensor, wq: torch.Tensor, sa: torch.Tensor, sw: torch.Tensor,
+                       bias: Optional[torch.Tensor] = None, with_bf16: bool = False):
+    """gate_up GEMM, SiLU*mul and per-token quantisation with the [M, 2I]
+    gate_up tensor never in HBM (:func:`gemm_silu`, then
+    :func:`quant_rows_amax`).  Bit-identical to
+    ``silu_and_mul_quant(w8a8_gemm(...))``.  Returns None where the fusion
+    does not apply; with ``with_bf16`` returns ``(QuantizedActivation, y)``."""
+    r = gemm_silu(aq, wq, sa, sw, bias)
+    if r is None:
+        return None
+    y, amax = r
+    qa = quant_rows_amax(y, amax)
+    return (qa, y) if with_bf16 else qa
 
 
 # The stream-K counter region at the head of a GEMM workspace (65536 tile
