@@ -598,11 +598,197 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_quant_kernel(
   if (threadIdx.x == 0) scale[row] = rs.s;
 }
 
+// Resident CTAs per SM of a kernel at a given block size and dynamic shared
+// memory, queried once per device and kernel instance.
+template <typename Kernel>
+int resident_ctas(Kernel kernel, int threads, size_t smem) {
+  static int cached[64] = {0};
+  const int dev = w8a8::current_device();
+  if (dev < 0 || dev >= 64) return 1;
+  if (cached[dev] == 0) {
+    int n = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kernel, threads, smem) != cudaSuccess || n < 1) n = 1;
+    cached[dev] = n;
+  }
+  return cached[dev];
+}
+
+// Warp-group RMSNorm + quantiser (many rows of at most 8192 values): G warps
+// own a row, lane t of the group holding vectors t + 32 G j of x (and of the
+// residual) as raw bf16 in registers; v = x (+ residual) in fp32 is computed
+// again in the second pass instead of being kept (8 fp32 per vector would
+// cost the occupancy the one-CTA-per-row kernel loses).  Both reductions
+// (sum of squares, absmax) are warp shuffles plus one shared-memory exchange
+// under the group's named barrier; the same arithmetic as rmsnorm_quant_kernel
+// (its sum of squares is accumulated in another order: the fp32 rounding of
+// the sum, hence r, may differ in the last bit, within the tolerance the y
+// output is held to).  Persistent grid, group g taking rows g, g + groups, ...
+template <int VPT, int G, bool ADD>
+__global__ void __launch_bounds__(kWarpThreads) rmsnorm_warp_kernel(
+    const __nv_bfloat16* __restrict__ x, int64_t ldx, const __nv_bfloat16* residual, int64_t ldr,
+    const __nv_bfloat16* __restrict__ w, float eps, int8_t* __restrict__ q, float* __restrict__ scale,
+    __nv_bfloat16* residual_out, __nv_bfloat16* __restrict__ y_out, int64_t M, int width) {
+  constexpr int kGroups = kWarpThreads / 32 / G;
+  __shared__ float part_ss[2][kWarpThreads / 32], part_mx[2][kWarpThreads / 32];
+  w8a8::dev::griddep_launch();  // early trigger, as in rows_reg_kernel
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int grp = warp / G;
+  const int t = (warp % G) * 32 + lane;
+  const int nvec = width >> 3;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * kGroups;
+  const uint4* wr = reinterpret_cast<const uint4*>(w);
+  auto group_bar = [&]() {
+    if (kGroups == 1 || grp == 0)
+      w8a8::dev::named_bar_sync(1, 32 * G);
+    else
+      w8a8::dev::named_bar_sync(2, 32 * G);
+  };
+  w8a8::dev::griddep_wait();  // x / residual are the previous kernel's output
+  int it = 0;
+  for (int64_t row = static_cast<int64_t>(blockIdx.x) * kGroups + grp; row < M; row += stride, ++it) {
+    const uint4* xr = reinterpret_cast<const uint4*>(x + row * ldx);
+    const uint4* rr = ADD ? reinterpret_cast<const uint4*>(residual + row * ldr) : nullptr;
+    uint4 xa[VPT], ra[VPT];
+#pragma unroll
+    for (int j = 0; j < VPT; ++j) {
+      const int vi = t + j * 32 * G;
+      if (vi < nvec) {
+        xa[j] = __ldcs(xr + vi);
+        if constexpr (ADD) ra[j] = __ldcs(rr + vi);
+      }
+    }
+    auto value = [&](int j, int e) {  // v of element e (0..7) of vector j, fp32
+      const __nv_bfloat162 hx = reinterpret_cast<const __nv_bfloat162*>(&xa[j])[e >> 1];
+      float f = (e & 1) ? __high2float(hx) : __low2float(hx);
+      if constexpr (ADD) {
+        const __nv_bfloat162 hr = reinterpret_cast<const __nv_bfloat162*>(&ra[j])[e >> 1];
+        f = __fadd_rn(f, (e & 1) ? __high2float(hr) : __low2float(hr));
+      }
+      return f;
+    };
+    float ss = 0.0f;
+    uint4* ro = ADD && residual_out ? reinterpret_cast<uint4*>(residual_out + row * ldr) : nullptr;
+#pragma unroll
+    for (int j = 0; j < VPT; ++j) {
+      const int vi = t + j * 32 * G;
+      if (vi >= nvec) continue;
+      uint4 o;
+      __nv_bfloat162* ho = reinterpret_cast<__nv_bfloat162*>(&o);
+#pragma unroll
+      for (int e = 0; e < 8; e += 2) {
+        const float a = value(j, e), b = value(j, e + 1);
+        ss = __fmaf_rn(a, a, ss);
+        ss = __fmaf_rn(b, b, ss);
+        ho[e >> 1] = __floats2bfloat162_rn(a, b);
+      }
+      if (ro) ro[vi] = o;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    if constexpr (G > 1) {
+      float* p = &part_ss[it & 1][grp * G];
+      if (lane == 0) p[warp % G] = ss;
+      group_bar();
+      ss = p[0];
+#pragma unroll
+      for (int k = 1; k < G; ++k) ss += p[k];
+    }
+    const float r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, static_cast<float>(width)), eps)));
+    __nv_bfloat162 m2 = __float2bfloat162_rn(0.0f);
+#pragma unroll
+    for (int j = 0; j < VPT; ++j) {
+      const int vi = t + j * 32 * G;
+      if (vi >= nvec) continue;
+      const uint4 wv = __ldg(wr + vi);
+      const __nv_bfloat162* hw = reinterpret_cast<const __nv_bfloat162*>(&wv);
+      uint4 yv;
+      __nv_bfloat162* hy = reinterpret_cast<__nv_bfloat162*>(&yv);
+#pragma unroll
+      for (int e = 0; e < 8; e += 2) {
+        const float2 wf = __bfloat1622float2(hw[e >> 1]);
+        hy[e >> 1] = __floats2bfloat162_rn(__fmul_rn(__fmul_rn(value(j, e), r), wf.x),
+                                           __fmul_rn(__fmul_rn(value(j, e + 1), r), wf.y));
+      }
+      xa[j] = yv;  // x of this vector is no longer needed: keep y in its place
+      m2 = vec8_absmax2(yv, m2);
+    }
+    float amax = warp_max(absmax_of(m2));
+    if constexpr (G > 1) {
+      float* p = &part_mx[it & 1][grp * G];
+      if (lane == 0) p[warp % G] = amax;
+      group_bar();
+#pragma unroll
+      for (int k = 0; k < G; ++k) amax = fmaxf(amax, p[k]);
+    }
+    const RowScale rs = row_scale(amax);
+    uint2* qr = reinterpret_cast<uint2*>(q + row * static_cast<int64_t>(width));
+    uint4* yr = y_out ? reinterpret_cast<uint4*>(y_out + row * static_cast<int64_t>(width)) : nullptr;
+#pragma unroll
+    for (int j = 0; j < VPT; ++j) {
+      const int vi = t + j * 32 * G;
+      if (vi >= nvec) continue;
+      qr[vi] = quant_vec8(xa[j], rs);
+      if (yr) yr[vi] = xa[j];
+    }
+    if (t == 0) scale[row] = rs.s;
+  }
+}
+
+template <int VPT, int G, bool ADD>
+cudaError_t launch_rmsnorm_warp(const __nv_bfloat16* x, int64_t ldx, const __nv_bfloat16* res, int64_t ldr,
+                                const __nv_bfloat16* w, float eps, int8_t* q, float* scale,
+                                __nv_bfloat16* res_out, __nv_bfloat16* y, int64_t M, int width, int nsm,
+                                cudaStream_t s) {
+  constexpr int kGroups = kWarpThreads / 32 / G;
+  const int per_sm = resident_ctas(rmsnorm_warp_kernel<VPT, G, ADD>, kWarpThreads, 0);
+  int64_t grid = (M + kGroups - 1) / kGroups;
+  const int64_t cap = static_cast<int64_t>(nsm) * per_sm;
+  if (grid > cap) grid = cap;
+  return w8a8::launch_pdl(rmsnorm_warp_kernel<VPT, G, ADD>, dim3(static_cast<unsigned>(grid)), dim3(kWarpThreads),
+                          0, s, x, ldx, res, ldr, w, eps, q, scale, res_out, y, M, width);
+}
+
+// The warp-group RMSNorm for `nvec` vectors per row: the fewest warps (1, 2
+// or 4) that keep a lane's vectors at 8 or fewer (x and the residual are both
+// held); not launched when 4 warps are not enough (K > 8192: the one-CTA kernel).
+template <bool ADD>
+int launch_rmsnorm_warp_any(const __nv_bfloat16* x, int64_t ldx, const __nv_bfloat16* res, int64_t ldr,
+                            const __nv_bfloat16* w, float eps, int8_t* q, float* scale, __nv_bfloat16* res_out,
+                            __nv_bfloat16* y, int64_t M, int width, int nsm, cudaStream_t s, bool* launched) {
+  const int nvec = width / 8;
+  *launched = false;
+  int g = 0;
+  for (int c = 1; c <= 4 && g == 0; c *= 2)
+    if ((nvec + 32 * c - 1) / (32 * c) <= 8) g = c;
+  if (g == 0) return W8A8_OK;
+  const int vpt = (nvec + 32 * g - 1) / (32 * g);
+#define W8A8_RMS(V, GG)                                                                                        \
+  W8A8_CUDA_TRY((launch_rmsnorm_warp<V, GG, ADD>(x, ldx, res, ldr, w, eps, q, scale, res_out, y, M, width, nsm, s)))
+  if (g == 1) {
+    if (vpt <= 4) W8A8_RMS(4, 1); else if (vpt <= 6) W8A8_RMS(6, 1); else W8A8_RMS(8, 1);
+  } else if (g == 2) {
+    if (vpt <= 4) W8A8_RMS(4, 2); else if (vpt <= 6) W8A8_RMS(6, 2); else W8A8_RMS(8, 2);
+  } else {
+    if (vpt <= 4) W8A8_RMS(4, 4); else if (vpt <= 6) W8A8_RMS(6, 4); else W8A8_RMS(8, 4);
+  }
+#undef W8A8_RMS
+  *launched = true;
+  return W8A8_OK;
+}
+
 template <bool ADD>
 int launch_rmsnorm(const __nv_bfloat16* x, int64_t ldx, const __nv_bfloat16* res, int64_t ldr,
                    const __nv_bfloat16* w, float eps, int8_t* q, float* scale, __nv_bfloat16* res_out,
                    __nv_bfloat16* y, int64_t M, int width, cudaStream_t s) {
   const int nvec = width / 8;
+  int nsm = w8a8::sm_count();
+  if (nsm <= 0) nsm = 148;
+  if (M >= 2LL * nsm && nvec >= 32) {  // many rows: warp groups per row
+    bool launched = false;
+    const int rc = launch_rmsnorm_warp_any<ADD>(x, ldx, res, ldr, w, eps, q, scale, res_out, y, M, width, nsm, s,
+                                                &launched);
+    if (rc != W8A8_OK || launched) return rc;
+  }
   const int vpt = nvec <= kNormThreads ? 1 : (nvec <= 2 * kNormThreads ? 2 : 4);
   const int need = (nvec + vpt - 1) / vpt;
   const int threads = need < 32 ? 32 : ((need + 31) / 32) * 32;
@@ -646,21 +832,6 @@ cudaError_t launch_cluster_rows(const __nv_bfloat16* in, int64_t ld, int8_t* q, 
   cfg.attrs = attr;
   cfg.numAttrs = 2;
   return cudaLaunchKernelEx(&cfg, rows_cluster_kernel<VPT, SILU>, in, ld, q, scale, y, width);
-}
-
-// Resident CTAs per SM of a kernel at a given block size and dynamic shared
-// memory, queried once per device and kernel instance.
-template <typename Kernel>
-int resident_ctas(Kernel kernel, int threads, size_t smem) {
-  static int cached[64] = {0};
-  const int dev = w8a8::current_device();
-  if (dev < 0 || dev >= 64) return 1;
-  if (cached[dev] == 0) {
-    int n = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kernel, threads, smem) != cudaSuccess || n < 1) n = 1;
-    cached[dev] = n;
-  }
-  return cached[dev];
 }
 
 template <int VPT, int G>

@@ -33,8 +33,12 @@ def _ulp_diff(a, b):
     return (ai - bi).abs()
 
 
+# one CTA per row below 2 x 148 rows; warp groups (1, 2 or 4 warps per row,
+# persistent grid) from there on
 @pytest.mark.parametrize("m,k,residual", [(1, 1024, False), (7, 4096, True), (256, 5120, True),
-                                          (33, 8192, False), (100, 2048, True), (5, 24, True)])
+                                          (33, 8192, False), (100, 2048, True), (5, 24, True),
+                                          (300, 5120, True), (4096, 5120, True), (1000, 8192, False),
+                                          (600, 2048, True), (777, 256, False), (300, 64, True)])
 def test_rmsnorm_quant_matches_oracle(pkg, oracle, cuda_dev, m, k, residual):
     x, w, r = _data(m, k, m * 31 + k, residual)
     qw, sw, yw, resw = oracle.rmsnorm_quant(x, w, EPS, r)
