@@ -749,8 +749,11 @@ cudaError_t launch_rmsnorm_warp(const __nv_bfloat16* x, int64_t ldx, const __nv_
 }
 
 // The warp-group RMSNorm for `nvec` vectors per row: the fewest warps (1, 2
-// or 4) that keep a lane's vectors at 8 or fewer (x and the residual are both
-// held); not launched when 4 warps are not enough (K > 8192: the one-CTA kernel).
+// or 4) that keep a lane's vectors at 6 or fewer (x and the residual are both
+// held); not launched when 4 warps are not enough.  Measured against the
+// one-CTA-per-row kernel: faster at K = 5120 (6 vectors per lane, 4 warps),
+// slower at 8 vectors per lane (K = 8192, 4 warps; K = 4096, 2 warps), where
+// the registers leave too few groups resident.
 template <bool ADD>
 int launch_rmsnorm_warp_any(const __nv_bfloat16* x, int64_t ldx, const __nv_bfloat16* res, int64_t ldr,
                             const __nv_bfloat16* w, float eps, int8_t* q, float* scale, __nv_bfloat16* res_out,
@@ -759,7 +762,7 @@ int launch_rmsnorm_warp_any(const __nv_bfloat16* x, int64_t ldx, const __nv_bflo
   *launched = false;
   int g = 0;
   for (int c = 1; c <= 4 && g == 0; c *= 2)
-    if ((nvec + 32 * c - 1) / (32 * c) <= 8) g = c;
+    if ((nvec + 32 * c - 1) / (32 * c) <= 6) g = c;
   if (g == 0) return W8A8_OK;
   const int vpt = (nvec + 32 * g - 1) / (32 * g);
 #define W8A8_RMS(V, GG)                                                                                        \
