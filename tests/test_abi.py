@@ -76,6 +76,17 @@ def test_host_validation_rejects_bad_arguments(pkg):
     assert st == L.ERR_INVALID_ARG and b"together" in lib.w8a8_last_error()
     st = lib.w8a8_silu_mul_quant(16, 32, None, None, None, 2, 16, None)
     assert st == L.ERR_INVALID_ARG and b"nothing to write" in lib.w8a8_last_error()
+    # gate_up GEMM with the SiLU epilogue and the quantiser with a known absmax
+    st = lib.w8a8_gemm_silu(16, 16, 16, 16, None, 16, None, 4, 512, 256, None, 0, None)
+    assert st == L.ERR_INVALID_ARG and b"amax" in lib.w8a8_last_error()
+    assert lib.w8a8_gemm_silu(None, None, None, None, None, None, None, 0, 512, 256, None, 0, None) == L.OK
+    st = lib.w8a8_quant_rows_amax(None, 16, None, None, None, 4, 16, None)
+    assert st == L.ERR_INVALID_ARG and b"null" in lib.w8a8_last_error()
+    st = lib.w8a8_quant_rows_amax(16, 16, 16, 16, 16, 4, 12, None)
+    assert st == L.ERR_INVALID_ARG and b"multiple of 8" in lib.w8a8_last_error()
+    st = lib.w8a8_quant_rows_amax(24, 16, 16, 16, 16, 4, 16, None)
+    assert st == L.ERR_ALIGNMENT
+    assert lib.w8a8_quant_rows_amax(None, 16, None, None, None, 0, 16, None) == L.OK
     # broadcast / peak probe: rejected on the host
     assert lib.w8a8_broadcast(None, 16, 16, 0, None) == L.ERR_INVALID_ARG
     assert lib.w8a8_mma_peak_probe(2, 10, None, None) == L.ERR_INVALID_ARG
