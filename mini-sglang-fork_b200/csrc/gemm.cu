@@ -177,6 +177,14 @@ int run_gemm(const int8_t* A, const int8_t* B, const float* sa, const float* sb,
                  "gemm_allreduce: %d padded %dx%d output tiles exceed the communicator's max_bytes %llu", p.num_tiles,
                  p.swap ? p.bn : 128, p.swap ? 128 : p.bn, comm->slot_bytes);
   }
+  if (p.variant == 7 && (comm != nullptr || silu_amax != nullptr) && p.pair_split) {
+    // the K split of the last wave is a plain-epilogue schedule: the fused
+    // reduce and the SiLU epilogue deal whole blocks
+    p.pair_split = 0;
+    p.cut_tiles = false;
+    p.ws_counter_bytes = 0;
+    p.ws_bytes = 0;
+  }
   if (p.cut_tiles) {
     W8A8_REQUIRE(workspace != nullptr && workspace_bytes >= p.ws_bytes, W8A8_ERR_WORKSPACE,
                  "gemm: stream-K needs a workspace of %zu bytes with zeroed counters", p.ws_bytes);
@@ -222,6 +230,8 @@ int run_gemm(const int8_t* A, const int8_t* B, const float* sa, const float* sb,
   args.units = p.units;
   args.wide_fast = p.wide_fast;
   args.vec_scales = ((reinterpret_cast<uintptr_t>(sb) & 15u) == 0 && (reinterpret_cast<uintptr_t>(bias) & 15u) == 0) ? 1 : 0;
+  // the K split of the pair kernel's last wave: plain, non-SiLU epilogue only
+  args.pair_split = p.pair_split;
   if (silu_amax) {
     args.silu_i = static_cast<int>(N / 2);
     args.amax = silu_amax;

@@ -81,6 +81,42 @@ __device__ __forceinline__ void pair_coords(const GemmArgs& a, int pairs_w, int 
   }
 }
 
+// The work of one CTA pair (cluster c of G): whole blocks c, c + G, ... and,
+// when the last wave is split along K (args.pair_split = s > 1), after them
+// one fragment f = c of the last wave's rem = num_pairs % G blocks: block
+// num_pairs - rem + f / s, k blocks [j kb / s, (j + 1) kb / s) with j = f % s.
+// Every role of both CTAs walks the same sequence.
+struct PairWalk {
+  int p, num_pairs, G, full, split, frag;
+  __device__ __forceinline__ PairWalk(const GemmArgs& a, int num_pairs_, int c, int G_)
+      : p(c), num_pairs(num_pairs_), G(G_), full(num_pairs_), split(a.pair_split > 1 ? a.pair_split : 0),
+        frag(-1) {
+    if (split) {
+      const int rem = num_pairs % G;
+      full = num_pairs - rem;
+      frag = c < rem * split ? c : -1;
+    }
+  }
+  // block, k range, j (-1: whole block)
+  __device__ __forceinline__ bool next(const GemmArgs& a, int& blk, int& kb0, int& kb1, int& j) {
+    if (p < full) {
+      blk = p;
+      kb0 = 0;
+      kb1 = a.kblocks;
+      j = -1;
+      p += G;
+      return true;
+    }
+    if (frag < 0) return false;
+    blk = full + frag / split;
+    j = frag % split;
+    kb0 = j * a.kblocks / split;
+    kb1 = (j + 1) * a.kblocks / split;
+    frag = -1;
+    return true;
+  }
+};
+
 // Index of output tile (tw, tn) in tile_coords' numbering.
 __device__ __forceinline__ int tile_index(const GemmArgs& a, int tw, int tn) {
   return a.wide_fast ? tn * a.tiles_w + tw : tw * a.tiles_n + tn;
@@ -157,11 +193,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(gemm2_block_threads<
       uint32_t phase = 0;
       uint32_t issued_mask = 0, issued_phase = 0;
       bool ok = true;
-      for (int p = cluster; p < num_pairs && ok; p += nclusters) {
+      PairWalk walk(args, num_pairs, cluster, nclusters);
+      int p, kb0, kb1, jf;
+      while (ok && walk.next(args, p, kb0, kb1, jf)) {
         int pw, tn;
         pair_coords(args, pairs_w, p, pw, tn);
         const int tw = 2 * pw + static_cast<int>(half);
-        for (int kb = 0; kb < args.kblocks; ++kb) {
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!dev::mbar_wait(dev::smem_u32(empty + stage), phase ^ 1u, abort_flag, args.err, kErrGemmWait,
                               tmo)) {
             ok = false;
@@ -207,14 +245,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(gemm2_block_threads<
       int acc = 0;
       uint32_t acc_phase = 0;
       bool ok = true;
-      for (int p = cluster; p < num_pairs && ok; p += nclusters) {
+      PairWalk walk(args, num_pairs, cluster, nclusters);
+      int p, kb0, kb1, jf;
+      while (ok && walk.next(args, p, kb0, kb1, jf)) {
         if (!dev::mbar_wait_cluster(dev::smem_u32(acc_empty + acc), acc_phase ^ 1u, abort_flag, args.err,
                                     kErrGemmWait, tmo)) {
           break;
         }
         dev::tc_fence_after();
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * T::kAccCols);
-        for (int kb = 0; kb < args.kblocks; ++kb) {
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!dev::mbar_wait(dev::smem_u32(full + stage), phase, abort_flag, args.err, kErrGemmWait, tmo)) {
             ok = false;
             break;
@@ -225,7 +265,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(gemm2_block_threads<
 #pragma unroll
           for (int k = 0; k < T::kBK / 32; ++k) {
             const uint64_t off = static_cast<uint64_t>((k * 32) >> 4);
-            dev::mma_i8_pair(d_tmem, da + off, db + off, T::kIdesc, (kb > 0 || k > 0) ? 1u : 0u);
+            dev::mma_i8_pair(d_tmem, da + off, db + off, T::kIdesc, (kb > kb0 || k > 0) ? 1u : 0u);
           }
           dev::tc_commit_pair(dev::smem_u32(empty + stage));
           dev::tc_commit_pair(dev::mapa(dev::smem_u32(empty + stage), 1));
@@ -291,7 +331,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(gemm2_block_threads<
     uint32_t sig_n = 0;
     uint32_t blk = 0;
     bool aborted = false;
-    for (int p = cluster; p < num_pairs; p += nclusters) {
+    PairWalk walk(args, num_pairs, cluster, nclusters);
+    int p, kb0, kb1, jf;
+    while (walk.next(args, p, kb0, kb1, jf)) {
       int pw, tn;
       pair_coords(args, pairs_w, p, pw, tn);
       const int tw = 2 * pw + static_cast<int>(half);
@@ -361,6 +403,100 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(gemm2_block_threads<
             }
           }
           if (real && row < args.M) atomicMax(args.amax + row, __float_as_uint(act::absmax_of(m2)));
+          if (++acc == 2) {
+            acc = 0;
+            acc_phase ^= 1u;
+          }
+          continue;
+        }
+      }
+      if constexpr (!FUSED) {
+        if (jf >= 0) {
+          // A fragment of a last-wave block (split along K).  The CTA of each
+          // half holds 128 rows x 256 columns of partial int32 sums.  Shares
+          // j > 0 are parked in this CTA's slot (layout [chunk][quarter]
+          // [8 column groups][lane][4 columns]: each warp store covers 512
+          // contiguous bytes) and counted in the half's counter; the share
+          // j = 0 (its pair is the block's owner) waits (bounded) for the
+          // others' count, adds their slots (same half, CTAs of the next
+          // pairs) and writes the block.  Shares never wait on anything, so
+          // no pair waits on a pair that waits.
+          int4* slots = reinterpret_cast<int4*>(args.ws);
+          constexpr int kSlotInt4 = 128 * 256 / 4;
+          uint32_t* counter = args.counters + 2 * p + static_cast<int>(half);
+          if (jf > 0) {
+            int4* mine = slots + static_cast<size_t>(blockIdx.x) * kSlotInt4;
+#pragma unroll 1
+            for (int c = c0; c < c0 + kChunksPerWarp; ++c) {
+              uint32_t v[32];
+              dev::tmem_ld32(t_acc + c * 32, v);
+              dev::tmem_wait_ld(v);
+              int4* dst = mine + ((c * 4 + quarter) * 8) * 32 + lane;
+#pragma unroll
+              for (int q = 0; q < 8; ++q)
+                __stcg(dst + q * 32, make_int4(static_cast<int>(v[4 * q]), static_cast<int>(v[4 * q + 1]),
+                                               static_cast<int>(v[4 * q + 2]), static_cast<int>(v[4 * q + 3])));
+            }
+            dev::tc_fence_before();
+            const uint32_t bar = dev::smem_u32(acc_empty + acc);
+            if (half == 0) {
+              dev::mbar_arrive(bar);
+            } else {
+              dev::mbar_arrive_cluster(dev::mapa(bar, 0));
+            }
+            // one fence after the barrier orders every epilogue thread's slot
+            // stores before the count
+            dev::named_bar_sync(1, kEpiThreads);
+            if (et == 0) {
+              __threadfence();
+              atomicAdd(counter, 1u);
+            }
+          } else {
+            bool counted = true;
+            if (et == 0)
+              counted = dev::wait_counter(counter, static_cast<uint32_t>(args.pair_split - 1), abort_flag,
+                                          args.err, kErrGemmWait, tmo);
+            if (dev::named_bar_or(1, kEpiThreads, !counted)) {
+              aborted = true;
+              break;
+            }
+            const int first = cluster;  // this pair holds share 0; shares 1..s-1 are the next pairs
+#pragma unroll 1
+            for (int c = c0; c < c0 + kChunksPerWarp; ++c) {
+              uint32_t v[32];
+              dev::tmem_ld32(t_acc + c * 32, v);
+              dev::tmem_wait_ld(v);
+#pragma unroll 1
+              for (int o = 1; o < args.pair_split; ++o) {
+                const int cta = 2 * (first + o) + static_cast<int>(half);
+                const int4* src = slots + static_cast<size_t>(cta) * kSlotInt4 + ((c * 4 + quarter) * 8) * 32 + lane;
+                int4 qv[8];
+#pragma unroll
+                for (int q = 0; q < 8; ++q) qv[q] = __ldcg(src + q * 32);
+#pragma unroll
+                for (int q = 0; q < 8; ++q) {  // two's-complement sums, as int32
+                  v[4 * q] += static_cast<uint32_t>(qv[q].x);
+                  v[4 * q + 1] += static_cast<uint32_t>(qv[q].y);
+                  v[4 * q + 2] += static_cast<uint32_t>(qv[q].z);
+                  v[4 * q + 3] += static_cast<uint32_t>(qv[q].w);
+                }
+              }
+              if (c == c0 + kChunksPerWarp - 1) {
+                dev::tc_fence_before();
+                const uint32_t bar = dev::smem_u32(acc_empty + acc);
+                if (half == 0) {
+                  dev::mbar_arrive(bar);
+                } else {
+                  dev::mbar_arrive_cluster(dev::mapa(bar, 0));
+                }
+              }
+              if (real) {
+                store_chunk_smem(args, row, tn * 256 + c * 32, sam, sbs + c * 32, bss + c * 32, v, emit16);
+                store_staged_chunk(args, stg, lane, tw * 128 + quarter * 32, tn * 256 + c * 32);
+              }
+            }
+            if (et == 0) *counter = 0u;
+          }
           if (++acc == 2) {
             acc = 0;
             acc_phase ^= 1u;

@@ -5,7 +5,8 @@
 //   1: normal, BN = 256   2: normal, BN = 128
 //   3..6: weight-stationary (swap), BN = 16 / 32 / 64 / 128 token columns
 //   7: CTA pairs with the 2-SM MMA, 256 x 256 blocks (two 128 x 256 tiles),
-//      whole blocks in grid-stride order over SM pairs (prefill shapes)
+//      whole blocks in grid-stride order over SM pairs (prefill shapes); a
+//      last wave at most half full is split along K over the idle pairs
 // Schedule: stream-K over G persistent CTAs (one per SM by default).  The
 // k-block iterations of all tiles are split evenly between the CTAs; tiles cut
 // by a CTA boundary are finished through the workspace (two int32 tile slots
@@ -33,6 +34,7 @@ struct GemmPlan {
   bool cut_tiles;           // some tile is shared by two or more CTAs
   size_t ws_counter_bytes;  // tile counters at the workspace head
   size_t ws_bytes;          // total workspace bytes needed (0 if no tile is cut)
+  int pair_split;           // pair variant: the last, partial wave's blocks split this many ways along K (0: none)
 };
 
 constexpr int kMaxVariant = 7;
@@ -61,6 +63,13 @@ inline size_t round_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 // call's partial tiles.
 constexpr int kMaxCounterTiles = 65536;
 constexpr size_t kCounterBytes = static_cast<size_t>(kMaxCounterTiles) * 4;
+
+// Counter words a plan uses at the workspace head: one per tile, or for the
+// pair variant one per 128-row half of each 256 x 256 block.
+inline size_t plan_counter_words(const GemmPlan& p) {
+  if (p.variant == 7) return 2 * static_cast<size_t>((p.tiles_w + 1) / 2) * p.tiles_n;
+  return static_cast<size_t>(p.num_tiles);
+}
 
 // Returns 0 and fills *p; nonzero on invalid input.  ctas_req = 0 picks one
 // CTA per SM.
@@ -96,8 +105,9 @@ inline int plan_gemm(int64_t M, int64_t N, int64_t K, int variant, int ctas_req,
   p->tiles_n = static_cast<int>((rows_n + p->bn - 1) / p->bn);
   p->num_tiles = p->tiles_w * p->tiles_n;
   p->kblocks = static_cast<int>((K + 127) / 128);
+  p->pair_split = 0;
   if (v == 7) {
-    // whole 256 x 256 blocks over SM pairs; no stream-K, no workspace
+    // whole 256 x 256 blocks over SM pairs in grid-stride order
     const int64_t pairs = static_cast<int64_t>((p->tiles_w + 1) / 2) * p->tiles_n;
     int64_t clusters = ctas_req > 0 ? ctas_req / 2 : nsm / 2;
     if (clusters > nsm / 2) clusters = nsm / 2;
@@ -112,6 +122,24 @@ inline int plan_gemm(int64_t M, int64_t N, int64_t K, int variant, int ctas_req,
     p->ws_counter_bytes = 0;
     p->ws_bytes = 0;
     p->wide_fast = (rows_w <= rows_n) ? 1 : 0;
+    // A last wave at most half full (e.g. 320 blocks on 74 pairs: 4 full
+    // waves and 24 blocks) is split along K: each of its blocks goes to
+    // `split` pairs, each taking a contiguous share of the k blocks (at least
+    // 8), and the pair holding the first share adds the others' int32 shares
+    // (one slot of 128 x 256 int32 per CTA, one counter per 128-row half).
+    const int64_t rem = pairs % clusters;
+    if (pairs >= clusters && rem > 0 && 2 * rem <= clusters) {
+      int split = static_cast<int>(clusters / rem);
+      if (split > 4) split = 4;
+      while (split > 1 && p->kblocks / split < 8) --split;
+      const size_t need = kCounterBytes + static_cast<size_t>(2 * clusters) * 128 * 256 * 4;
+      if (split >= 2 && need <= ws_avail && 2 * pairs <= kMaxCounterTiles) {
+        p->pair_split = split;
+        p->cut_tiles = true;
+        p->ws_counter_bytes = kCounterBytes;
+        p->ws_bytes = need;
+      }
+    }
     return 0;
   }
   const long long total_iters = static_cast<long long>(p->num_tiles) * p->kblocks;

@@ -93,6 +93,9 @@ struct GemmArgs {
   // [M, I] (ldc = I); amax[m] collects max |y| of row m as float bits.
   int silu_i;
   uint32_t* amax;
+  // pair kernel: the blocks of the last, partial wave are split pair_split
+  // ways along K (0: every block whole); slots in ws, counters per 128-row half
+  int pair_split;
 };
 
 // Shared memory of the fused epilogue and reduction state (FusedState, below).

@@ -104,7 +104,7 @@ int w8a8_gemm_static_scratch(const int8_t* A, const int8_t* B, const float* sa, 
   if (rc) return rc;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (p.cut_tiles)
-    W8A8_CUDA_TRY(cudaMemsetAsync(scratch, 0, static_cast<size_t>(p.num_tiles) * sizeof(uint32_t), s));
+    W8A8_CUDA_TRY(cudaMemsetAsync(scratch, 0, w8a8::plan_counter_words(p) * sizeof(uint32_t), s));
   return w8a8::run_gemm(A, B, sa, sb, bias, C, c_i32, M, N, K, 0, 0, scratch, kStaticScratchBytes, s,
                         w8a8::kDefaultGemmTimeoutNs, nullptr);
 }

@@ -107,7 +107,9 @@ def test_planner_variant_choice(pkg, m, n, k, variant, bn, swap):
     assert p["kblocks"] == (k + 127) // 128
     assert p["gran"] in (1, p["kblocks"])
     if p["workspace_bytes"]:
-        assert p["workspace_bytes"] >= 2 * p["grid"] * 128 * p["bn"] * 4
+        # stream-K: two int32 tile slots per CTA; pair variant: one 128 x 256 slot per CTA
+        slots = 1 if p["variant"] == 7 else 2
+        assert p["workspace_bytes"] >= slots * p["grid"] * 128 * p["bn"] * 4
 
 
 def _schedule(tiles, kblocks, grid, gran=1):
@@ -210,6 +212,42 @@ def test_planner_stream_k_balances_few_tiles(pkg):
     # the pair variant deals whole 256 x 256 blocks to an even number of CTAs
     p = pkg.ops.gemm_plan(8192, 24576, 4096)
     assert p["variant"] == 7 and p["grid"] == 148 and p["workspace_bytes"] == 0
+
+
+def _pair_split(pairs, clusters, kblocks):
+    """Host model of the pair variant's last-wave K split (plan_gemm): a last
+    wave at most half full goes to min(clusters // rem, 4) pairs per block,
+    each with at least 8 k blocks."""
+    rem = pairs % clusters
+    if pairs < clusters or rem == 0 or 2 * rem > clusters:
+        return 0
+    split = min(clusters // rem, 4)
+    while split > 1 and kblocks // split < 8:
+        split -= 1
+    return split if split >= 2 else 0
+
+
+@pytest.mark.parametrize("m,n,k,ctas", [
+    (4096, 5120, 25600, 0), (4096, 5120, 8192, 0),       # 320 blocks on 74 pairs: 24 left, split 3
+    (8192, 24576, 4096, 0),                              # 3072 blocks: 38 left, more than half a wave
+    (1100, 1024, 2128, 16), (500, 1200, 4224, 18), (1280, 1024, 3200, 18), (1280, 1024, 2176, 12),
+    (1280, 1024, 2176, 10),                              # 20 blocks on 5 pairs: no last wave
+    (1280, 1024, 1024, 12),                              # 8 k blocks: shares would be under 8
+])
+def test_planner_pair_last_wave_split(pkg, m, n, k, ctas):
+    p = pkg.ops.gemm_plan(m, n, k, variant=7, ctas=ctas, num_sms=148)
+    pairs = ((m + 255) // 256) * ((n + 255) // 256)
+    clusters = p["grid"] // 2
+    split = _pair_split(pairs, clusters, (k + 127) // 128)
+    if split:
+        assert p["workspace_bytes"] == 256 * 1024 + p["grid"] * 128 * 256 * 4
+    else:
+        assert p["workspace_bytes"] == 0
+    # a workspace too small for the slots keeps whole blocks
+    q = pkg.ops.gemm_plan(m, n, k, variant=7, ctas=ctas, num_sms=148, workspace_bytes=1 << 20)
+    assert q["workspace_bytes"] == 0 and q["grid"] == p["grid"]
+    if (m, n, k, ctas) == (4096, 5120, 25600, 0):
+        assert split == 3
 
 
 def test_every_plan_fits_the_static_scratch(pkg):

@@ -82,6 +82,25 @@ def test_gemm_pair_variant_bit_exact(pkg, oracle, cuda_dev, m, n, k, ctas):
     _check(pkg, oracle, cuda_dev, m, n, k, variant=7, ctas=ctas, bias=(m % 2 == 0), seed=m + ctas)
 
 
+@pytest.mark.parametrize("m,n,k,ctas", [
+    (1100, 1024, 2128, 16),   # 20 blocks on 8 pairs: 4 left, split 2 (17 k blocks: 8 + 9), phantom half
+    (500, 1200, 4224, 18),    # 10 blocks on 9 pairs: 1 left, split 4 (33 k blocks), N tail
+    (1280, 1024, 3200, 18),   # 20 blocks on 9 pairs: 2 left, split 3 (25 k blocks; 4 would leave 6 each)
+    (1280, 1024, 2176, 12),   # 20 blocks on 6 pairs: 2 left, split 2 (3 would leave 5 k blocks each)
+])
+def test_gemm_pair_last_wave_split(pkg, oracle, cuda_dev, m, n, k, ctas):
+    """Pair variant with its last, partial wave split along K over the idle
+    pairs: share j > 0 parks its int32 partial sums in the workspace, the pair
+    holding share 0 adds them.  Bit-exact, and the counters return to zero."""
+    p = pkg.ops.gemm_plan(m, n, k, variant=7, ctas=ctas,
+                          num_sms=torch.cuda.get_device_properties(0).multi_processor_count)
+    assert p["workspace_bytes"] > 0   # the split is planned
+    for rep in range(2):
+        _check(pkg, oracle, cuda_dev, m, n, k, variant=7, ctas=ctas, bias=(rep == 1), seed=m + k + rep)
+    ws = pkg.ops.gemm_workspace(cuda_dev)
+    assert int(ws[: 65536 * 4].count_nonzero()) == 0
+
+
 def test_stream_k_counters_return_to_zero(pkg, oracle, cuda_dev):
     """Back-to-back stream-K calls of different shapes sharing the workspace:
     every call leaves the tile counters at the workspace head zeroed, and no
