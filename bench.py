@@ -1159,6 +1159,99 @@ def run_gemm_only(args, dev):
                       "plans": [pkg.ops.gemm_plan(a.shape[0], w.shape[0], a.shape[1]) for a, w, *_ in shapes]}))
 
 
+# Mixture-of-experts layer (the experts of Qwen3-30B-A3B's MoE MLP): not a
+# BASELINE configuration; measured so the grouped GEMM has a throughput and
+# roofline record beside the dense path.
+MOE_SHAPE = {"experts": 128, "topk": 8, "hidden": 2048, "inter": 768}
+
+
+def run_moe(args, dev):
+    """``--moe``: the W8A8 experts of one MoE layer (align, quantise-scatter,
+    gate_up grouped GEMM with SiLU*mul, quantiser, down grouped GEMM with the
+    routing weight, top-k sum) at each M of ``--moe-m``; random int8 expert
+    weights, seeded N(0, 1) activations and router logits routed with the
+    reference's fused_topk arithmetic.  Per-stage device times from CUDA-graph
+    replays (L2 flushed before each), and the grouped GEMMs' int8 throughput
+    against the measured MMA ceiling and against this library's dense GEMM on
+    the same operation count."""
+    pkg = _pkg()
+    ops = pkg.ops
+    E, K, H, I = MOE_SHAPE["experts"], MOE_SHAPE["topk"], MOE_SHAPE["hidden"], MOE_SHAPE["inter"]
+    g = torch.Generator(device=dev).manual_seed(0)
+    w1q = torch.randint(-127, 128, (E, 2 * I, H), dtype=torch.int8, device=dev, generator=g)
+    w2q = torch.randint(-127, 128, (E, H, I), dtype=torch.int8, device=dev, generator=g)
+    sw1 = torch.rand(E, 2 * I, device=dev, generator=g) * 1e-3 + 1e-5
+    sw2 = torch.rand(E, H, device=dev, generator=g) * 1e-3 + 1e-5
+    stream = torch.cuda.Stream(dev)
+    flush_buf = torch.zeros(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
+    ops.gemm_workspace(dev)
+    peak = int8_peak(pkg, stream)
+    reps = max(args.steps, 5)
+    per_m = {}
+    for m in args.moe_m:
+        x = torch.randn(m, H, device=dev, generator=g).bfloat16()
+        logits = torch.randn(m, E, device=dev, generator=g)
+        p = torch.softmax(logits.float(), dim=-1)
+        w, ids = torch.topk(p, K, dim=-1)
+        w = w / w.sum(-1, keepdim=True)
+        w = (w / (w.sum(-1, keepdim=True) + 1e-8)).contiguous()
+        ids = ids.to(torch.int32).contiguous()
+        total, _, out = time_graph(lambda: ops.fused_experts_w8a8(x, w1q, sw1, w2q, sw2, w, ids), reps,
+                                   max(args.warmup, 3), flush_buf, stream)
+        layer_ms = total / reps
+        r = ops.moe_align(ids, E)
+        q = ops.moe_quant_scatter(x, r)
+        y, amax = ops.moe_gemm(q, r.sa_sorted, w1q, sw1, r, silu=True)
+        qy = ops.moe_quant_rows(y, amax, r)
+        c3 = ops.moe_gemm(qy.q, qy.s, w2q, sw2, r, route_w=w)
+        torch.cuda.synchronize()
+        nb = int(r.num_blocks.item())
+        st = {
+            "align": time_kernel_events(lambda: ops.moe_align(ids, E), reps, flush_buf, stream),
+            "quant_scatter": time_kernel_events(lambda: ops.moe_quant_scatter(x, r), reps, flush_buf, stream),
+            "gate_up_silu": time_kernel_events(lambda: ops.moe_gemm(q, r.sa_sorted, w1q, sw1, r, silu=True), reps,
+                                               flush_buf, stream),
+            "quant_y": time_kernel_events(lambda: ops.moe_quant_rows(y, amax, r), reps, flush_buf, stream),
+            "down": time_kernel_events(lambda: ops.moe_gemm(qy.q, qy.s, w2q, sw2, r, route_w=w), reps, flush_buf,
+                                       stream),
+            "topk_sum": time_kernel_events(lambda: ops.moe_sum(c3, r), reps, flush_buf, stream),
+        }
+        slots = m * K
+        ops1, ops2 = 2.0 * slots * 2 * I * H, 2.0 * slots * H * I
+        active = int(torch.unique(ids).numel())
+        wbytes1, wbytes2 = active * 2 * I * H, active * H * I
+        rec = {
+            "tokens_per_s": round(m / (layer_ms * 1e-3), 1), "layer_us": round(layer_ms * 1e3, 2),
+            "stages_us": {k_: round(v * 1e3, 2) for k_, v in st.items()},
+            "blocks": nb, "padding_rows_frac": round(1.0 - slots / max(nb * 128, 1), 4), "active_experts": active,
+            "gate_up_tops": round(ops1 / (st["gate_up_silu"] * 1e-3) / 1e12, 1),
+            "down_tops": round(ops2 / (st["down"] * 1e-3) / 1e12, 1),
+            "gate_up_weight_gbs": round(wbytes1 / (st["gate_up_silu"] * 1e-3) / 1e9, 1),
+            "down_weight_gbs": round(wbytes2 / (st["down"] * 1e-3) / 1e9, 1),
+        }
+        if m >= 512:
+            # dense yardstick: one W8A8 GEMM with the gate_up's operation count
+            a = torch.randint(-127, 128, (slots, H), dtype=torch.int8, device=dev, generator=g)
+            sa = torch.rand(slots, device=dev, generator=g) * 1e-3
+            wd, sd = w1q[0].contiguous(), sw1[0].contiguous()
+            dense_ms = time_kernel_events(lambda: ops.w8a8_gemm(a, wd, sa, sd), reps, flush_buf, stream)
+            rec["dense_same_ops_us"] = round(dense_ms * 1e3, 2)
+            rec["gate_up_vs_dense"] = round(dense_ms / st["gate_up_silu"], 3)
+        per_m[str(m)] = rec
+        del out, r, q, y, amax, qy, c3
+    assert ops.device_error() == 0
+    head = per_m[str(args.moe_m[-1])]
+    return {
+        "metric": "W8A8 MoE-layer tokens/s (experts of a Qwen3-30B-A3B MoE MLP: 128 experts, top-8, H 2048, I 768)",
+        "value": head["tokens_per_s"], "unit": "tokens/s", "n_gpus": 1, "steps": reps, "warmup": max(args.warmup, 3),
+        "higher_is_better": True, "dtype": "int8 (int32 accumulate, fp32 dequant, bf16 out)",
+        "data": "synthetic: random int8 expert weights, seeded N(0,1) activations and router logits",
+        "config": {"workload": "moe", "M": args.moe_m[-1], **MOE_SHAPE,
+                   "l2": "flushed before every timed replay (256 MB written, then read back)"},
+        "int8_peak_tops": peak, "per_m": per_m,
+    }
+
+
 def run_kernel_only(args, dev):
     """Profiling entry: three rounds of [quantiser, gate_up GEMM, fused
     SiLU*mul+quant], then three of the fused residual-add + RMSNorm +
@@ -1192,6 +1285,9 @@ def main():
     ap.add_argument("--gemm", default="", help="profiling entry: GEMM shapes MxNxK,... (see run_gemm_only)")
     ap.add_argument("--silu", action="store_true",
                     help="with --gemm: the GEMM with the SiLU*mul epilogue and the quantiser of its product")
+    ap.add_argument("--moe", action="store_true", help="MoE experts layer (see run_moe), not the headline")
+    ap.add_argument("--moe-m", type=lambda v: [int(x) for x in v.split(",") if x], default=[1, 64, 512, 4096],
+                    help="token counts for --moe (the last is the line's value)")
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
@@ -1233,6 +1329,9 @@ def main():
         return
     if args.kernel_only:
         run_kernel_only(args, dev)
+        return
+    if args.moe:
+        print(json.dumps(run_moe(args, dev)), flush=True)
         return
     if world > 1:
         torch.distributed.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,

@@ -171,6 +171,63 @@ int w8a8_mma_peak_probe(int pair, int64_t iters, int64_t* ops_out, void* stream)
 int w8a8_gemm_plan(int64_t M, int64_t N, int64_t K, int variant, int ctas, size_t workspace_bytes,
                    int num_sms, int64_t* out);
 
+/* ------------------------------------------------------ mixture of experts
+ * The expert path of fused_experts_impl (M/moe/fused.py:135-215) with int8
+ * expert weights: w1 [E, 2I, H] ([gate; up] per expert) and w2 [E, H, I],
+ * per-channel fp32 scales [E, 2I] / [E, H].  A slot s = t * topk + j is
+ * token t's j-th choice (topk_ids / topk_weights [T, topk], row-major).
+ * Sorted buffers have P = 128 * w8a8_moe_max_blocks(T * topk, E) rows; the
+ * calls chain on one stream with no host sync (CUDA-graph capturable):
+ *   w8a8_moe_align -> w8a8_moe_quant_scatter -> w8a8_moe_gemm (w1, SiLU)
+ *   -> w8a8_moe_quant_rows -> w8a8_moe_gemm (w2, routed) -> w8a8_moe_sum */
+
+/* Bound on the 128-row expert blocks of T * topk slots over E experts. */
+int64_t w8a8_moe_max_blocks(int64_t num_slots, int64_t num_experts);
+
+/* moe_align_block_size (M/moe/fused.py:32-83) with 128-row blocks: expert e
+ * gets ceil(c_e / 128) consecutive blocks, its c_e slots first (order within
+ * an expert unspecified), padding after.  Writes sorted_ids[P] (slot of each
+ * row; num_slots on padding), block_expert[max_blocks], num_blocks[1],
+ * inv_pos[num_slots] (row of each slot; -1 for an expert id outside [0, E),
+ * which then contributes nothing) and 0 to sa_sorted on padding rows.
+ * E <= 1024. */
+int w8a8_moe_align(const int32_t* topk_ids, int64_t num_slots, int num_experts, int32_t* sorted_ids,
+                   int32_t* block_expert, int32_t* num_blocks, int32_t* inv_pos, float* sa_sorted,
+                   void* stream);
+
+/* Per-token quantiser (w8a8_quant_per_token's rule) of x[T, K] whose int8 row
+ * and scale are written to rows inv_pos[t * topk + j] (skipped when < 0) of
+ * q_sorted[P, K] / sa_sorted[P].  K % 8 == 0, K <= 16384. */
+int w8a8_moe_quant_scatter(const void* x, int64_t ldx, int64_t T, int64_t K, const int32_t* inv_pos, int topk,
+                           int8_t* q_sorted, float* sa_sorted, void* stream);
+
+/* Grouped W8A8 GEMM over the expert-sorted rows (tcgen05, 128 x 256 tiles of
+ * one expert each; the blocks in use are read from num_blocks on the
+ * device).  w [E * N, K] int8, sw [E * N].
+ *  - silu_amax != null: w holds [gate; up] (N = 2I, N % 32 == 0); C [P, I]
+ *    receives y = bf16(silu(g) * u), g and u the bf16 dequantised gate and
+ *    up values, and silu_amax[P] (zeroed by the caller) each row's max |y|
+ *    as float bits -- fused_moe_kernel on w1 plus silu_and_mul.
+ *  - otherwise C [P, N] = bf16(((f32(acc) * sa) * sw) * route_w[slot]),
+ *    route_w (nullable; needs sorted_ids) the slot's routing weight --
+ *    fused_moe_kernel on w2 with MUL_ROUTED_WEIGHT.
+ * K % 16 == 0, N % 16 == 0, 16-byte aligned a_sorted, w, sw and C. */
+int w8a8_moe_gemm(const int8_t* a_sorted, const int8_t* w, const float* sa_sorted, const float* sw,
+                  const int32_t* block_expert, const int32_t* num_blocks, int64_t max_blocks,
+                  const int32_t* sorted_ids, const float* route_w, int64_t num_slots, void* C,
+                  uint32_t* silu_amax, int num_experts, int64_t N, int64_t K, void* stream);
+
+/* w8a8_quant_rows_amax over the rows in use (128 * *num_blocks, read on the
+ * device) of y[P, K]. */
+int w8a8_moe_quant_rows(const void* y, int64_t ldy, const uint32_t* amax, int8_t* q, float* scale,
+                        const int32_t* num_blocks, int64_t max_blocks, int64_t K, void* stream);
+
+/* moe_sum_reduce (M/kernel/triton/fused_moe.py:5-48): out[t] = bf16(sum over
+ * j = 0..topk-1 of f32(c_sorted[inv_pos[t * topk + j]])), an fp32 sum from
+ * zero in choice order; dropped choices add nothing.  H % 8 == 0. */
+int w8a8_moe_sum(const void* c_sorted, int64_t ldc, const int32_t* inv_pos, int64_t T, int topk, int64_t H,
+                 void* out, int64_t ldo, void* stream);
+
 /* ---------------------------------------------------------------- kernel 3
  * Tensor-parallel communicator over NVLink / NVSwitch peer memory.
  * Replaces NCCLWrapper (M/kernel/csrc/src/pynccl.cu:74-91) + init_pynccl

@@ -16,7 +16,7 @@ from .distributed import (DistributedCommunicator, DistributedInfo, destroy_dist
                           enable_peer_mem_distributed, get_tp_info, reset_tp_info, set_tp_info,
                           try_get_tp_info)
 from .layers import (BaseOP, GatedMLP, LinearColParallelMerged, LinearOProj, LinearQKVMerged,
-                     LinearReplicated, LinearRowParallel, RMSNormFusedQuant, silu_and_mul,
+                     LinearReplicated, LinearRowParallel, MoELayer, RMSNormFusedQuant, silu_and_mul,
                      silu_and_mul_quant)
 from .ops import QuantizedActivation, quant_per_token, w8a8_gemm
 from .weights import load_w8a8_state_dict, w8a8_weight_stream
@@ -25,6 +25,7 @@ __all__ = [
     "W8A8Error",
     "BaseOP",
     "GatedMLP",
+    "MoELayer",
     "LinearColParallelMerged",
     "LinearOProj",
     "LinearQKVMerged",

@@ -52,6 +52,13 @@ SIGNATURES = {
     "w8a8_quant_rows_amax": (_c_int, [_c_vp, _c_i64, _c_vp, _c_vp, _c_vp, _c_i64, _c_i64, _c_vp]),
     "w8a8_rmsnorm_quant": (_c_int, [_c_vp, _c_i64, _c_vp, _c_i64, _c_vp, ctypes.c_float, _c_vp, _c_vp,
                                     _c_vp, _c_vp, _c_i64, _c_i64, _c_vp]),
+    "w8a8_moe_max_blocks": (_c_i64, [_c_i64, _c_i64]),
+    "w8a8_moe_align": (_c_int, [_c_vp, _c_i64, _c_int, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp]),
+    "w8a8_moe_quant_scatter": (_c_int, [_c_vp, _c_i64, _c_i64, _c_i64, _c_vp, _c_int, _c_vp, _c_vp, _c_vp]),
+    "w8a8_moe_gemm": (_c_int, [_c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_i64, _c_vp, _c_vp, _c_i64, _c_vp,
+                               _c_vp, _c_int, _c_i64, _c_i64, _c_vp]),
+    "w8a8_moe_quant_rows": (_c_int, [_c_vp, _c_i64, _c_vp, _c_vp, _c_vp, _c_vp, _c_i64, _c_i64, _c_vp]),
+    "w8a8_moe_sum": (_c_int, [_c_vp, _c_i64, _c_vp, _c_i64, _c_int, _c_i64, _c_vp, _c_i64, _c_vp]),
     "w8a8_gemm_workspace_size": (_c_size, [_c_i64, _c_i64, _c_i64]),
     "w8a8_gemm": (_c_int, [_c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp,
                            _c_i64, _c_i64, _c_i64, _c_vp, _c_size, _c_vp]),

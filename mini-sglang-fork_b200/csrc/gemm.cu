@@ -31,6 +31,8 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
   return fn;
 }
 
+}  // namespace
+
 // Tensor map over a row-major int8 matrix [rows, K] read as boxes of
 // box_rows x 128 bytes with the 128-byte swizzle; out-of-range rows/columns
 // read as zero.
@@ -49,6 +51,8 @@ int encode_operand(CUtensorMap* tm, const void* base, int64_t rows, int64_t K, i
                (long long)rows, (long long)K, box_rows);
   return W8A8_OK;
 }
+
+namespace {
 
 template <int BN, int STAGES, bool SWAP, bool FUSED>
 int launch_variant(const GemmPlan& p, const CUtensorMap& tw, const CUtensorMap& tn, const GemmArgs& args,

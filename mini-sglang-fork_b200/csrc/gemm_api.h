@@ -2,6 +2,7 @@
 // points (gemm.cu) and the fused row-parallel GEMM + all-reduce (comm.cu).
 #pragma once
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 #include <cstddef>
@@ -20,6 +21,11 @@ int run_gemm(const int8_t* A, const int8_t* B, const float* sa, const float* sb,
              int32_t* c_i32, int64_t M, int64_t N, int64_t K, int variant, int ctas, void* workspace,
              size_t workspace_bytes, cudaStream_t stream, long long timeout_ns, const CommView* comm,
              uint32_t* silu_amax = nullptr);
+
+// Tensor map over a row-major int8 matrix [rows, K] (row stride K) read as
+// boxes of box_rows x 128 bytes with the 128-byte swizzle; out-of-range rows
+// and columns read as zero.
+int encode_operand(CUtensorMap* tm, const void* base, int64_t rows, int64_t K, int box_rows);
 
 // Host-side checks of a GEMM call (shape limits, null pointers, 16-byte
 // alignment) that run_gemm makes before any launch; 0 or a status code.

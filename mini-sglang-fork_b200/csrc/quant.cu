@@ -318,10 +318,12 @@ constexpr int kWarpThreads = 128;  // 4 warps: groups of G = 1, 2 or 4 (at most 
 #define W8A8_WARP_MAX_VPT 10  // vectors per lane before G doubles
 #endif
 
-template <int VPT, int G>
+template <int VPT, int G, bool SCATTER = false>
 __global__ void __launch_bounds__(kWarpThreads) rows_warp_kernel(const __nv_bfloat16* __restrict__ in, int64_t ld,
                                                                  int8_t* __restrict__ q, float* __restrict__ scale,
-                                                                 int64_t M, int width) {
+                                                                 int64_t M, int width,
+                                                                 const int32_t* __restrict__ dst_rows = nullptr,
+                                                                 int fanout = 0) {
   constexpr int kGroups = kWarpThreads / 32 / G;
   __shared__ float part[2][kWarpThreads / 32];  // per-warp maxima, by row parity
   w8a8::dev::griddep_launch();  // early trigger, as in rows_reg_kernel
@@ -360,13 +362,33 @@ __global__ void __launch_bounds__(kWarpThreads) rows_warp_kernel(const __nv_bflo
       for (int k = 0; k < G; ++k) amax = fmaxf(amax, p[k]);
     }
     const RowScale rs = row_scale(amax);
-    uint2* qr = reinterpret_cast<uint2*>(q + row * static_cast<int64_t>(width));
+    if constexpr (SCATTER) {
+      // mixture of experts: the row's int8 values and scale go to each of
+      // the rows dst_rows[row * fanout + f] (skipped when negative)
+      uint2 qv[VPT];
 #pragma unroll
-    for (int j = 0; j < VPT; ++j) {
-      const int vi = t + j * 32 * G;
-      if (vi < nvec) qr[vi] = quant_vec8(v[j], rs);
+      for (int j = 0; j < VPT; ++j)
+        if (t + j * 32 * G < nvec) qv[j] = quant_vec8(v[j], rs);
+      for (int f = 0; f < fanout; ++f) {
+        const int d = __ldg(dst_rows + row * fanout + f);
+        if (d < 0) continue;
+        uint2* qr = reinterpret_cast<uint2*>(q + static_cast<int64_t>(d) * width);
+#pragma unroll
+        for (int j = 0; j < VPT; ++j) {
+          const int vi = t + j * 32 * G;
+          if (vi < nvec) qr[vi] = qv[j];
+        }
+        if (t == 0) scale[d] = rs.s;
+      }
+    } else {
+      uint2* qr = reinterpret_cast<uint2*>(q + row * static_cast<int64_t>(width));
+#pragma unroll
+      for (int j = 0; j < VPT; ++j) {
+        const int vi = t + j * 32 * G;
+        if (vi < nvec) qr[vi] = quant_vec8(v[j], rs);
+      }
+      if (t == 0) scale[row] = rs.s;
     }
-    if (t == 0) scale[row] = rs.s;
   }
 }
 
@@ -380,11 +402,16 @@ constexpr int kAmaxVpt = 4;
 __global__ void __launch_bounds__(kAmaxThreads) rows_amax_kernel(const __nv_bfloat16* __restrict__ y, int64_t ld,
                                                                  const uint32_t* __restrict__ amax,
                                                                  int8_t* __restrict__ q, float* __restrict__ scale,
-                                                                 int64_t M, int width) {
+                                                                 int64_t M, int width,
+                                                                 const int32_t* __restrict__ num_blocks) {
   __shared__ float s_s, s_inv;
   __shared__ int s_exact;
   w8a8::dev::griddep_launch();  // early trigger, as in rows_reg_kernel
   w8a8::dev::griddep_wait();    // y and amax are the previous kernel's output
+  if (num_blocks != nullptr) {  // rows in use: the 128-row blocks of the expert-sorted layout
+    const int64_t used = static_cast<int64_t>(max(*num_blocks, 0)) * 128;
+    if (used < M) M = used;
+  }
   const int nvec = width >> 3;
   const int v0 = blockIdx.x * (kAmaxThreads * kAmaxVpt) + threadIdx.x;
   for (int64_t row = blockIdx.y; row < M; row += gridDim.y) {
@@ -837,29 +864,29 @@ cudaError_t launch_cluster_rows(const __nv_bfloat16* in, int64_t ld, int8_t* q, 
   return cudaLaunchKernelEx(&cfg, rows_cluster_kernel<VPT, SILU>, in, ld, q, scale, y, width);
 }
 
-template <int VPT, int G>
+template <int VPT, int G, bool SCATTER>
 cudaError_t launch_warp_rows(const __nv_bfloat16* in, int64_t ld, int8_t* q, float* scale, int64_t M, int width,
-                             int nsm, cudaStream_t s) {
+                             int nsm, cudaStream_t s, const int32_t* dst, int fanout) {
   constexpr int kGroups = kWarpThreads / 32 / G;
-  const int per_sm = resident_ctas(rows_warp_kernel<VPT, G>, kWarpThreads, 0);
+  const int per_sm = resident_ctas(rows_warp_kernel<VPT, G, SCATTER>, kWarpThreads, 0);
   int64_t grid = (M + kGroups - 1) / kGroups;
   const int64_t cap = static_cast<int64_t>(nsm) * per_sm;
   if (grid > cap) grid = cap;
-  return w8a8::launch_pdl(rows_warp_kernel<VPT, G>, dim3(static_cast<unsigned>(grid)), dim3(kWarpThreads), 0, s,
-                          in, ld, q, scale, M, width);
+  return w8a8::launch_pdl(rows_warp_kernel<VPT, G, SCATTER>, dim3(static_cast<unsigned>(grid)), dim3(kWarpThreads),
+                          0, s, in, ld, q, scale, M, width, dst, fanout);
 }
 
 // Vectors per lane rounded up to an instantiated count (2, 4, 6, 8, 10, 12, 16).
-template <int G>
+template <int G, bool SCATTER>
 cudaError_t launch_warp_rows_vpt(int vpt, const __nv_bfloat16* in, int64_t ld, int8_t* q, float* scale, int64_t M,
-                                 int width, int nsm, cudaStream_t s) {
-  if (vpt <= 2) return launch_warp_rows<2, G>(in, ld, q, scale, M, width, nsm, s);
-  if (vpt <= 4) return launch_warp_rows<4, G>(in, ld, q, scale, M, width, nsm, s);
-  if (vpt <= 6) return launch_warp_rows<6, G>(in, ld, q, scale, M, width, nsm, s);
-  if (vpt <= 8) return launch_warp_rows<8, G>(in, ld, q, scale, M, width, nsm, s);
-  if (vpt <= 10) return launch_warp_rows<10, G>(in, ld, q, scale, M, width, nsm, s);
-  if (vpt <= 12) return launch_warp_rows<12, G>(in, ld, q, scale, M, width, nsm, s);
-  return launch_warp_rows<16, G>(in, ld, q, scale, M, width, nsm, s);
+                                 int width, int nsm, cudaStream_t s, const int32_t* dst, int fanout) {
+  if (vpt <= 2) return launch_warp_rows<2, G, SCATTER>(in, ld, q, scale, M, width, nsm, s, dst, fanout);
+  if (vpt <= 4) return launch_warp_rows<4, G, SCATTER>(in, ld, q, scale, M, width, nsm, s, dst, fanout);
+  if (vpt <= 6) return launch_warp_rows<6, G, SCATTER>(in, ld, q, scale, M, width, nsm, s, dst, fanout);
+  if (vpt <= 8) return launch_warp_rows<8, G, SCATTER>(in, ld, q, scale, M, width, nsm, s, dst, fanout);
+  if (vpt <= 10) return launch_warp_rows<10, G, SCATTER>(in, ld, q, scale, M, width, nsm, s, dst, fanout);
+  if (vpt <= 12) return launch_warp_rows<12, G, SCATTER>(in, ld, q, scale, M, width, nsm, s, dst, fanout);
+  return launch_warp_rows<16, G, SCATTER>(in, ld, q, scale, M, width, nsm, s, dst, fanout);
 }
 
 // Warps per row for the warp-group path: the fewest (1, 2 or 4) that keep a
@@ -870,16 +897,22 @@ inline int warp_group_size(int nvec) {
   return (nvec + 127) / 128 <= 16 ? 4 : 0;
 }
 
-int launch_warp_group(const __nv_bfloat16* in, int64_t ld, int8_t* q, float* scale, int64_t M, int width, int g,
-                      int nsm, cudaStream_t s) {
+template <bool SCATTER>
+int launch_warp_group_t(const __nv_bfloat16* in, int64_t ld, int8_t* q, float* scale, int64_t M, int width, int g,
+                        int nsm, cudaStream_t s, const int32_t* dst, int fanout) {
   const int nvec = width / 8;
   const int vpt = (nvec + 32 * g - 1) / (32 * g);
   switch (g) {
-    case 1: W8A8_CUDA_TRY(launch_warp_rows_vpt<1>(vpt, in, ld, q, scale, M, width, nsm, s)); break;
-    case 2: W8A8_CUDA_TRY(launch_warp_rows_vpt<2>(vpt, in, ld, q, scale, M, width, nsm, s)); break;
-    default: W8A8_CUDA_TRY(launch_warp_rows_vpt<4>(vpt, in, ld, q, scale, M, width, nsm, s)); break;
+    case 1: W8A8_CUDA_TRY((launch_warp_rows_vpt<1, SCATTER>(vpt, in, ld, q, scale, M, width, nsm, s, dst, fanout))); break;
+    case 2: W8A8_CUDA_TRY((launch_warp_rows_vpt<2, SCATTER>(vpt, in, ld, q, scale, M, width, nsm, s, dst, fanout))); break;
+    default: W8A8_CUDA_TRY((launch_warp_rows_vpt<4, SCATTER>(vpt, in, ld, q, scale, M, width, nsm, s, dst, fanout))); break;
   }
   return W8A8_OK;
+}
+
+int launch_warp_group(const __nv_bfloat16* in, int64_t ld, int8_t* q, float* scale, int64_t M, int width, int g,
+                      int nsm, cudaStream_t s) {
+  return launch_warp_group_t<false>(in, ld, q, scale, M, width, g, nsm, s, nullptr, 0);
 }
 
 template <bool SILU>
@@ -940,6 +973,29 @@ int launch_rows(const __nv_bfloat16* in, int64_t ld, int8_t* q, float* scale, __
 
 }  // namespace
 
+namespace w8a8 {
+
+// rows_amax_kernel over rows [0, M) (with num_blocks: [0, min(M, 128 *
+// *num_blocks)), the bound read on the device).
+int launch_rows_amax(const __nv_bfloat16* y, int64_t ld, const uint32_t* amax, int8_t* q, float* scale, int64_t M,
+                     int width, const int32_t* num_blocks, cudaStream_t s) {
+  const int64_t nvec = width / 8;
+  const int64_t gx = (nvec + kAmaxThreads * kAmaxVpt - 1) / (kAmaxThreads * kAmaxVpt);
+  int64_t gy = M < 65535 ? M : 65535;
+  if (num_blocks != nullptr) {
+    // the rows in use are known on the device only: cover the bound with
+    // about four CTAs per SM (the kernel strides over rows)
+    const int64_t cap = 4LL * w8a8::sm_count() / (gx > 0 ? gx : 1);
+    if (gy > cap && cap > 0) gy = cap;
+  }
+  W8A8_REQUIRE(gx <= 0x7fffffff, W8A8_ERR_UNSUPPORTED, "quant_rows_amax: K too large");
+  W8A8_CUDA_TRY(w8a8::launch_pdl(rows_amax_kernel, dim3(static_cast<unsigned>(gx), static_cast<unsigned>(gy)),
+                                 dim3(kAmaxThreads), 0, s, y, ld, amax, q, scale, M, width, num_blocks));
+  return W8A8_OK;
+}
+
+}  // namespace w8a8
+
 extern "C" {
 
 int w8a8_quant_rows_amax(const void* y, int64_t ldy, const uint32_t* amax, int8_t* q, float* scale, int64_t M,
@@ -953,14 +1009,8 @@ int w8a8_quant_rows_amax(const void* y, int64_t ldy, const uint32_t* amax, int8_
                "quant_rows_amax: row stride %lld must be >= K and a multiple of 8", (long long)ldy);
   W8A8_REQUIRE(W8A8_ALIGNED16(y) && W8A8_ALIGNED16(q), W8A8_ERR_ALIGNMENT,
                "quant_rows_amax: y and q must be 16-byte aligned");
-  const int64_t nvec = K / 8;
-  const int64_t gx = (nvec + kAmaxThreads * kAmaxVpt - 1) / (kAmaxThreads * kAmaxVpt);
-  const int64_t gy = M < 65535 ? M : 65535;
-  W8A8_REQUIRE(gx <= 0x7fffffff, W8A8_ERR_UNSUPPORTED, "quant_rows_amax: K too large");
-  W8A8_CUDA_TRY(w8a8::launch_pdl(rows_amax_kernel, dim3(static_cast<unsigned>(gx), static_cast<unsigned>(gy)),
-                                 dim3(kAmaxThreads), 0, static_cast<cudaStream_t>(stream),
-                                 static_cast<const __nv_bfloat16*>(y), ldy, amax, q, scale, M, static_cast<int>(K)));
-  return W8A8_OK;
+  return w8a8::launch_rows_amax(static_cast<const __nv_bfloat16*>(y), ldy, amax, q, scale, M, static_cast<int>(K),
+                                nullptr, static_cast<cudaStream_t>(stream));
 }
 
 int w8a8_quant_per_token(const void* x, int64_t ldx, int8_t* q, float* scale, int64_t M, int64_t K,
@@ -980,6 +1030,28 @@ int w8a8_quant_per_token(const void* x, int64_t ldx, int8_t* q, float* scale, in
                (long long)K);
   return launch_rows<false>(static_cast<const __nv_bfloat16*>(x), ldx, q, scale, nullptr, M, static_cast<int>(K),
                             static_cast<cudaStream_t>(stream));
+}
+
+int w8a8_moe_quant_scatter(const void* x, int64_t ldx, int64_t T, int64_t K, const int32_t* inv_pos, int topk,
+                           int8_t* q_sorted, float* sa_sorted, void* stream) {
+  W8A8_REQUIRE(T >= 0 && K >= 0, W8A8_ERR_INVALID_ARG, "moe_quant_scatter: negative shape T=%lld K=%lld",
+               (long long)T, (long long)K);
+  if (T == 0) return W8A8_OK;
+  W8A8_REQUIRE(x && inv_pos && q_sorted && sa_sorted, W8A8_ERR_INVALID_ARG, "moe_quant_scatter: null pointer");
+  W8A8_REQUIRE(topk >= 1 && topk <= 64, W8A8_ERR_UNSUPPORTED, "moe_quant_scatter: top-k %d (1..64 supported)", topk);
+  W8A8_REQUIRE(K > 0 && K % 8 == 0, W8A8_ERR_INVALID_ARG, "moe_quant_scatter: K=%lld must be a positive multiple of 8",
+               (long long)K);
+  W8A8_REQUIRE(ldx >= K && ldx % 8 == 0, W8A8_ERR_INVALID_ARG,
+               "moe_quant_scatter: row stride %lld must be >= K and a multiple of 8", (long long)ldx);
+  W8A8_REQUIRE(T * topk <= 0x7fffffff, W8A8_ERR_UNSUPPORTED, "moe_quant_scatter: too many slots");
+  W8A8_REQUIRE(W8A8_ALIGNED16(x) && W8A8_ALIGNED16(q_sorted), W8A8_ERR_ALIGNMENT,
+               "moe_quant_scatter: x and q_sorted must be 16-byte aligned");
+  const int g = warp_group_size(static_cast<int>(K / 8));
+  W8A8_REQUIRE(g > 0, W8A8_ERR_UNSUPPORTED, "moe_quant_scatter: K=%lld exceeds the 16384 limit", (long long)K);
+  const int nsm = w8a8::sm_count();
+  W8A8_REQUIRE(nsm > 0, W8A8_ERR_CUDA, "moe_quant_scatter: no CUDA device");
+  return launch_warp_group_t<true>(static_cast<const __nv_bfloat16*>(x), ldx, q_sorted, sa_sorted, T,
+                                   static_cast<int>(K), g, nsm, static_cast<cudaStream_t>(stream), inv_pos, topk);
 }
 
 int w8a8_silu_mul_quant(const void* gate_up, int64_t ld, int8_t* q, float* scale, void* y_out,

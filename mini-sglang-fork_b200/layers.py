@@ -34,6 +34,7 @@ __all__ = [
     "LinearOProj",
     "LinearRowParallel",
     "GatedMLP",
+    "MoELayer",
     "silu_and_mul",
     "silu_and_mul_quant",
 ]
@@ -219,3 +220,58 @@ class GatedMLP(BaseOP):
         y = self.gate_up_proj.forward_silu_quant(x)
         del x
         return self.down_proj.forward(y)
+
+
+class MoELayer(BaseOP):
+    """W8A8 ``MoELayer`` (M/layers/moe.py:8-58): the experts of a mixture-of-
+    experts MLP, TP-sharded on the intermediate dim like the reference's
+    (``intermediate_size / tp`` per rank).  State dict: ``gate_up_proj`` int8
+    [E, 2I_local, H] ([gate; up] per expert), ``gate_up_proj_scale`` fp32
+    [E, 2I_local], ``down_proj`` int8 [E, H, I_local], ``down_proj_scale``
+    fp32 [E, H] (per output channel of the unsharded weights, replicated on
+    the dim-1 shards as for the dense layers).  ``forward(hidden_states,
+    router_logits)`` routes with the reference's ``fused_topk`` arithmetic
+    (softmax in fp32, top-k, optional renormalisation; torch ops on the
+    device), runs :func:`ops.fused_experts_w8a8` and, for tp > 1, the
+    plugin stack's ``all_reduce``.  Only ``activation="silu"`` with the
+    routing weight on the down projection (the reference's defaults) exists
+    in W8A8."""
+
+    def __init__(self, num_experts: int, top_k: int, hidden_size: int, intermediate_size: int,
+                 renormalize: bool = True, activation: str = "silu",
+                 apply_router_weight_on_input: bool = False):
+        if activation != "silu" or apply_router_weight_on_input:
+            raise ValueError("MoELayer (W8A8): only activation='silu' with the routing weight on the down "
+                             "projection is provided")
+        self.num_experts = num_experts
+        self.top_k = top_k
+        self.hidden_size = hidden_size
+        self.intermediate_size = intermediate_size
+        self.renormalize = renormalize
+        self.activation = activation
+        self.apply_router_weight_on_input = apply_router_weight_on_input
+        self._comm = communicator()
+        self.tp_size = tp_size = get_tp_info().size
+        i_local = div_even(intermediate_size, tp_size)
+        self.gate_up_proj = torch.empty(num_experts, 2 * i_local, hidden_size, dtype=torch.int8)
+        self.gate_up_proj_scale = torch.empty(num_experts, 2 * i_local, dtype=torch.float32)
+        self.down_proj = torch.empty(num_experts, hidden_size, i_local, dtype=torch.int8)
+        self.down_proj_scale = torch.empty(num_experts, hidden_size, dtype=torch.float32)
+
+    def route(self, router_logits: torch.Tensor):
+        """``fused_topk`` (M/moe/fused.py:9-29): ``(topk_weights fp32, topk_ids
+        int32)``, both [T, top_k]."""
+        p = torch.softmax(router_logits.float(), dim=-1)
+        w, ids = torch.topk(p, self.top_k, dim=-1)
+        if self.renormalize:
+            w = w / w.sum(dim=-1, keepdim=True)
+            w = w / (w.sum(dim=-1, keepdim=True) + 1e-8)
+        return w.contiguous(), ids.to(torch.int32).contiguous()
+
+    def forward(self, hidden_states: torch.Tensor, router_logits: torch.Tensor) -> torch.Tensor:
+        topk_weights, topk_ids = self.route(router_logits)
+        out = ops.fused_experts_w8a8(hidden_states, self.gate_up_proj, self.gate_up_proj_scale, self.down_proj,
+                                     self.down_proj_scale, topk_weights, topk_ids)
+        if self.tp_size > 1:
+            out = self._comm.all_reduce(out)
+        return out

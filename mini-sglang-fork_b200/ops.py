@@ -7,7 +7,7 @@ non-CUDA tensor, a missing library or a non-B200 device raises.
 from __future__ import annotations
 
 import ctypes
-from typing import Dict, Optional, Tuple
+from typing import Dict, NamedTuple, Optional, Tuple
 
 import torch
 
@@ -28,6 +28,13 @@ __all__ = [
     "check_gemm_operands",
     "QuantizedActivation",
     "WORKSPACE_BYTES",
+    "MoeRouting",
+    "moe_align",
+    "moe_quant_scatter",
+    "moe_gemm",
+    "moe_quant_rows",
+    "moe_sum",
+    "fused_experts_w8a8",
 ]
 
 # Split-K workspace kept per device (zeroed once, left zeroed by every call).
@@ -289,6 +296,170 @@ def gate_up_silu_quant(aq: torch.Tensor, wq: torch.Tensor, sa: torch.Tensor, sw:
     y, amax = r
     qa = quant_rows_amax(y, amax)
     return (qa, y) if with_bf16 else qa
+
+
+# ---------------------------------------------------------------------------
+# mixture of experts (fused_experts_impl, M/moe/fused.py:135-215)
+# ---------------------------------------------------------------------------
+class MoeRouting(NamedTuple):
+    """The expert-sorted layout of one batch's routed slots (``w8a8_moe_align``).
+
+    Slot ``s = t * topk + j`` is token t's j-th choice.  Rows ``[0, 128 *
+    num_blocks)`` of every sorted buffer are in use (``num_blocks`` lives on
+    the device); ``P = 128 * max_blocks`` rows are allocated."""
+    sorted_ids: torch.Tensor    # [P] int32: slot of each row (num_slots on padding)
+    block_expert: torch.Tensor  # [max_blocks] int32: expert of each 128-row block
+    num_blocks: torch.Tensor    # [1] int32, device
+    inv_pos: torch.Tensor       # [num_slots] int32: row of each slot (-1: dropped)
+    sa_sorted: torch.Tensor     # [P] fp32: activation scale of each row (0 on padding)
+    max_blocks: int
+    num_experts: int
+    topk: int
+
+
+def _check_2d(name: str, t: torch.Tensor, dtype: torch.dtype, shape: Tuple[int, ...]) -> None:
+    if t.dtype != dtype or tuple(t.shape) != tuple(shape) or not t.is_contiguous():
+        raise _lib.W8A8Error(_lib.ERR_INVALID_ARG,
+                             f"{name}: expected a contiguous {dtype} tensor of shape {tuple(shape)}, got "
+                             f"{t.dtype} {tuple(t.shape)}{'' if t.is_contiguous() else ' (non-contiguous)'}")
+
+
+def moe_align(topk_ids: torch.Tensor, num_experts: int) -> MoeRouting:
+    """``moe_align_block_size`` (M/moe/fused.py:32-83) with 128-row blocks."""
+    _require_cuda("moe_align", topk_ids)
+    if topk_ids.dim() != 2 or topk_ids.dtype != torch.int32 or not topk_ids.is_contiguous():
+        raise _lib.W8A8Error(_lib.ERR_INVALID_ARG, "moe_align: topk_ids must be a contiguous int32 [T, topk]")
+    t, k = topk_ids.shape
+    n = t * k
+    lib = _lib.load()
+    mb = int(lib.w8a8_moe_max_blocks(n, num_experts)) if n > 0 else 0
+    dev = topk_ids.device
+    p = 128 * mb
+    r = MoeRouting(torch.empty(p, dtype=torch.int32, device=dev), torch.empty(max(mb, 1), dtype=torch.int32, device=dev),
+                   torch.empty(1, dtype=torch.int32, device=dev), torch.empty(n, dtype=torch.int32, device=dev),
+                   torch.empty(p, dtype=torch.float32, device=dev), mb, num_experts, k)
+    _lib.check(lib.w8a8_moe_align(_ptr(topk_ids), n, num_experts, _ptr(r.sorted_ids), _ptr(r.block_expert),
+                                  _ptr(r.num_blocks), _ptr(r.inv_pos), _ptr(r.sa_sorted), _stream(topk_ids)),
+               "moe_align")
+    return r
+
+
+def moe_quant_scatter(x: torch.Tensor, routing: MoeRouting) -> torch.Tensor:
+    """Per-token quantisation of ``x [T, H]`` into the expert-sorted rows:
+    returns ``q_sorted [P, H]`` int8 and fills ``routing.sa_sorted``."""
+    _require_cuda("moe_quant_scatter", x)
+    if x.dtype != torch.bfloat16 or x.dim() != 2 or x.stride(1) != 1:
+        raise _lib.W8A8Error(_lib.ERR_INVALID_ARG, "moe_quant_scatter: x must be a 2-D bf16 tensor with unit column stride")
+    t, h = x.shape
+    if routing.inv_pos.numel() != t * routing.topk:
+        raise _lib.W8A8Error(_lib.ERR_INVALID_ARG, "moe_quant_scatter: routing was built for another token count")
+    q = torch.empty(128 * routing.max_blocks, h, dtype=torch.int8, device=x.device)
+    if t > 0:
+        _lib.check(_lib.load().w8a8_moe_quant_scatter(_ptr(x), x.stride(0), t, h, _ptr(routing.inv_pos), routing.topk,
+                                                      _ptr(q), _ptr(routing.sa_sorted), _stream(x)),
+                   "moe_quant_scatter")
+    return q
+
+
+def moe_gemm(a_sorted: torch.Tensor, sa_sorted: torch.Tensor, w: torch.Tensor, sw: torch.Tensor,
+             routing: MoeRouting, route_w: Optional[torch.Tensor] = None, silu: bool = False):
+    """Grouped W8A8 GEMM over the expert-sorted rows (``w8a8_moe_gemm``):
+    ``w [E, N, K]`` int8, ``sw [E, N]`` fp32.  ``silu``: ``w`` is [gate; up]
+    per expert and the result is ``(y [P, N/2] bf16, amax [P] int32)``;
+    otherwise ``c [P, N]`` bf16 with the routing weight (``route_w [T, topk]``
+    fp32, nullable) applied."""
+    _require_cuda("moe_gemm", a_sorted, sa_sorted, w, sw, route_w)
+    e, n, k = w.shape if w.dim() == 3 else (0, 0, 0)
+    p = 128 * routing.max_blocks
+    if w.dim() != 3 or e != routing.num_experts:
+        raise _lib.W8A8Error(_lib.ERR_INVALID_ARG, f"moe_gemm: w must be [E={routing.num_experts}, N, K]")
+    _check_2d("moe_gemm w", w, torch.int8, (e, n, k))
+    _check_2d("moe_gemm sw", sw, torch.float32, (e, n))
+    _check_2d("moe_gemm a_sorted", a_sorted, torch.int8, (p, k))
+    _check_2d("moe_gemm sa_sorted", sa_sorted, torch.float32, (p,))
+    if route_w is not None:
+        _check_2d("moe_gemm route_w", route_w, torch.float32, (routing.inv_pos.numel() // routing.topk, routing.topk))
+        if silu:
+            raise _lib.W8A8Error(_lib.ERR_INVALID_ARG, "moe_gemm: no routing weight with the SiLU epilogue")
+    dev = a_sorted.device
+    out = torch.empty(p, n // 2 if silu else n, dtype=torch.bfloat16, device=dev)
+    amax = torch.zeros(p, dtype=torch.int32, device=dev) if silu else None
+    if p > 0:
+        _lib.check(_lib.load().w8a8_moe_gemm(
+            _ptr(a_sorted), _ptr(w), _ptr(sa_sorted), _ptr(sw), _ptr(routing.block_expert), _ptr(routing.num_blocks),
+            routing.max_blocks, _ptr(routing.sorted_ids), _ptr(route_w), routing.inv_pos.numel(), _ptr(out),
+            _ptr(amax), e, n, k, _stream(a_sorted)), "moe_gemm")
+    return (out, amax) if silu else out
+
+
+def moe_quant_rows(y: torch.Tensor, amax: torch.Tensor, routing: MoeRouting) -> QuantizedActivation:
+    """Row quantisation of the sorted ``y [P, I]`` with its known absmax, over
+    the rows in use only."""
+    _require_cuda("moe_quant_rows", y, amax)
+    p = 128 * routing.max_blocks
+    if y.dtype != torch.bfloat16 or y.dim() != 2 or y.shape[0] != p or y.stride(1) != 1:
+        raise _lib.W8A8Error(_lib.ERR_INVALID_ARG, "moe_quant_rows: y must be a bf16 [P, I] tensor")
+    _check_2d("moe_quant_rows amax", amax, torch.int32, (p,))
+    i = y.shape[1]
+    q = torch.empty(p, i, dtype=torch.int8, device=y.device)
+    s = torch.empty(p, dtype=torch.float32, device=y.device)
+    if p > 0:
+        _lib.check(_lib.load().w8a8_moe_quant_rows(_ptr(y), y.stride(0), _ptr(amax), _ptr(q), _ptr(s),
+                                                   _ptr(routing.num_blocks), routing.max_blocks, i, _stream(y)),
+                   "moe_quant_rows")
+    return QuantizedActivation(q, s)
+
+
+def moe_sum(c_sorted: torch.Tensor, routing: MoeRouting, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """``moe_sum_reduce`` (M/kernel/triton/fused_moe.py:5-48): ``out[t] =
+    bf16(sum_j f32(c[row(t, j)]))`` in choice order."""
+    _require_cuda("moe_sum", c_sorted, out)
+    t = routing.inv_pos.numel() // max(routing.topk, 1)
+    h = c_sorted.shape[1]
+    if c_sorted.dtype != torch.bfloat16 or c_sorted.dim() != 2 or c_sorted.stride(1) != 1:
+        raise _lib.W8A8Error(_lib.ERR_INVALID_ARG, "moe_sum: c_sorted must be a bf16 [P, H] tensor")
+    if out is None:
+        out = torch.empty(t, h, dtype=torch.bfloat16, device=c_sorted.device)
+    elif out.dtype != torch.bfloat16 or tuple(out.shape) != (t, h) or out.stride(1) != 1:
+        raise _lib.W8A8Error(_lib.ERR_INVALID_ARG, f"moe_sum: out must be bf16 [{t}, {h}] with unit column stride")
+    if t > 0:
+        _lib.check(_lib.load().w8a8_moe_sum(_ptr(c_sorted), c_sorted.stride(0), _ptr(routing.inv_pos), t,
+                                            routing.topk, h, _ptr(out), out.stride(0), _stream(c_sorted)), "moe_sum")
+    return out
+
+
+def fused_experts_w8a8(x: torch.Tensor, w1q: torch.Tensor, sw1: torch.Tensor, w2q: torch.Tensor,
+                       sw2: torch.Tensor, topk_weights: torch.Tensor, topk_ids: torch.Tensor,
+                       out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """The W8A8 counterpart of ``fused_experts_impl`` (M/moe/fused.py:135-215)
+    with ``activation="silu"`` and the routing weight applied to the down
+    GEMM: ``x [T, H]`` bf16, ``w1q [E, 2I, H]`` / ``sw1 [E, 2I]``, ``w2q [E,
+    H, I]`` / ``sw2 [E, H]``, ``topk_weights [T, k]`` fp32, ``topk_ids [T, k]``
+    int32 -> ``[T, H]`` bf16.  Six launches, no host sync: align, quantise
+    into the sorted rows, gate_up grouped GEMM with SiLU*mul, quantise y,
+    down grouped GEMM with the routing weight, top-k sum."""
+    _require_cuda("fused_experts_w8a8", x, w1q, sw1, w2q, sw2, topk_weights, topk_ids)
+    if x.dim() != 2 or w1q.dim() != 3 or w2q.dim() != 3:
+        raise _lib.W8A8Error(_lib.ERR_INVALID_ARG, "fused_experts_w8a8: x [T, H], w1q [E, 2I, H], w2q [E, H, I]")
+    t, h = x.shape
+    e, n2, _ = w1q.shape
+    if tuple(w1q.shape) != (e, n2, h) or tuple(w2q.shape) != (e, h, n2 // 2) or n2 % 2:
+        raise _lib.W8A8Error(_lib.ERR_INVALID_ARG,
+                             f"fused_experts_w8a8: w1q {tuple(w1q.shape)} / w2q {tuple(w2q.shape)} do not match "
+                             f"H={h}")
+    if topk_ids.dim() != 2 or topk_ids.shape[0] != t or tuple(topk_weights.shape) != tuple(topk_ids.shape):
+        raise _lib.W8A8Error(_lib.ERR_INVALID_ARG, "fused_experts_w8a8: topk_ids / topk_weights must be [T, topk]")
+    _check_2d("fused_experts_w8a8 topk_weights", topk_weights, torch.float32, tuple(topk_ids.shape))
+    routing = moe_align(topk_ids, e)
+    if out is None:
+        out = torch.empty(t, h, dtype=torch.bfloat16, device=x.device)
+    if routing.max_blocks == 0:
+        return out.zero_()
+    qx = moe_quant_scatter(x, routing)
+    y, amax = moe_gemm(qx, routing.sa_sorted, w1q, sw1, routing, silu=True)
+    qy = moe_quant_rows(y, amax, routing)
+    c3 = moe_gemm(qy.q, qy.s, w2q, sw2, routing, route_w=topk_weights)
+    return moe_sum(c3, routing, out)
 
 
 # The stream-K counter region at the head of a GEMM workspace (65536 tile
