@@ -32,32 +32,59 @@ constexpr int kAlignThreads = 1024;
 constexpr int kMaxExperts = kAlignThreads;
 constexpr int kMoeStages = 4;
 
-// One CTA: count the slots of every expert (shared-memory atomics), an
-// exclusive scan of the per-expert block counts gives each expert's first
-// row, then every slot takes the next row of its expert.  The order of the
-// slots inside an expert follows the atomics (not the slot order); nothing
-// downstream depends on it: every row of the grouped GEMM is computed on its
-// own, and the combine sums a token's choices in choice order through the
-// slot -> row map.  Slots whose expert id is outside [0, E) are dropped
-// (inv_pos = -1) and contribute nothing.  Padding rows get the slot id
-// num_slots and scale 0.
+// G CTAs, no communication between them: every CTA counts ALL slots per
+// expert (shared-memory atomics; the ids are read from L2 after the first
+// CTA), and separately the slots before its own range, so it knows each
+// expert's first row (an exclusive scan of the per-expert block counts) and
+// where its own slots of each expert start.  It then places the slots of its
+// range [g * chunk, (g + 1) * chunk): every slot takes the next row of its
+// expert.  The scattered row stores are spread over the G SMs; the counting
+// is repeated G times but runs in parallel.  Each thread loads kAlignIds ids
+// at once (coalesced across the CTA) before touching the counters.
+// The order of the slots inside an expert follows the atomics (not the slot
+// order); nothing downstream depends on it: every row of the grouped GEMM is
+// computed on its own, and the combine sums a token's choices in choice order
+// through the slot -> row map.  Slots whose expert id is outside [0, E) are
+// dropped (inv_pos = -1) and contribute nothing.  Padding rows get the slot
+// id num_slots and scale 0, written row-contiguously (rows shared out over
+// the CTAs); CTA 0 writes the block -> expert table and the block count.
+constexpr int kAlignIds = 16;
+constexpr int kAlignSharedBlocks = 4096;  // block -> expert table held in shared memory
 __global__ void __launch_bounds__(kAlignThreads) moe_align_kernel(const int32_t* __restrict__ ids, int num_slots,
-                                                                  int E, int32_t* __restrict__ sorted_ids,
+                                                                  int E, int chunk, int32_t* __restrict__ sorted_ids,
                                                                   int32_t* __restrict__ block_expert,
                                                                   int32_t* __restrict__ num_blocks,
                                                                   int32_t* __restrict__ inv_pos,
                                                                   float* __restrict__ sa_sorted) {
   __shared__ int cnt[kMaxExperts];
+  __shared__ int before[kMaxExperts];
+  __shared__ int first_row[kMaxExperts];
   __shared__ int next_row[kMaxExperts];
   __shared__ int warp_sum[kAlignThreads / 32];
+  __shared__ uint16_t blk_e[kAlignSharedBlocks];
   dev::griddep_launch();
   dev::griddep_wait();  // the expert ids are the router's output
   const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+  const int my_begin = blockIdx.x * chunk;
+  const int my_end = min(num_slots, my_begin + chunk);
+  constexpr int kStep = kAlignThreads * kAlignIds;
   cnt[t] = 0;
+  before[t] = 0;
   __syncthreads();
-  for (int s = t; s < num_slots; s += kAlignThreads) {
-    const int e = ids[s];
-    if (e >= 0 && e < E) atomicAdd(&cnt[e], 1);
+  for (int base = 0; base < num_slots; base += kStep) {
+    int e[kAlignIds];
+#pragma unroll
+    for (int j = 0; j < kAlignIds; ++j) {
+      const int s = base + j * kAlignThreads + t;
+      e[j] = s < num_slots ? __ldg(ids + s) : -1;
+    }
+#pragma unroll
+    for (int j = 0; j < kAlignIds; ++j) {
+      if (e[j] >= 0 && e[j] < E) {
+        atomicAdd(&cnt[e[j]], 1);
+        if (base + j * kAlignThreads + t < my_begin) atomicAdd(&before[e[j]], 1);
+      }
+    }
   }
   __syncthreads();
   const int c = t < E ? cnt[t] : 0;
@@ -81,32 +108,60 @@ __global__ void __launch_bounds__(kAlignThreads) moe_align_kernel(const int32_t*
   }
   __syncthreads();
   const int first_block = incl - nbk + (warp > 0 ? warp_sum[warp - 1] : 0);
+  const int total = warp_sum[kAlignThreads / 32 - 1];
   if (t < E) {
-    next_row[t] = first_block * 128;
-    for (int k = 0; k < nbk; ++k) block_expert[first_block + k] = t;
+    first_row[t] = first_block * 128;
+    next_row[t] = first_block * 128 + before[t];
+    for (int k = 0; k < nbk; ++k) {
+      if (blockIdx.x == 0) block_expert[first_block + k] = t;
+      if (first_block + k < kAlignSharedBlocks) blk_e[first_block + k] = static_cast<uint16_t>(t);
+    }
+  }
+  if (blockIdx.x == 0 && t == 0) *num_blocks = total;
+  __syncthreads();
+  if (total <= kAlignSharedBlocks) {
+    // row r is padding when it lies past its expert's c_e slots
+    for (int r = blockIdx.x * kAlignThreads + t; r < total * 128; r += gridDim.x * kAlignThreads) {
+      const int e = blk_e[r >> 7];
+      if (r - first_row[e] >= cnt[e]) {
+        sorted_ids[r] = num_slots;
+        sa_sorted[r] = 0.0f;
+      }
+    }
+  } else if (blockIdx.x == 0 && t < E) {
     for (int r = first_block * 128 + c; r < (first_block + nbk) * 128; ++r) {
       sorted_ids[r] = num_slots;
       sa_sorted[r] = 0.0f;
     }
   }
-  if (t == 0) *num_blocks = warp_sum[kAlignThreads / 32 - 1];
-  __syncthreads();
-  for (int s = t; s < num_slots; s += kAlignThreads) {
-    const int e = ids[s];
-    if (e >= 0 && e < E) {
-      const int r = atomicAdd(&next_row[e], 1);
-      sorted_ids[r] = s;
-      inv_pos[s] = r;
-    } else {
-      inv_pos[s] = -1;
+  for (int base = my_begin; base < my_end; base += kStep) {
+    int e[kAlignIds];
+#pragma unroll
+    for (int j = 0; j < kAlignIds; ++j) {
+      const int s = base + j * kAlignThreads + t;
+      e[j] = s < my_end ? __ldg(ids + s) : -1;
+    }
+#pragma unroll
+    for (int j = 0; j < kAlignIds; ++j) {
+      const int s = base + j * kAlignThreads + t;
+      if (s >= my_end) continue;
+      if (e[j] >= 0 && e[j] < E) {
+        const int r = atomicAdd(&next_row[e[j]], 1);
+        sorted_ids[r] = s;
+        inv_pos[s] = r;
+      } else {
+        inv_pos[s] = -1;
+      }
     }
   }
 }
 
 // out[t] = bf16(sum_j f32(C[row(t, j)])), j = 0..topk-1 in order, from an
 // fp32 zero -- moe_sum_reduce_kernel's arithmetic.  One thread per 8 columns
-// of a token; a dropped choice (row -1) adds nothing.
+// of a token; a dropped choice (row -1) adds nothing.  With topk <= KMAX the
+// rows and then the values of all choices are loaded before the sum.
 constexpr int kSumThreads = 256;
+template <int KMAX>
 __global__ void __launch_bounds__(kSumThreads) moe_sum_kernel(const __nv_bfloat16* __restrict__ c, int64_t ldc,
                                                               const int32_t* __restrict__ inv_pos, int64_t T,
                                                               int topk, int nvec, __nv_bfloat16* __restrict__ out,
@@ -121,16 +176,30 @@ __global__ void __launch_bounds__(kSumThreads) moe_sum_kernel(const __nv_bfloat1
     float acc[8];
 #pragma unroll
     for (int k = 0; k < 8; ++k) acc[k] = 0.0f;
-    for (int j = 0; j < topk; ++j) {
-      const int r = __ldg(inv_pos + tok * topk + j);
-      if (r < 0) continue;
-      const uint4 raw = __ldg(reinterpret_cast<const uint4*>(c + static_cast<int64_t>(r) * ldc) + v);
+    auto add = [&](const uint4& raw) {
       const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw);
 #pragma unroll
       for (int k = 0; k < 4; ++k) {
         const float2 f = __bfloat1622float2(h[k]);
         acc[2 * k] = __fadd_rn(acc[2 * k], f.x);
         acc[2 * k + 1] = __fadd_rn(acc[2 * k + 1], f.y);
+      }
+    };
+    if (KMAX > 0) {
+      int r[KMAX > 0 ? KMAX : 1];
+      uint4 raw[KMAX > 0 ? KMAX : 1];
+#pragma unroll
+      for (int j = 0; j < KMAX; ++j) r[j] = j < topk ? __ldg(inv_pos + tok * topk + j) : -1;
+#pragma unroll
+      for (int j = 0; j < KMAX; ++j)
+        if (r[j] >= 0) raw[j] = __ldg(reinterpret_cast<const uint4*>(c + static_cast<int64_t>(r[j]) * ldc) + v);
+#pragma unroll
+      for (int j = 0; j < KMAX; ++j)
+        if (r[j] >= 0) add(raw[j]);
+    } else {
+      for (int j = 0; j < topk; ++j) {
+        const int r = __ldg(inv_pos + tok * topk + j);
+        if (r >= 0) add(__ldg(reinterpret_cast<const uint4*>(c + static_cast<int64_t>(r) * ldc) + v));
       }
     }
     uint4 pk;
@@ -195,9 +264,13 @@ int w8a8_moe_align(const int32_t* topk_ids, int64_t num_slots, int num_experts, 
   }
   W8A8_REQUIRE(topk_ids && sorted_ids && block_expert && inv_pos && sa_sorted, W8A8_ERR_INVALID_ARG,
                "moe_align: null pointer");
-  W8A8_CUDA_TRY(launch_pdl(moe_align_kernel, dim3(1), dim3(kAlignThreads), 0, s, topk_ids,
-                           static_cast<int>(num_slots), num_experts, sorted_ids, block_expert, num_blocks, inv_pos,
-                           sa_sorted));
+  // one CTA per 2048 slots, at most 64 (every CTA counts all slots)
+  int64_t grid = (num_slots + 2047) / 2048;
+  if (grid > 64) grid = 64;
+  const int chunk = static_cast<int>((num_slots + grid - 1) / grid);
+  W8A8_CUDA_TRY(launch_pdl(moe_align_kernel, dim3(static_cast<unsigned>(grid)), dim3(kAlignThreads), 0, s, topk_ids,
+                           static_cast<int>(num_slots), num_experts, chunk, sorted_ids, block_expert, num_blocks,
+                           inv_pos, sa_sorted));
   return W8A8_OK;
 }
 
@@ -302,7 +375,9 @@ int w8a8_moe_sum(const void* c_sorted, int64_t ldc, const int32_t* inv_pos, int6
   int64_t grid = (total + kSumThreads - 1) / kSumThreads;
   const int64_t cap = static_cast<int64_t>(nsm) * 8;
   if (grid > cap) grid = cap;
-  W8A8_CUDA_TRY(launch_pdl(moe_sum_kernel, dim3(static_cast<unsigned>(grid)), dim3(kSumThreads), 0,
+  auto kern = topk <= 2 ? moe_sum_kernel<2> : topk <= 4 ? moe_sum_kernel<4> : topk <= 8 ? moe_sum_kernel<8>
+                                                                                   : moe_sum_kernel<0>;
+  W8A8_CUDA_TRY(launch_pdl(kern, dim3(static_cast<unsigned>(grid)), dim3(kSumThreads), 0,
                            static_cast<cudaStream_t>(stream), static_cast<const __nv_bfloat16*>(c_sorted), ldc,
                            inv_pos, T, topk, nvec, static_cast<__nv_bfloat16*>(out), ldo));
   return W8A8_OK;

@@ -444,6 +444,44 @@ __global__ void __launch_bounds__(kAmaxThreads) rows_amax_kernel(const __nv_bflo
   }
 }
 
+// Narrow rows (at most 256 vectors, K <= 2048) with a known absmax: one warp
+// per row, every lane's VPT vector loads issued before any is converted, the
+// warps of the grid striding over the rows (with num_blocks the row count is
+// read on the device).  The same arithmetic as rows_amax_kernel.
+constexpr int kAmaxWarpThreads = 256;
+template <int VPT>
+__global__ void __launch_bounds__(kAmaxWarpThreads) rows_amax_warp_kernel(
+    const __nv_bfloat16* __restrict__ y, int64_t ld, const uint32_t* __restrict__ amax, int8_t* __restrict__ q,
+    float* __restrict__ scale, int64_t M, int width, const int32_t* __restrict__ num_blocks) {
+  w8a8::dev::griddep_launch();  // early trigger, as in rows_reg_kernel
+  w8a8::dev::griddep_wait();    // y and amax are the previous kernel's output
+  if (num_blocks != nullptr) {
+    const int64_t used = static_cast<int64_t>(max(*num_blocks, 0)) * 128;
+    if (used < M) M = used;
+  }
+  const int lane = threadIdx.x & 31;
+  const int nvec = width >> 3;
+  constexpr int kWarps = kAmaxWarpThreads / 32;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * kWarps;
+  for (int64_t row = static_cast<int64_t>(blockIdx.x) * kWarps + (threadIdx.x >> 5); row < M; row += stride) {
+    const uint4* src = reinterpret_cast<const uint4*>(y + row * ld);
+    uint4 v[VPT];
+#pragma unroll
+    for (int j = 0; j < VPT; ++j) {
+      const int vi = lane + 32 * j;
+      if (vi < nvec) v[j] = __ldcs(src + vi);
+    }
+    const RowScale rs = row_scale(__uint_as_float(__ldg(amax + row)));
+    uint2* dst = reinterpret_cast<uint2*>(q + row * static_cast<int64_t>(width));
+#pragma unroll
+    for (int j = 0; j < VPT; ++j) {
+      const int vi = lane + 32 * j;
+      if (vi < nvec) dst[vi] = quant_vec8(v[j], rs);
+    }
+    if (lane == 0) scale[row] = rs.s;
+  }
+}
+
 // Cluster path (few rows): one row per cluster of C CTAs (C = the cluster
 // size, 2..8), CTA c taking vectors [c*nvec/C, (c+1)*nvec/C) of the row in
 // registers (VPT per thread).  Each CTA reduces its share's absmax, publishes
@@ -971,6 +1009,18 @@ int launch_rows(const __nv_bfloat16* in, int64_t ld, int8_t* q, float* scale, __
   return W8A8_OK;
 }
 
+template <int VPT>
+cudaError_t launch_rows_amax_warp(const __nv_bfloat16* y, int64_t ld, const uint32_t* amax, int8_t* q,
+                                  float* scale, int64_t M, int width, const int32_t* num_blocks, cudaStream_t s) {
+  constexpr int kWarps = kAmaxWarpThreads / 32;
+  const int per_sm = resident_ctas(rows_amax_warp_kernel<VPT>, kAmaxWarpThreads, 0);
+  int64_t grid = (M + kWarps - 1) / kWarps;
+  const int64_t cap = static_cast<int64_t>(w8a8::sm_count()) * per_sm;
+  if (grid > cap) grid = cap;
+  return w8a8::launch_pdl(rows_amax_warp_kernel<VPT>, dim3(static_cast<unsigned>(grid)), dim3(kAmaxWarpThreads), 0,
+                          s, y, ld, amax, q, scale, M, width, num_blocks);
+}
+
 }  // namespace
 
 namespace w8a8 {
@@ -980,6 +1030,18 @@ namespace w8a8 {
 int launch_rows_amax(const __nv_bfloat16* y, int64_t ld, const uint32_t* amax, int8_t* q, float* scale, int64_t M,
                      int width, const int32_t* num_blocks, cudaStream_t s) {
   const int64_t nvec = width / 8;
+  if (nvec <= 256) {
+    const int vpt = static_cast<int>((nvec + 31) / 32);
+    cudaError_t e;
+    if (vpt <= 1) e = launch_rows_amax_warp<1>(y, ld, amax, q, scale, M, width, num_blocks, s);
+    else if (vpt <= 2) e = launch_rows_amax_warp<2>(y, ld, amax, q, scale, M, width, num_blocks, s);
+    else if (vpt <= 3) e = launch_rows_amax_warp<3>(y, ld, amax, q, scale, M, width, num_blocks, s);
+    else if (vpt <= 4) e = launch_rows_amax_warp<4>(y, ld, amax, q, scale, M, width, num_blocks, s);
+    else if (vpt <= 6) e = launch_rows_amax_warp<6>(y, ld, amax, q, scale, M, width, num_blocks, s);
+    else e = launch_rows_amax_warp<8>(y, ld, amax, q, scale, M, width, num_blocks, s);
+    W8A8_CUDA_TRY(e);
+    return W8A8_OK;
+  }
   const int64_t gx = (nvec + kAmaxThreads * kAmaxVpt - 1) / (kAmaxThreads * kAmaxVpt);
   int64_t gy = M < 65535 ? M : 65535;
   if (num_blocks != nullptr) {

@@ -49,6 +49,7 @@ CASES = [
     (100, 320, 192, 16, 4, False, False),     # partial feature tile (I % 128), N tail in the down GEMM
     (700, 256, 128, 6, 2, True, False),       # several blocks per expert
     (300, 1024, 256, 32, 8, False, True),     # many experts, some empty
+    (2048, 256, 128, 64, 8, True, True),      # 16384 slots: the layout kernel spreads over 8 CTAs
 ]
 
 
