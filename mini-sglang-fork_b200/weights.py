@@ -24,11 +24,16 @@ and yields this rank's (name, tensor) pairs, sharded and merged:
 Quantisation at load runs the library's CUDA quantiser on the weight rows
 (``ops.quant_per_token``: per-row absmax == per-output-channel for a
 [N, K] weight) on ``device``; there is no CPU quantiser in the product.
-MoE expert stacking (weight.py:62-73) is not covered: W8A8 MoE is not part of
-this path.
+* MoE experts (``num_experts`` given): every ``<prefix>.experts.<i>.<name>``
+  tensor, once sharded and merged, is held until all experts have it and then
+  yielded stacked on a new dim 0 under ``<prefix>.<name>`` with ``.weight``
+  dropped -- the reference's ``_get_expert_stack_info`` / ``torch.stack``
+  (weight.py:62-73,111-119); the scale ``...gate_up_proj.weight_scale``
+  stacks under ``...gate_up_proj_scale``, the name ``MoELayer`` gives it.
 """
 from __future__ import annotations
 
+import re
 from typing import Callable, Dict, Iterable, Iterator, Optional, Tuple
 
 import torch
@@ -47,6 +52,7 @@ _MERGE_GROUPS = {
     ".up_proj": (".gate_up_proj", "up", ("gate", "up")),
 }
 _SKIP_PREFIXES = ("vision_tower.", "multi_modal_projector.")
+_EXPERT = re.compile(r"^(?P<prefix>.+\.experts)\.(?P<idx>\d+)\.(?P<name>.+)$")
 
 Quantiser = Callable[[torch.Tensor], Tuple[torch.Tensor, torch.Tensor]]
 
@@ -86,8 +92,10 @@ def shard_weight_scale(key: str, scale: torch.Tensor, rank: int, world: int,
 
 
 def is_linear_weight(key: str) -> bool:
-    """A weight of one of the W8A8 projections (q/k/v/o/gate/up/down)."""
-    return key.endswith(".weight") and any(s in key for s in _SPLIT_DIM_0 + _SPLIT_DIM_1)
+    """A weight of one of the W8A8 projections (q/k/v/o/gate/up/down), or the
+    MoE router ``mlp.gate`` (a LinearReplicated in M/models/utils.py:62-66)."""
+    return key.endswith(".weight") and (any(s in key for s in _SPLIT_DIM_0 + _SPLIT_DIM_1)
+                                        or key.endswith(".mlp.gate.weight"))
 
 
 def cuda_quantiser(device: torch.device) -> Quantiser:
@@ -108,6 +116,19 @@ def _merge_info(key: str):
     return None
 
 
+def expert_stack_info(key: str) -> Optional[Tuple[str, int]]:
+    """``(packed key, expert index)`` of an expert-scoped key, else None."""
+    m = _EXPERT.match(key)
+    if m is None:
+        return None
+    name = m.group("name")
+    if name.endswith(".weight_scale"):
+        name = name[: -len(".weight_scale")] + "_scale"
+    elif name.endswith(".weight"):
+        name = name[: -len(".weight")]
+    return f"{m.group('prefix')}.{name}", int(m.group("idx"))
+
+
 def _cast(key: str, value: torch.Tensor, dtype: torch.dtype) -> torch.Tensor:
     """The engine's load-time cast to the model dtype (M/engine/engine.py:146),
     which must leave int8 weights and their fp32 scales alone."""
@@ -121,17 +142,33 @@ def _cast(key: str, value: torch.Tensor, dtype: torch.dtype) -> torch.Tensor:
 def w8a8_weight_stream(items: Iterable[Tuple[str, torch.Tensor]], rank: int, world: int,
                        num_kv_heads: Optional[int], quantise: Optional[Quantiser] = None,
                        device: Optional[torch.device] = None,
-                       dtype: torch.dtype = torch.bfloat16) -> Iterator[Tuple[str, torch.Tensor]]:
+                       dtype: torch.dtype = torch.bfloat16,
+                       num_experts: Optional[int] = None) -> Iterator[Tuple[str, torch.Tensor]]:
     """Shard and merge a checkpoint stream for ``rank`` of ``world`` (see the
     module docstring).  ``quantise`` turns a floating [N, K] weight into
     (int8 [N, K], fp32 [N]); by default the CUDA quantiser on ``device``
     (the current CUDA device if None).  Floating tensors other than the scales
     (biases, norms, embeddings) are cast to ``dtype``.  Raises if a merge group
     is incomplete at the end of the stream; an int8 weight without its scale is
-    caught by the layers' ``load_state_dict``."""
+    caught by the layers' ``load_state_dict``.  With ``num_experts`` the
+    experts' tensors are stacked (module docstring)."""
     if not (0 <= rank < world):
         raise _lib.W8A8Error(_lib.ERR_INVALID_ARG, f"rank {rank} not in [0, {world})")
     merge_buf: Dict[str, Dict[str, torch.Tensor]] = {}
+    expert_buf: Dict[str, Dict[int, torch.Tensor]] = {}
+
+    def out(key: str, value: torch.Tensor) -> Iterator[Tuple[str, torch.Tensor]]:
+        info = expert_stack_info(key) if num_experts else None
+        if info is None:
+            yield key, value
+            return
+        packed, idx = info
+        slots = expert_buf.setdefault(packed, {})
+        slots[idx] = value
+        if len(slots) == num_experts:
+            del expert_buf[packed]
+            yield packed, torch.stack([slots[i] for i in range(num_experts)], dim=0)
+
     for name, tensor in items:
         if name.startswith(_SKIP_PREFIXES):
             continue
@@ -151,23 +188,26 @@ def w8a8_weight_stream(items: Iterable[Tuple[str, torch.Tensor]], rank: int, wor
             value = _cast(key, value, dtype)
             info = _merge_info(key)
             if info is None:
-                yield key, value
+                yield from out(key, value)
                 continue
             merged_key, slot, slots = info
             group = merge_buf.setdefault(merged_key, {})
             group[slot] = value
             if all(s in group for s in slots):
                 del merge_buf[merged_key]
-                yield merged_key, torch.cat([group[s] for s in slots], dim=0)
+                yield from out(merged_key, torch.cat([group[s] for s in slots], dim=0))
     if merge_buf:
         raise _lib.W8A8Error(_lib.ERR_INVALID_ARG, f"incomplete merge groups in checkpoint: {sorted(merge_buf)}")
+    if expert_buf:
+        raise _lib.W8A8Error(_lib.ERR_INVALID_ARG, f"incomplete expert tensors in checkpoint: {sorted(expert_buf)}")
 
 
 def load_w8a8_state_dict(items: Iterable[Tuple[str, torch.Tensor]], rank: int, world: int,
                          num_kv_heads: Optional[int], quantise: Optional[Quantiser] = None,
                          device: Optional[torch.device] = None,
-                         dtype: torch.dtype = torch.bfloat16) -> Dict[str, torch.Tensor]:
+                         dtype: torch.dtype = torch.bfloat16,
+                         num_experts: Optional[int] = None) -> Dict[str, torch.Tensor]:
     """``dict(w8a8_weight_stream(...))`` -- the state dict to hand to the
     model's ``load_state_dict`` in place of the engine's
     ``{k: v.to(dtype) for k, v in load_weight(...)}`` (M/engine/engine.py:139-146)."""
-    return dict(w8a8_weight_stream(items, rank, world, num_kv_heads, quantise, device, dtype))
+    return dict(w8a8_weight_stream(items, rank, world, num_kv_heads, quantise, device, dtype, num_experts))

@@ -170,3 +170,44 @@ def test_prefixes_and_skipped_towers(pkg, oracle):
 def test_scales_must_be_vectors(pkg):
     with pytest.raises(pkg.W8A8Error, match="1-D"):
         pkg.weights.shard_weight_scale("x.q_proj.weight", torch.ones(2, 2), 0, 1, None)
+
+
+@pytest.mark.parametrize("world", [1, 2])
+def test_moe_experts_are_stacked(pkg, oracle, world):
+    """Per-expert gate/up/down tensors (HF layout) are sharded, merged into
+    gate_up_proj, quantised per output channel of the unsharded weight and
+    stacked over the experts under the MoELayer's state-dict names."""
+    E, H, I = 4, 64, 32
+    g = torch.Generator().manual_seed(5)
+    p = "model.layers.0.mlp."
+    items, full = [], {}
+    for e in range(E):
+        for proj, shape in (("gate_proj", (I, H)), ("up_proj", (I, H)), ("down_proj", (H, I))):
+            w = (torch.randn(*shape, generator=g) * 0.02).bfloat16()
+            full[(e, proj)] = w
+            items.append((f"{p}experts.{e}.{proj}.weight", w))
+    items.append((p + "gate.weight", (torch.randn(E, H, generator=g) * 0.02).bfloat16()))
+    for r in range(world):
+        got = pkg.load_w8a8_state_dict(items, r, world, None, quantise=oracle.quant_weight_per_channel,
+                                       num_experts=E)
+        assert sorted(k for k in got if ".experts." in k) == [
+            p + "experts.down_proj", p + "experts.down_proj_scale", p + "experts.gate_up_proj",
+            p + "experts.gate_up_proj_scale"]
+        il = I // world
+        assert tuple(got[p + "experts.gate_up_proj"].shape) == (E, 2 * il, H)
+        assert tuple(got[p + "experts.down_proj"].shape) == (E, H, il)
+        assert tuple(got[p + "experts.down_proj_scale"].shape) == (E, H)
+        for e in range(E):
+            qg, sg = oracle.quant_weight_per_channel(full[(e, "gate_proj")])
+            qu, su = oracle.quant_weight_per_channel(full[(e, "up_proj")])
+            qd, sd = oracle.quant_weight_per_channel(full[(e, "down_proj")])
+            sl = slice(r * il, (r + 1) * il)
+            assert torch.equal(got[p + "experts.gate_up_proj"][e], torch.cat([qg[sl], qu[sl]]))
+            assert torch.equal(got[p + "experts.gate_up_proj_scale"][e], torch.cat([sg[sl], su[sl]]))
+            assert torch.equal(got[p + "experts.down_proj"][e], qd[:, sl])
+            assert torch.equal(got[p + "experts.down_proj_scale"][e], sd)
+        # the router (a LinearReplicated) is quantised whole on every rank
+        qr, sr = oracle.quant_weight_per_channel(items[-1][1])
+        assert torch.equal(got[p + "gate.weight"], qr) and torch.equal(got[p + "gate.weight_scale"], sr)
+    with pytest.raises(pkg.W8A8Error):
+        pkg.load_w8a8_state_dict(items[:-4], 0, 1, None, quantise=oracle.quant_weight_per_channel, num_experts=E)
