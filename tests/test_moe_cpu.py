@@ -123,3 +123,48 @@ def test_moe_layer_state_dict_contract(pkg):
                                        torch.zeros(2, 2), torch.zeros(2, 2, dtype=torch.int32))
     finally:
         pkg.reset_tp_info()
+
+
+@pytest.mark.parametrize("tp", [1, 2, 4])
+def test_loader_shards_feed_the_tp_experts(pkg, oracle, tp):
+    """Per-rank expert tensors from the loader (HF per-expert layout in) are
+    exactly the intermediate-dim shards the TP restatement uses, and
+    MoELayer's state dict at that TP accepts them."""
+    E, H, I, T, K = 4, 64, 64, 6, 2
+    g = torch.Generator().manual_seed(9)
+    p = "model.layers.0.mlp."
+    items, w1, w2 = [], [], []
+    for e in range(E):
+        gate = (torch.randn(I, H, generator=g) * 0.02).bfloat16()
+        up = (torch.randn(I, H, generator=g) * 0.02).bfloat16()
+        down = (torch.randn(H, I, generator=g) * 0.02).bfloat16()
+        items += [(f"{p}experts.{e}.gate_proj.weight", gate), (f"{p}experts.{e}.up_proj.weight", up),
+                  (f"{p}experts.{e}.down_proj.weight", down)]
+        w1.append(torch.cat([gate, up]))
+        w2.append(down)
+    q1 = [oracle.quant_weight_per_channel(w) for w in w1]
+    q2 = [oracle.quant_weight_per_channel(w) for w in w2]
+    w1q, sw1 = torch.stack([q for q, _ in q1]), torch.stack([s for _, s in q1])
+    w2q, sw2 = torch.stack([q for q, _ in q2]), torch.stack([s for _, s in q2])
+    x = torch.randn(T, H, generator=g).bfloat16()
+    tw, tid = oracle.fused_topk(torch.randn(T, E, generator=g), K, renormalize=True)
+    want, parts = oracle.tp_moe_experts(x, w1q, sw1, w2q, sw2, tw, tid, tp)
+    got_parts = []
+    for r in range(tp):
+        sd = pkg.load_w8a8_state_dict(items, r, tp, None, quantise=oracle.quant_weight_per_channel, num_experts=E)
+        pre = p + "experts."
+        out, _ = oracle.moe_experts_w8a8(x, sd[pre + "gate_up_proj"], sd[pre + "gate_up_proj_scale"],
+                                         sd[pre + "down_proj"], sd[pre + "down_proj_scale"], tw, tid)
+        got_parts.append(out)
+        assert torch.equal(out, parts[r])
+        pkg.reset_tp_info()
+        pkg.set_tp_info(r, tp)
+        try:
+            layer = pkg.MoELayer(num_experts=E, top_k=K, hidden_size=H, intermediate_size=I)
+            layer.load_state_dict({k[len(pre):]: v for k, v in sd.items() if k.startswith(pre)})
+            assert tuple(layer.gate_up_proj.shape) == (E, 2 * I // tp, H)
+        finally:
+            pkg.reset_tp_info()
+    assert torch.equal(oracle.all_reduce_sum(got_parts) if tp > 1 else got_parts[0], want)
+    if tp == 1:
+        assert torch.equal(want, oracle.moe_experts_w8a8(x, w1q, sw1, w2q, sw2, tw, tid)[0])
