@@ -250,6 +250,54 @@ def test_planner_pair_last_wave_split(pkg, m, n, k, ctas):
         assert split == 3
 
 
+def _pair_walk(pairs, clusters, kblocks, split):
+    """Host model of the pair kernel's PairWalk: cluster c takes whole blocks
+    c, c + G, ... below full = pairs - rem, then (split > 1) fragment f = c of
+    the last wave: block full + f // split, k blocks [j kb / split, (j + 1) kb
+    / split) with j = f % split.  Returns {cluster: [(block, k0, k1, j)]}."""
+    rem = pairs % clusters if split else 0
+    full = pairs - rem
+    walk = {}
+    for c in range(clusters):
+        items = [(b, 0, kblocks, -1) for b in range(c, full if split else pairs, clusters)]
+        if split and c < rem * split:
+            j = c % split
+            items.append((full + c // split, j * kblocks // split, (j + 1) * kblocks // split, j))
+        walk[c] = items
+    return walk
+
+
+@pytest.mark.parametrize("m,n,k,ctas", [
+    (4096, 5120, 25600, 0), (4096, 5120, 8192, 0), (4096, 2560, 5120, 0), (4096, 1280, 5120, 0),
+    (1100, 1024, 2128, 16), (500, 1200, 4224, 18), (1280, 1024, 3200, 18), (1280, 1024, 2176, 12),
+    (8192, 1280, 8192, 0), (3000, 3000, 3000, 0),
+])
+def test_pair_walk_covers_every_k_block_once(pkg, m, n, k, ctas):
+    """Every (block, k block) of the pair plan is computed exactly once; a
+    split block's share 0 sits on the pair whose next split - 1 pairs hold
+    shares 1.. of the same block (the owner protocol's slot addressing), and
+    every share has at least 8 k blocks."""
+    p = pkg.ops.gemm_plan(m, n, k, variant=7, ctas=ctas, num_sms=148)
+    pairs = ((m + 255) // 256) * ((n + 255) // 256)
+    clusters = p["grid"] // 2
+    kb = (k + 127) // 128
+    split = _pair_split(pairs, clusters, kb)
+    walk = _pair_walk(pairs, clusters, kb, split)
+    seen = {}
+    for c, items in walk.items():
+        for b, k0, k1, j in items:
+            for x in range(k0, k1):
+                assert (b, x) not in seen, (b, x)
+                seen[(b, x)] = c
+            if j == 0:
+                for o in range(1, split):
+                    b2, k0b, k1b, j2 = walk[c + o][-1]
+                    assert (b2, j2) == (b, o) and k0b == (o * kb) // split
+            if j >= 0:
+                assert k1 - k0 >= 8
+    assert len(seen) == pairs * kb
+
+
 def test_every_plan_fits_the_static_scratch(pkg):
     """The no-allocation entry point's 20 MiB scratch covers every stream-K plan
     the planner makes on a 148-SM device (the largest, 128 x 128 tiles with a
