@@ -317,6 +317,12 @@ class MoeRouting(NamedTuple):
     topk: int
 
 
+def _one_device(name: str, *ts: Optional[torch.Tensor]) -> None:
+    devs = {t.device for t in ts if t is not None}
+    if len(devs) > 1:
+        raise _lib.W8A8Error(_lib.ERR_INVALID_ARG, f"{name}: operands on several devices {sorted(map(str, devs))}")
+
+
 def _check_2d(name: str, t: torch.Tensor, dtype: torch.dtype, shape: Tuple[int, ...]) -> None:
     if t.dtype != dtype or tuple(t.shape) != tuple(shape) or not t.is_contiguous():
         raise _lib.W8A8Error(_lib.ERR_INVALID_ARG,
@@ -351,6 +357,7 @@ def moe_quant_scatter(x: torch.Tensor, routing: MoeRouting) -> torch.Tensor:
     if x.dtype != torch.bfloat16 or x.dim() != 2 or x.stride(1) != 1:
         raise _lib.W8A8Error(_lib.ERR_INVALID_ARG, "moe_quant_scatter: x must be a 2-D bf16 tensor with unit column stride")
     t, h = x.shape
+    _one_device("moe_quant_scatter", x, routing.inv_pos, routing.sa_sorted)
     if routing.inv_pos.numel() != t * routing.topk:
         raise _lib.W8A8Error(_lib.ERR_INVALID_ARG, "moe_quant_scatter: routing was built for another token count")
     q = torch.empty(128 * routing.max_blocks, h, dtype=torch.int8, device=x.device)
@@ -373,6 +380,7 @@ def moe_gemm(a_sorted: torch.Tensor, sa_sorted: torch.Tensor, w: torch.Tensor, s
     p = 128 * routing.max_blocks
     if w.dim() != 3 or e != routing.num_experts:
         raise _lib.W8A8Error(_lib.ERR_INVALID_ARG, f"moe_gemm: w must be [E={routing.num_experts}, N, K]")
+    _one_device("moe_gemm", a_sorted, sa_sorted, w, sw, route_w, routing.sorted_ids, routing.block_expert)
     _check_2d("moe_gemm w", w, torch.int8, (e, n, k))
     _check_2d("moe_gemm sw", sw, torch.float32, (e, n))
     _check_2d("moe_gemm a_sorted", a_sorted, torch.int8, (p, k))
@@ -400,6 +408,7 @@ def moe_quant_rows(y: torch.Tensor, amax: torch.Tensor, routing: MoeRouting) -> 
     if y.dtype != torch.bfloat16 or y.dim() != 2 or y.shape[0] != p or y.stride(1) != 1:
         raise _lib.W8A8Error(_lib.ERR_INVALID_ARG, "moe_quant_rows: y must be a bf16 [P, I] tensor")
     _check_2d("moe_quant_rows amax", amax, torch.int32, (p,))
+    _one_device("moe_quant_rows", y, amax, routing.num_blocks)
     i = y.shape[1]
     q = torch.empty(p, i, dtype=torch.int8, device=y.device)
     s = torch.empty(p, dtype=torch.float32, device=y.device)
@@ -415,9 +424,10 @@ def moe_sum(c_sorted: torch.Tensor, routing: MoeRouting, out: Optional[torch.Ten
     bf16(sum_j f32(c[row(t, j)]))`` in choice order."""
     _require_cuda("moe_sum", c_sorted, out)
     t = routing.inv_pos.numel() // max(routing.topk, 1)
-    h = c_sorted.shape[1]
+    _one_device("moe_sum", c_sorted, out, routing.inv_pos)
     if c_sorted.dtype != torch.bfloat16 or c_sorted.dim() != 2 or c_sorted.stride(1) != 1:
         raise _lib.W8A8Error(_lib.ERR_INVALID_ARG, "moe_sum: c_sorted must be a bf16 [P, H] tensor")
+    h = c_sorted.shape[1]
     if out is None:
         out = torch.empty(t, h, dtype=torch.bfloat16, device=c_sorted.device)
     elif out.dtype != torch.bfloat16 or tuple(out.shape) != (t, h) or out.stride(1) != 1:
@@ -450,6 +460,7 @@ def fused_experts_w8a8(x: torch.Tensor, w1q: torch.Tensor, sw1: torch.Tensor, w2
     if topk_ids.dim() != 2 or topk_ids.shape[0] != t or tuple(topk_weights.shape) != tuple(topk_ids.shape):
         raise _lib.W8A8Error(_lib.ERR_INVALID_ARG, "fused_experts_w8a8: topk_ids / topk_weights must be [T, topk]")
     _check_2d("fused_experts_w8a8 topk_weights", topk_weights, torch.float32, tuple(topk_ids.shape))
+    _one_device("fused_experts_w8a8", x, w1q, sw1, w2q, sw2, topk_weights, topk_ids, out)
     routing = moe_align(topk_ids, e)
     if out is None:
         out = torch.empty(t, h, dtype=torch.bfloat16, device=x.device)
