@@ -168,3 +168,20 @@ def test_loader_shards_feed_the_tp_experts(pkg, oracle, tp):
     assert torch.equal(oracle.all_reduce_sum(got_parts) if tp > 1 else got_parts[0], want)
     if tp == 1:
         assert torch.equal(want, oracle.moe_experts_w8a8(x, w1q, sw1, w2q, sw2, tw, tid)[0])
+
+
+@pytest.mark.parametrize("renorm", [True, False])
+def test_layer_routing_follows_fused_topk(pkg, oracle, renorm):
+    """MoELayer.route (torch ops, run here on CPU tensors) is fused_topk's
+    arithmetic: the same experts and the same weights."""
+    pkg.reset_tp_info()
+    pkg.set_tp_info(0, 1)
+    try:
+        layer = pkg.MoELayer(num_experts=16, top_k=4, hidden_size=64, intermediate_size=32, renormalize=renorm)
+        logits = torch.randn(33, 16, generator=torch.Generator().manual_seed(4))
+        w, ids = layer.route(logits)
+        w_ref, ids_ref = oracle.fused_topk(logits, 4, renormalize=renorm)
+        assert ids.dtype == torch.int32 and w.dtype == torch.float32
+        assert torch.equal(ids, ids_ref) and torch.equal(w, w_ref)
+    finally:
+        pkg.reset_tp_info()
