@@ -793,9 +793,9 @@ def run_ours(args, rank, world, dev):
     if world > 1:
         comm = D.enable_peer_mem_distributed(D.get_tp_info(), None, max_bytes=args.m * HIDDEN * 2, device=dev)
         comm.set_mode(args.comm_mode)
-        comm_kind = ("fused into the row-parallel GEMMs (NVLink peer memory; two-shot through NVSwitch multicast "
-                     "at world >= 4)" if comm.nvls else
-                     f"fused into the row-parallel GEMMs (NVLink peer memory; no NVLS: {comm.nvls_error})")
+        comm_kind = ("fused into the row-parallel GEMMs (NVLink peer-memory stores; NVSwitch multicast buffer "
+                     "attached, used by mode 3 only)" if comm.nvls else
+                     f"fused into the row-parallel GEMMs (NVLink peer-memory stores; no NVLS: {comm.nvls_error})")
         comm_kind += f"; mode {args.comm_mode}"
     stream = torch.cuda.Stream(dev)
     flush_buf = torch.zeros(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
